@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Benchmark of the JHQ search hot path on B200 (one JSON line on rank 0).
+
+Workload ("C1"): flat JHQ embedding search, 100,000
+base + 1,000 queries, D=1024, L2-normalised Gaussian-mixture data (1,024
+components, sigma 0.35), M=128, B=8, Br=4, alpha=4, k=10, query batch 64.
+A "step" is one search() of all 1,000 queries. Metric: QPS (at the recall@10
+the run reports; the configuration is the one whose recall is >= 0.95).
+
+  value  : QPS with queries resident in HBM (jhq_search_device), device-timed
+           with CUDA events on the search stream, L2 flushed before every step.
+  e2e    : QPS through the reference-facing C-ABI call jhq_search with host
+           buffers (H2D of queries and D2H of results inside the timed region).
+  roofline: ADC-scan kernel, algorithmic code bytes (queries x N x M bytes)
+           / scan device time, from a profiled pass of the same steps.
+  cpu_baseline: the scalar oracle (oracle/jhq_oracle.c) on all host cores on a
+           bounded sample of the same queries and index.
+
+Multi-GPU (torchrun, N ranks): query-parallel replicas — each rank serves its
+own 1,000-query stream against a full copy of the index (weak scaling, no
+data-path collective); value = all ranks' queries / max rank time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(name="c1", n=100_000, nq=1_000, d=1024, M=128, B=8, Br=4, alpha=4.0, k=10,
+           nlist=1, nprobe=1, batch=64, seed=0)
+METRIC = "QPS at recall@10>=0.95 (C1 flat JHQ, 100k x 1024, 1 B200)"
+
+
+def workload_config(extra=None):
+    c = {"workload": "C1 flat JHQ: 100k base + 1k queries, D=1024 normalised GMM(1024, 0.35), "
+                     "M=128 B=8 Br=4 alpha=4 k=10, query batch 64",
+         "n_base": CFG["n"], "n_queries": CFG["nq"], "d": CFG["d"], "M": CFG["M"], "B": CFG["B"],
+         "Br": CFG["Br"], "alpha": CFG["alpha"], "k": CFG["k"], "nlist": CFG["nlist"],
+         "batch": CFG["batch"], "l2": "flushed (256 MiB write) before every timed step"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+# ----------------------------------------------------------------------------- helpers
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        os.unlink(self.f.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def build_oracle_inputs(idx):
+    t = idx.get_trained()
+    pc, rc, co, asg = idx.get_codes()
+    return t, pc, rc, co, asg
+
+
+def time_oracle(oracle, t, pc, rc, co, asg, q, p, k, budget_s=10.0, threads=0):
+    """QPS of the oracle on a sample of queries sized to ~budget_s of CPU time."""
+    def run(qs):
+        t0 = time.perf_counter()
+        qr = oracle.rotate(t["Pi"], qs)
+        oracle.search(qr, M=p["M"], B=p["B"], Br=p["Br"], c1d=t["c1d"], res_c1d=t["res_c1d"],
+                      codes=pc, res=rc, corr=co, assign=asg, cents=t["cents"], k=k,
+                      alpha=p["alpha"], nprobe=p["nprobe"], nthreads=threads)
+        return time.perf_counter() - t0
+    cores = threads or os.cpu_count()
+    probe = min(len(q), max(1, cores))
+    dt = run(q[:probe])
+    n = int(min(len(q), max(probe, budget_s / max(dt, 1e-6) * probe)))
+    dt = run(q[:n])
+    return n / dt, n, dt, cores
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200 import datasets
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+
+    base, queries = datasets.make("c1", seed=CFG["seed"])
+    k = CFG["k"]
+    p = J.Params(M=CFG["M"], B=CFG["B"], Br=CFG["Br"], alpha=CFG["alpha"], nlist=CFG["nlist"],
+                 nprobe=CFG["nprobe"], batch_size=CFG["batch"], device=local)
+    idx = J.JHQGpuIndex(CFG["d"], p)
+    t0 = time.perf_counter()
+    idx.train(base[:min(len(base), 100_000)])
+    t_train = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    idx.add(base)
+    t_add = time.perf_counter() - t0
+    gt = datasets.ground_truth_torch(base, queries, k, device=f"cuda:{local}")
+
+    nq = len(queries)
+    stream = torch.cuda.Stream(device=dev)
+    q_dev = torch.from_numpy(queries).to(dev)
+    D = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    I = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(), stream.cuda_stream)
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    recall = datasets.recall_at_k(I.cpu().numpy(), gt, k)
+
+    # ---- device-timed value
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    l0 = J.kernel_launches()
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    launches = J.kernel_launches() - l0 - 0
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    clocks = clk.summary()
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = ws * args.steps * nq / (ms / 1000.0)
+
+    # ---- e2e through the host C-ABI call
+    qh = np.ascontiguousarray(queries)
+    idx.search(qh, k)
+    e2e_s = []
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        torch.cuda.synchronize(dev)
+        barrier()
+        t0 = time.perf_counter()
+        Dh, Ih = idx.search(qh, k)
+        e2e_s.append(time.perf_counter() - t0)
+    e2e_tot = sum(e2e_s)
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_tot], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_tot = float(t.item())
+    e2e = ws * args.steps * nq / e2e_tot
+    recall_host = datasets.recall_at_k(Ih, gt, k)
+
+    # ---- profiled pass: per-stage device time -> roofline of the scan kernel
+    idx.set_profiling(True)
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    stages, nbatches = idx.stage_times()
+    idx.set_profiling(False)
+    scan_ms = stages["scan"] / args.steps                     # per step (all batches)
+    scan_bytes = nq * CFG["n"] * CFG["M"] * CFG["B"] / 8      # algorithmic code bytes per step
+    peak, peak_kind = peaks()
+    achieved = scan_bytes / (scan_ms / 1000.0) / 1e9
+    nbatch = -(-nq // CFG["batch"])
+    traffic = None
+    tr_path = os.path.join(ROOT, "profiles", "scan_c1_traffic.json")
+    if os.path.exists(tr_path):
+        with open(tr_path) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+
+    if rank != 0:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    # ---- CPU baseline: oracle on a bounded sample (rank 0, N=1 only)
+    cpu = None
+    if ws == 1 and not args.no_cpu:
+        from oracle import Oracle
+        o = Oracle()
+        t, pc, rc, co, asg = build_oracle_inputs(idx)
+        pp = dict(M=CFG["M"], B=CFG["B"], Br=CFG["Br"], alpha=CFG["alpha"], nprobe=CFG["nprobe"])
+        qps, ns, dt, cores = time_oracle(o, t, pc, rc, co, asg, queries, pp, k, budget_s=10.0)
+        cpu = {"value": round(qps, 2), "unit": "QPS", "cores": cores, "kind": "port",
+               "sample": f"{ns} of the {nq} C1 queries against the same 100k index "
+                         f"({dt:.1f} s, OpenMP over queries)"}
+
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "QPS", "n_gpus": ws,
+        "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes / f32 accumulate",
+        "data": "synthetic (seeded normalised Gaussian mixture, BASELINE configs[1] shape)",
+        "config": workload_config({"parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"}),
+        "recall_at_10": round(recall, 4), "recall_at_10_host_path": round(recall_host, 4),
+        "e2e": {"value": round(e2e, 1), "unit": "QPS", "h2d_bytes_per_step": nq * CFG["d"] * 4,
+                "d2h_bytes_per_step": nq * k * 8},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_kind": peak_kind, "kernel": "scan_kernel (LUT + ADC + top-ck)",
+                     "algorithmic_bytes_per_step": int(scan_bytes),
+                     "launches_per_step": nbatch},
+        "stage_ms_per_step": {kk: round(v / args.steps, 4) for kk, v in stages.items()},
+        "clocks": clocks, "cpu_baseline": cpu,
+        "train_s": round(t_train, 2), "add_s": round(t_add, 3),
+    }
+    print(json.dumps(out), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference has no CPU search of its own: this arm times the oracle port
+    (scalar C restatement of the v14/v3 search, OpenMP on all host cores) on an
+    index trained by the reference's own cpu/ code (oracle/_ref) when present."""
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return
+    from jhq_gpu_b200 import datasets
+    from oracle import REF_SO, Oracle, RefCPU
+    o = Oracle()
+    base, queries = datasets.make("c1", seed=CFG["seed"])
+    d, M, B, Br, k = CFG["d"], CFG["M"], CFG["B"], CFG["Br"], CFG["k"]
+    ntr = min(len(base), 100_000)
+    if os.path.exists(REF_SO):
+        r = RefCPU()
+        sigma = r.sigma(base[:ntr])
+        Pi = r.rotation(d, 42)
+        c1d = r.c1d(d, M, B, sigma)
+        train_kind = "reference cpu/ (oracle/_ref)"
+    else:
+        import jhq_gpu_b200 as J
+        sigma = o.sigma(base[:ntr])
+        Pi = J.jl_rotation(d, 42)
+        c1d = o.c1d(sigma, 1 << (B // (d // M)))
+        train_kind = "oracle restatement"
+    if os.path.exists(REF_SO):
+        y = RefCPU().apply(d, 42, base)          # the reference's cblas_sgemm rotation
+    else:
+        y = base @ Pi.reshape(d, d)
+    codes = o.encode_primary(y, M, B, c1d)
+    yhat = o.reconstruct(codes[:ntr], d, M, B, c1d)
+    res_c1d = o.kmeans1d((y[:ntr] - yhat).ravel(), 1 << Br)
+    rc, corr = o.encode_residual(y, codes, M, B, c1d, res_c1d, Br)
+    t = dict(Pi=Pi, c1d=c1d, res_c1d=res_c1d, cents=np.zeros((1, d), np.float32))
+    asg = np.zeros(len(base), np.int32)
+    pp = dict(M=M, B=B, Br=Br, alpha=CFG["alpha"], nprobe=1)
+    for _ in range(args.warmup):
+        time_oracle(o, t, codes, rc, corr, asg, queries[:8], pp, k, budget_s=0.5)
+    vals, samples = [], []
+    for _ in range(args.steps):
+        qps, ns, dt, cores = time_oracle(o, t, codes, rc, corr, asg, queries, pp, k, budget_s=3.0)
+        vals.append(qps)
+        samples.append(ns)
+    qps = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(qps, 2), "unit": "QPS",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u8 codes / f32 accumulate",
+        "data": "synthetic (seeded normalised Gaussian mixture, BASELINE configs[1] shape)",
+        "config": workload_config({"training": train_kind}),
+        "cpu_baseline": {"value": round(qps, 2), "unit": "QPS", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"median over {args.steps} steps of {min(samples)}-{max(samples)} "
+                                   f"C1 queries each (~3 s per step), flat scan of all 100k codes"},
+        "e2e": {"value": round(qps, 2), "unit": "QPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference ships no CPU search path; its CUDA demos need nvcc builds of the "
+                "reference tree, which are not part of this arm",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

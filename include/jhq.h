@@ -1,0 +1,165 @@
+/*
+ * jhq.h — C-ABI of the B200 JHQ search engine (libjhq_b200.so).
+ *
+ * Drop-in boundary for the reference's jhq_gpu::JHQGpuIndex
+ * (jhq_v14_streaming_add/jhq_gpu_index.cuh:14-47) and its search_gpu /
+ * SearchWorkspace pair (jhq_v14_streaming_add/search.cuh:24-69). Each entry
+ * point names the reference member it replaces. Plain pointers and sizes only;
+ * every function returns a JHQ_* status (0 = success) and never exits or
+ * throws; jhq_last_error() gives the message of the calling thread's last
+ * failure. Host pointers are caller-owned; the index owns every device buffer.
+ *
+ * Threading: like the reference (whose search() is const but mutates a
+ * mutable workspace, search.cuh:24-46 / jhq_gpu_index.cuh:73-74), one index
+ * serves one caller at a time.
+ */
+#ifndef JHQ_B200_H
+#define JHQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------- */
+#define JHQ_OK        0
+#define JHQ_EINVAL    1   /* bad argument (reference: std::invalid_argument)      */
+#define JHQ_ENOMEM    2   /* device or pinned allocation failed                    */
+#define JHQ_ETIMEDOUT 3   /* a bounded wait on the device ran out                  */
+#define JHQ_EDEVICE   4   /* CUDA error (reference: CUDA_CHECK -> exit(1))         */
+#define JHQ_ESTATE    5   /* call order (reference: std::runtime_error, e.g.
+                             "call train() before add()", "index is empty")      */
+#define JHQ_EIO       6   /* save/load file error or bad format                    */
+
+/* ---- parameters: JHQGpuIndex::Params (jhq_gpu_index.cuh:16-36) ------- */
+typedef struct jhq_params {
+    int   M;           /* subspaces                      (default 96)    */
+    int   B;           /* primary bits per subspace      (default 8)     */
+    int   Br;          /* residual bits per dim, 4 or 8  (default 4)     */
+    float alpha;       /* ck = max(k, ceil(alpha k))     (default 4.0)   */
+    int   nlist;       /* IVF lists, 1 = flat            (default 1024)  */
+    int   nprobe;      /* lists probed per query         (default 8)     */
+    int   ivf_iters;   /* k-means iterations             (default 8)     */
+    int   batch_size;  /* queries per search batch       (default 256)   */
+    int   seed;        /* JL rotation seed               (default 42)    */
+    int   add_batch;   /* rows rotated+encoded at once   (default 65536) */
+    int   device;      /* CUDA device ordinal; -1 = current device at create */
+} jhq_params;
+
+typedef struct jhq_index jhq_index;
+
+/* Fills the reference's defaults (jhq_gpu_index.cuh:17-35), device = -1. */
+int jhq_params_default(jhq_params* p);
+
+/* JHQGpuIndex(int d, Params p) — validation as jhq_gpu_index.cu:103-131. */
+int jhq_index_create(int d, const jhq_params* p, jhq_index** out);
+/* ~JHQGpuIndex() — jhq_gpu_index.cu:133-163. NULL is accepted. */
+int jhq_index_destroy(jhq_index* idx);
+
+/* JHQGpuIndex::train(h_x, n_train) — jhq_gpu_index.cu:333-364.
+ * Estimates sigma, builds the Lloyd-Max codebook and the QR rotation on the
+ * host, rotates/encodes on the device, trains IVF centroids (k-means, nlist>1)
+ * and the Br-bit residual codebook (1-D k-means). x: host [n][d] float32. */
+int jhq_train(jhq_index* idx, const float* x, int64_t n);
+
+/* JHQGpuIndex::add(h_x, n) — jhq_gpu_index.cu:417-532. Unlike the reference
+ * (single call only, :419-420) add may be called repeatedly (streaming add);
+ * ids continue from the current ntotal. x: host [n][d] float32. */
+int jhq_add(jhq_index* idx, const float* x, int64_t n);
+
+/* JHQGpuIndex::search(h_q, nq, k, h_dists, h_labels) — jhq_gpu_index.cu:535-552
+ * and search_gpu (search.cu:388-445). Host buffers; [nq][k] row-major outputs.
+ * Distances carry the reference's +|q_rot|^2 offset (residual_encode corr,
+ * encode.cu:85). Missing results are id -1, distance +inf (search.cu:285-286). */
+int jhq_search(jhq_index* idx, const float* q, int64_t nq, int k,
+               float* dists, int32_t* ids);
+
+/* Same as jhq_search with DEVICE buffers on `stream` (cudaStream_t, NULL =
+ * the index's stream); no host copies, asynchronous w.r.t. the host. */
+int jhq_search_device(jhq_index* idx, const float* d_q, int64_t nq, int k,
+                      float* d_dists, int32_t* d_ids, void* stream);
+
+/* Waits for the index's stream with a deadline (replaces the unbounded
+ * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
+int jhq_synchronize(jhq_index* idx, double timeout_s);
+
+/* Accessors: JHQGpuIndex::ntotal() / dim() (jhq_gpu_index.cuh:44-45). */
+int jhq_ntotal(const jhq_index* idx, int64_t* n);
+int jhq_dim(const jhq_index* idx, int* d);
+int jhq_is_trained(const jhq_index* idx, int* trained);
+
+/* ---- trained artefacts (Pi, c1d, res_c1d, IVF centroids) -------------
+ * The reference keeps these private (jhq_gpu_index.cuh:56-61). They are
+ * exported/imported here so that two builds can run on identical training
+ * (parity), and for persistence. Sizes: Pi d*d (column-major, as
+ * cpu/jl_transform.h:24), c1d K1D = 2^(B/(d/M)), res_c1d 2^Br, cents nlist*d.
+ * jhq_get_trained copies out (NULL pointers skipped); jhq_set_trained replaces
+ * the index's training and requires an empty index. */
+int jhq_get_trained(const jhq_index* idx, float* Pi, float* c1d, float* res_c1d,
+                    float* cents, float* sigma);
+int jhq_set_trained(jhq_index* idx, const float* Pi, const float* c1d,
+                    const float* res_c1d, const float* cents, float sigma);
+
+/* Codes of the stored vectors in id order: primary [n][M], residual
+ * [n][ceil(d*Br/8)], corr [n], list assignment [n] (encode.cu:20-86,
+ * jhq_gpu_index.cu:458-473). Any pointer may be NULL. */
+int jhq_get_codes(const jhq_index* idx, uint8_t* primary, uint8_t* residual,
+                  float* corr, int32_t* assign);
+
+/* JL rotation y = Pi x of host rows (jhq_gpu_index.cu:209-225). */
+int jhq_rotate(jhq_index* idx, const float* x, int64_t n, float* y);
+
+/* Encode already-rotated host rows with the index's codebooks without adding
+ * them (primary_encode_kernel + residual_encode_kernel, encode.cu:20-86). */
+int jhq_encode(jhq_index* idx, const float* y, int64_t n, uint8_t* primary,
+               uint8_t* residual, float* corr);
+
+/* Serialise / restore trained artefacts and stored codes (versioned binary).
+ * The reference has no persistence; every demo retrains (demo :78-86). */
+int jhq_save(const jhq_index* idx, const char* path);
+int jhq_load(const char* path, int device, jhq_index** out);
+
+/* ---- sharded search (one process per GPU) ----------------------------
+ * k-way merge of per-shard top-k lists on the device: in_dists/in_ids are
+ * [nshards][nq][k] (device), out [nq][k] (device), order (distance, id),
+ * missing entries (+inf, -1). Used after an all-gather of every shard's
+ * jhq_search_device output. No reference counterpart (single-GPU only). */
+int jhq_merge_shards(const float* d_in_dists, const int32_t* d_in_ids,
+                     int nshards, int64_t nq, int k,
+                     float* d_out_dists, int32_t* d_out_ids, void* stream);
+
+/* ---- per-stage timing (the reference's jhq_v9_step_timing / v13 step
+ * events, jhq_v13_step_timing/search.cu:456-491) -------------------------
+ * With profiling on, search runs each batch as direct launches (no CUDA
+ * graph) with CUDA events between the stages and accumulates per-stage device
+ * time. Stages: 0 rotate, 1 coarse scores + probe selection, 2 scan partition,
+ * 3 LUT + ADC scan + top-ck, 4 refine + final top-k. jhq_set_profiling resets
+ * the totals; jhq_stage_times copies min(n, 5) totals (ms) and batch counts. */
+#define JHQ_NUM_STAGES 5
+int jhq_set_profiling(jhq_index* idx, int on);
+int jhq_stage_times(const jhq_index* idx, double* ms, int64_t* batches, int n);
+
+/* ---- host-side training primitives (no GPU needed) --------------------
+ * The CPU steps of train(), exported so callers can reproduce or inspect them:
+ *  jhq_jl_rotation      JLTransform(d, seed) -> Pi (cpu/jl_transform.cpp:21-56);
+ *                       Householder QR in double, LAPACK sign convention.
+ *  jhq_estimate_sigma   JLTransform::estimate_sigma (cpu/jl_transform.cpp:73-83).
+ *  jhq_lloyd_max_c1d    LloydMaxCodebook codewords (cpu/codebook.cpp:60-80).
+ *  jhq_kmeans_1d        train_1d_kmeans (cpu/codebook.cpp:8-58); *nout = count. */
+int jhq_jl_rotation(int d, int seed, float* Pi);
+int jhq_estimate_sigma(const float* x, int64_t n, int d, float* sigma);
+int jhq_lloyd_max_c1d(float sigma, int K1D, float* c1d);
+int jhq_kmeans_1d(const float* vals, int64_t n, int Kr, int max_iter, float* out, int* nout);
+
+/* Per-call kernel launch counter of the calling process (all indexes), for
+ * reporting how many engine kernels ran in a timed region. */
+int64_t jhq_kernel_launches(void);
+
+const char* jhq_last_error(void);
+const char* jhq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JHQ_B200_H */

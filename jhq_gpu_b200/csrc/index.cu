@@ -1,0 +1,686 @@
+// index.cu — jhq::Index: train / add / search orchestration on one GPU.
+// Mirrors JHQGpuIndex (jhq_v14_streaming_add/jhq_gpu_index.cu) and
+// search_gpu (jhq_v14_streaming_add/search.cu:388-445); see index.h for
+// the device data layout.
+#include "index.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <thread>
+
+#include "kernels.cuh"
+#include "train_cpu.h"
+
+namespace jhq {
+
+namespace {
+constexpr int64_t SCORE_BYTES = 256ll << 20;     // bound of one coarse-score block
+constexpr int MAX_CK_PAD = 256;
+
+template <class T>
+void h2d(T* dst, const T* src, size_t n, cudaStream_t s) {
+    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyHostToDevice, s));
+}
+template <class T>
+void d2h(T* dst, const T* src, size_t n, cudaStream_t s) {
+    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyDeviceToHost, s));
+}
+}  // namespace
+
+// ---- construction: JHQGpuIndex ctor validation (jhq_gpu_index.cu:103-131) ----
+Index::Index(int d, const Params& p) : p_(p) {
+    if (d <= 0) fail(JHQ_EINVAL, "d must be positive");
+    if (p.M <= 0) fail(JHQ_EINVAL, "M must be positive");
+    if (d % p.M != 0) fail(JHQ_EINVAL, "d must be divisible by M");
+    if (p.B <= 0 || p.B % (d / p.M) != 0) fail(JHQ_EINVAL, "B must be divisible by Ds = d/M");
+    if (p.B > 8) fail(JHQ_EINVAL, "B must be <= 8");
+    if (p.Br != 4 && p.Br != 8) fail(JHQ_EINVAL, "Br must be 4 or 8");
+    if (p.nlist <= 0) fail(JHQ_EINVAL, "nlist must be positive");
+    if (p.nprobe <= 0) fail(JHQ_EINVAL, "nprobe must be positive");
+    if (p.ivf_iters <= 0) fail(JHQ_EINVAL, "ivf_iters must be positive");
+    if (p.batch_size <= 0) fail(JHQ_EINVAL, "batch_size must be positive");
+    if (p.add_batch <= 0) fail(JHQ_EINVAL, "add_batch must be positive");
+    if (!(p.alpha > 0.0f)) fail(JHQ_EINVAL, "alpha must be positive");
+    d_ = d; M_ = p.M; B_ = p.B; Br_ = p.Br;
+    Ds_ = d / M_; bpd_ = B_ / Ds_; K1D_ = 1 << bpd_; Kr_ = 1 << Br_;
+    bpv_ = (d * Br_ + 7) / 8;
+    bpv_pad_ = (int)ceil_div(bpv_, 16) * 16;
+    Mp_ = (int)ceil_div(M_, 16) * 16;
+    p_.nprobe = std::min(p.nprobe, p.nlist);
+    if (d > 16384) fail(JHQ_EINVAL, "d must be <= 16384");
+    if (scan_smem_bytes(Mp_, d_, MAX_CK_PAD) > 227 * 1024)
+        fail(JHQ_EINVAL, "M too large: the per-query byte LUT (M x 1 KB) must fit in shared memory");
+    if (p.device < 0) JHQ_CUDA(cudaGetDevice(&dev_));
+    else dev_ = p.device;
+    p_.device = dev_;
+    DeviceGuard g(dev_);
+    JHQ_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+}
+
+Index::~Index() {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(dev_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    destroy_graph();
+    for (auto& e : prof_ev_)
+        if (e) cudaEventDestroy(e);
+    if (stream_) cudaStreamDestroy(stream_);
+    // DevBuf / PinnedBuf members free themselves (device still current).
+    dPi_.release(); dc1d_.release(); dres_.release(); dcentsT_.release(); dnorms_.release();
+    dpcodes_.release(); drcodes_.release(); dpages_.release(); dcorr_.release();
+    dassign_.release(); dslot_ids_.release(); dlist_page_off_.release();
+    ws_.q.release(); ws_.q_rot.release(); ws_.scores.release(); ws_.out_d.release();
+    ws_.probes.release(); ws_.ppo.release(); ws_.out_i.release(); ws_.qpage_off.release();
+    ws_.cand.release(); ws_.nvalid.release();
+    ws_.h_q.release(); ws_.h_d.release(); ws_.h_i.release(); ws_.h_nvalid.release();
+    cudaSetDevice(prev);
+}
+
+void Index::destroy_graph() {
+    if (ws_.exec) cudaGraphExecDestroy(ws_.exec);
+    if (ws_.graph) cudaGraphDestroy(ws_.graph);
+    ws_.exec = nullptr;
+    ws_.graph = nullptr;
+    ws_.graph_kernels = 0;
+}
+
+// ---- device helpers ----------------------------------------------------------
+void Index::rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const {
+    gemm_rows(d_x, dPi_.get(), d_y, n, d_, d_, EPI_STORE, nullptr, s);
+}
+
+void Index::assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaStream_t s) {
+    if (p_.nlist == 1) {
+        JHQ_CUDA(cudaMemsetAsync(d_assign, 0, n * sizeof(int32_t), s));
+        return;
+    }
+    int64_t rows = std::max<int64_t>(1, std::min<int64_t>(n, SCORE_BYTES / 4 / p_.nlist));
+    DevBuf<float> scores((size_t)rows * p_.nlist);
+    for (int64_t r0 = 0; r0 < n; r0 += rows) {
+        int64_t nr = std::min(rows, n - r0);
+        gemm_rows(d_y + r0 * d_, dcentsT_.get(), scores.get(), nr, d_, p_.nlist, EPI_COARSE,
+                  dnorms_.get(), s);
+        argmin_rows(scores.get(), nr, p_.nlist, d_assign + r0, s);
+    }
+    JHQ_CUDA(cudaStreamSynchronize(s));   // scores is freed on return
+}
+
+void Index::upload_trained() {
+    dPi_.resize((size_t)d_ * d_);
+    h2d(dPi_.get(), Pi_.data(), Pi_.size(), stream_);
+    dc1d_.resize(K1D_);
+    h2d(dc1d_.get(), c1d_.data(), c1d_.size(), stream_);
+    dres_.resize(Kr_);
+    if (!res_c1d_.empty()) h2d(dres_.get(), res_c1d_.data(), res_c1d_.size(), stream_);
+    // centroids as the row-major [d][nlist] right operand, plus |c|^2 in double
+    // (jhq_gpu_index.cu:243-249)
+    const int nl = p_.nlist;
+    std::vector<float> cT((size_t)d_ * nl), norms(nl);
+    for (int c = 0; c < nl; ++c) {
+        double s = 0.0;
+        for (int j = 0; j < d_; ++j) {
+            float v = cents_[(size_t)c * d_ + j];
+            cT[(size_t)j * nl + c] = v;
+            s += (double)v * v;
+        }
+        norms[c] = (float)s;
+    }
+    dcentsT_.resize(cT.size());
+    dnorms_.resize(nl);
+    h2d(dcentsT_.get(), cT.data(), cT.size(), stream_);
+    h2d(dnorms_.get(), norms.data(), norms.size(), stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+}
+
+// ---- train: JHQGpuIndex::train (jhq_gpu_index.cu:333-364) --------------------
+void Index::train(const float* h_x, int64_t n) {
+    DeviceGuard g(dev_);
+    if (!h_x || n <= 0) fail(JHQ_EINVAL, "train: need at least one vector");
+    if (n < p_.nlist) fail(JHQ_EINVAL, "n_train must be >= nlist");
+    if (n > INT32_MAX / std::max(1, d_)) fail(JHQ_EINVAL, "train: n_train * d exceeds 2^31");
+    if (ntotal_ > 0) fail(JHQ_ESTATE, "train() on a non-empty index");
+
+    sigma_ = train::estimate_sigma(h_x, n, d_);
+    c1d_ = train::lloyd_max_c1d(sigma_, K1D_);
+    Pi_ = train::build_rotation(d_, p_.seed);
+    res_c1d_.clear();
+    cents_.assign((size_t)p_.nlist * d_, 0.0f);
+    upload_trained();
+
+    // rotate + primary-encode the training rows on the device
+    DevBuf<float> dx((size_t)std::min<int64_t>(n, p_.add_batch) * d_);
+    DevBuf<float> dy((size_t)n * d_);
+    DevBuf<uint8_t> dcodes((size_t)n * M_);
+    for (int64_t r0 = 0; r0 < n; r0 += p_.add_batch) {
+        int64_t nr = std::min<int64_t>(p_.add_batch, n - r0);
+        h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
+        rotate_device(dx.get(), nr, dy.get() + r0 * d_, stream_);
+    }
+    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), nullptr, dcodes.get(), nullptr,
+                bpv_pad_, nullptr, stream_);
+    std::vector<float> y((size_t)n * d_);
+    std::vector<uint8_t> codes((size_t)n * M_);
+    d2h(y.data(), dy.get(), y.size(), stream_);
+    d2h(codes.data(), dcodes.get(), codes.size(), stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    dx.release();
+
+    // IVF centroids: Lloyd k-means in the rotated space (jhq_gpu_index.cu:228-299)
+    {
+        const int nl = p_.nlist;
+        for (int c = 0; c < nl; ++c) {
+            int64_t src = (int64_t)c * n / nl;
+            std::memcpy(&cents_[(size_t)c * d_], &y[(size_t)src * d_], sizeof(float) * d_);
+        }
+        DevBuf<int32_t> dassign((size_t)n);
+        std::vector<int32_t> as((size_t)n);
+        std::vector<double> sums((size_t)nl * d_);
+        std::vector<int> counts(nl);
+        for (int iter = 0; iter < p_.ivf_iters; ++iter) {
+            upload_trained();
+            assign_device(dy.get(), n, dassign.get(), stream_);
+            d2h(as.data(), dassign.get(), as.size(), stream_);
+            JHQ_CUDA(cudaStreamSynchronize(stream_));
+            std::fill(sums.begin(), sums.end(), 0.0);
+            std::fill(counts.begin(), counts.end(), 0);
+            for (int64_t i = 0; i < n; ++i) {
+                int c = as[i];
+                counts[c]++;
+                double* sc = &sums[(size_t)c * d_];
+                const float* yi = &y[(size_t)i * d_];
+                for (int j = 0; j < d_; ++j) sc[j] += yi[j];
+            }
+            for (int c = 0; c < nl; ++c) {
+                float* cc = &cents_[(size_t)c * d_];
+                if (counts[c] == 0) {
+                    int64_t src = ((int64_t)c * 1103515245 + (int64_t)(iter * 12345)) % n;
+                    std::memcpy(cc, &y[(size_t)src * d_], sizeof(float) * d_);
+                    continue;
+                }
+                const double inv = 1.0 / (double)counts[c];
+                const double* sc = &sums[(size_t)c * d_];
+                for (int j = 0; j < d_; ++j) cc[j] = (float)(sc[j] * inv);
+            }
+        }
+    }
+    dy.release();
+
+    // residual codebook: 1-D k-means of y - yhat (jhq_gpu_index.cu:302-330)
+    {
+        std::vector<float> yhat((size_t)d_);
+        for (int64_t i = 0; i < n; ++i) {
+            train::reconstruct(&codes[(size_t)i * M_], 1, d_, M_, B_, c1d_.data(), yhat.data());
+            float* yi = &y[(size_t)i * d_];
+            for (int j = 0; j < d_; ++j) yi[j] = yi[j] - yhat[j];
+        }
+        res_c1d_ = train::kmeans_1d(y.data(), (int64_t)y.size(), Kr_);
+        res_c1d_.resize(Kr_, res_c1d_.empty() ? 0.0f : res_c1d_.back());
+    }
+    upload_trained();
+    trained_ = true;
+    layout_dirty_ = true;
+}
+
+void Index::set_trained(const float* Pi, const float* c1d, const float* res_c1d,
+                        const float* cents, float sigma) {
+    DeviceGuard g(dev_);
+    if (ntotal_ > 0) fail(JHQ_ESTATE, "set_trained() on a non-empty index");
+    if (!Pi || !c1d || !res_c1d || !cents) fail(JHQ_EINVAL, "set_trained: null artefact");
+    Pi_.assign(Pi, Pi + (size_t)d_ * d_);
+    c1d_.assign(c1d, c1d + K1D_);
+    res_c1d_.assign(res_c1d, res_c1d + Kr_);
+    cents_.assign(cents, cents + (size_t)p_.nlist * d_);
+    sigma_ = sigma;
+    upload_trained();
+    trained_ = true;
+    layout_dirty_ = true;
+    destroy_graph();
+}
+
+void Index::get_trained(float* Pi, float* c1d, float* res_c1d, float* cents, float* sigma) const {
+    if (!trained_) fail(JHQ_ESTATE, "index is not trained");
+    if (Pi) std::memcpy(Pi, Pi_.data(), Pi_.size() * sizeof(float));
+    if (c1d) std::memcpy(c1d, c1d_.data(), c1d_.size() * sizeof(float));
+    if (res_c1d) std::memcpy(res_c1d, res_c1d_.data(), res_c1d_.size() * sizeof(float));
+    if (cents) std::memcpy(cents, cents_.data(), cents_.size() * sizeof(float));
+    if (sigma) *sigma = sigma_;
+}
+
+// ---- add: JHQGpuIndex::add (jhq_gpu_index.cu:417-532), repeatable ------------
+void Index::grow_master(int64_t need) {
+    if (need <= cap_) return;
+    int64_t nc = std::max<int64_t>(need, cap_ + cap_ / 2);
+    DevBuf<uint8_t> pc((size_t)nc * M_), rc((size_t)nc * bpv_pad_);
+    DevBuf<float> co((size_t)nc);
+    DevBuf<int32_t> as((size_t)nc);
+    if (ntotal_ > 0) {
+        JHQ_CUDA(cudaMemcpyAsync(pc.get(), dpcodes_.get(), (size_t)ntotal_ * M_, cudaMemcpyDeviceToDevice, stream_));
+        JHQ_CUDA(cudaMemcpyAsync(rc.get(), drcodes_.get(), (size_t)ntotal_ * bpv_pad_, cudaMemcpyDeviceToDevice, stream_));
+        JHQ_CUDA(cudaMemcpyAsync(co.get(), dcorr_.get(), (size_t)ntotal_ * 4, cudaMemcpyDeviceToDevice, stream_));
+        JHQ_CUDA(cudaMemcpyAsync(as.get(), dassign_.get(), (size_t)ntotal_ * 4, cudaMemcpyDeviceToDevice, stream_));
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
+    }
+    dpcodes_ = std::move(pc);
+    drcodes_ = std::move(rc);
+    dcorr_ = std::move(co);
+    dassign_ = std::move(as);
+    cap_ = nc;
+}
+
+void Index::add(const float* h_x, int64_t n) {
+    DeviceGuard g(dev_);
+    if (!trained_) fail(JHQ_ESTATE, "call train() before add()");
+    if (n < 0 || (n > 0 && !h_x)) fail(JHQ_EINVAL, "add: bad input");
+    if (n == 0) return;
+    if (ntotal_ + n > INT32_MAX) fail(JHQ_EINVAL, "add: more than 2^31-1 vectors");
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    grow_master(ntotal_ + n);
+    const int64_t AB = std::min<int64_t>(p_.add_batch, n);
+    DevBuf<float> dx((size_t)AB * d_), dy((size_t)AB * d_);
+    for (int64_t r0 = 0; r0 < n; r0 += AB) {
+        const int64_t nr = std::min(AB, n - r0);
+        const int64_t at = ntotal_ + r0;
+        h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
+        rotate_device(dx.get(), nr, dy.get(), stream_);
+        assign_device(dy.get(), nr, dassign_.get() + at, stream_);
+        encode_rows(dy.get(), nr, d_, M_, B_, Br_, dc1d_.get(), dres_.get(),
+                    dpcodes_.get() + at * M_, drcodes_.get() + at * bpv_pad_, bpv_pad_,
+                    dcorr_.get() + at, stream_);
+    }
+    h_assign_.resize((size_t)(ntotal_ + n));
+    d2h(h_assign_.data() + ntotal_, dassign_.get() + ntotal_, (size_t)n, stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    ntotal_ += n;
+    rebuild_layout();
+}
+
+// Group vectors by list (stable in id order), pad lists to 32-vector pages and
+// scatter the primary codes into the page layout. Replaces thrust::sort_by_key
+// + gather_list_storage_kernel + transpose_uint8_kernel (jhq_gpu_index.cu:468-522).
+void Index::rebuild_layout() {
+    const int nl = p_.nlist;
+    std::vector<int64_t> cnt(nl, 0);
+    for (int64_t i = 0; i < ntotal_; ++i) {
+        int a = h_assign_[(size_t)i];
+        if (a < 0 || a >= nl) fail(JHQ_EDEVICE, "invalid IVF assignment");
+        cnt[a]++;
+    }
+    std::vector<int32_t> lpo(nl + 1, 0);
+    int64_t pages = 0;
+    for (int c = 0; c < nl; ++c) {
+        lpo[c] = (int32_t)pages;
+        pages += ceil_div(cnt[c], 32);
+        if (pages > INT32_MAX) fail(JHQ_EINVAL, "too many pages");
+    }
+    lpo[nl] = (int32_t)pages;
+    std::vector<int32_t> slots((size_t)pages * 32, -1);
+    std::vector<int64_t> cur(nl);
+    for (int c = 0; c < nl; ++c) cur[c] = (int64_t)lpo[c] * 32;
+    for (int64_t i = 0; i < ntotal_; ++i) slots[(size_t)cur[h_assign_[(size_t)i]]++] = (int32_t)i;
+    npages_ = pages;
+    dlist_page_off_.resize(nl + 1);
+    dslot_ids_.resize(std::max<size_t>(1, slots.size()));
+    dpages_.resize(std::max<size_t>(16, (size_t)pages * Mp_ * 32));
+    h2d(dlist_page_off_.get(), lpo.data(), lpo.size(), stream_);
+    h2d(dslot_ids_.get(), slots.data(), slots.size(), stream_);
+    scatter_pages(dslot_ids_.get(), (int64_t)slots.size(), dpcodes_.get(), M_, Mp_, dpages_.get(),
+                  stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    layout_dirty_ = false;
+    destroy_graph();          // captured pointers changed
+}
+
+// ---- search: search_gpu (search.cu:388-445) ----------------------------------
+void Index::check_search_args(int64_t nq, int k) const {
+    if (nq < 0) fail(JHQ_EINVAL, "nq must be >= 0");
+    if (k <= 0) fail(JHQ_EINVAL, "k must be positive");
+    if (!trained_ || ntotal_ == 0) fail(JHQ_ESTATE, "index is empty");
+    int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
+    if (next_pow2(ck) > MAX_CK_PAD) fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) must be <= 256");
+}
+
+void Index::prepare_workspace(int k) {
+    const int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
+    const int ck_pad = std::max(32, next_pow2(ck));
+    const int Bq = p_.batch_size;
+    if (ws_.batch_cap == Bq && ws_.k == k && ws_.exec) return;
+    destroy_graph();
+    scan_configure();
+    refine_configure();
+    const int grid = scan_grid_for(Mp_, d_, ck_pad);
+    ws_.q.ensure((size_t)Bq * d_);
+    ws_.q_rot.ensure((size_t)Bq * d_);
+    if (p_.nlist > 1) ws_.scores.ensure((size_t)Bq * p_.nlist);
+    ws_.probes.ensure((size_t)Bq * p_.nprobe);
+    ws_.ppo.ensure((size_t)Bq * (p_.nprobe + 1));
+    ws_.qpage_off.ensure((size_t)Bq + 1);
+    ws_.cand.ensure((size_t)(grid + Bq) * ck);
+    ws_.out_d.ensure((size_t)Bq * k);
+    ws_.out_i.ensure((size_t)Bq * k);
+    ws_.nvalid.ensure(1);
+    ws_.h_q.ensure((size_t)2 * Bq * d_);
+    ws_.h_d.ensure((size_t)2 * Bq * k);
+    ws_.h_i.ensure((size_t)2 * Bq * k);
+    if (p_.nlist == 1)
+        JHQ_CUDA(cudaMemsetAsync(ws_.probes.get(), 0, (size_t)Bq * p_.nprobe * 4, stream_));
+    ws_.batch_cap = Bq;
+    ws_.k = k;
+    ws_.ck = ck;
+    ws_.ck_pad = ck_pad;
+    ws_.grid = grid;
+    // capture the per-batch pipeline once (capture_graph, search.cu:315-386)
+    const int64_t before = g_kernel_launches.load();
+    JHQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+        enqueue_batch(stream_);
+    } catch (...) {
+        cudaGraph_t gph = nullptr;
+        cudaStreamEndCapture(stream_, &gph);
+        if (gph) cudaGraphDestroy(gph);
+        throw;
+    }
+    JHQ_CUDA(cudaStreamEndCapture(stream_, &ws_.graph));
+    JHQ_CUDA(cudaGraphInstantiate(&ws_.exec, ws_.graph, 0));
+    ws_.graph_kernels = g_kernel_launches.load() - before;
+    g_kernel_launches.fetch_sub(ws_.graph_kernels);     // counted when launched instead
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+}
+
+// Kernel sequence of one query batch on the workspace buffers.
+void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
+    auto mark = [&](int i) { if (ev) JHQ_CUDA(cudaEventRecord(ev[i], s)); };
+    const int Bq = ws_.batch_cap;
+    mark(0);
+    rotate_device(ws_.q.get(), Bq, ws_.q_rot.get(), s);
+    mark(1);
+    if (p_.nlist > 1) {
+        gemm_rows(ws_.q_rot.get(), dcentsT_.get(), ws_.scores.get(), Bq, d_, p_.nlist, EPI_COARSE,
+                  dnorms_.get(), s);
+        select_probes(ws_.scores.get(), Bq, p_.nlist, p_.nprobe, ws_.probes.get(), s);
+    }
+    mark(2);
+    scan_prepare(ws_.probes.get(), Bq, p_.nprobe, dlist_page_off_.get(), ws_.nvalid.get(),
+                 ws_.ppo.get(), ws_.qpage_off.get(), s);
+    ScanArgs sa;
+    sa.q_rot = ws_.q_rot.get(); sa.c1d = dc1d_.get(); sa.probes = ws_.probes.get();
+    sa.probe_page_off = ws_.ppo.get(); sa.qpage_off = ws_.qpage_off.get();
+    sa.list_page_off = dlist_page_off_.get(); sa.pages = dpages_.get();
+    sa.slot_ids = dslot_ids_.get(); sa.cand = ws_.cand.get();
+    sa.nq = Bq; sa.d = d_; sa.M = M_; sa.Mp = Mp_; sa.B = B_; sa.nprobe = p_.nprobe;
+    sa.ck = ws_.ck; sa.ck_pad = ws_.ck_pad; sa.grid = ws_.grid;
+    mark(3);
+    scan_topck(sa, s);
+    mark(4);
+    RefineArgs ra;
+    ra.q_rot = ws_.q_rot.get(); ra.res_c1d = dres_.get(); ra.cand = ws_.cand.get();
+    ra.qpage_off = ws_.qpage_off.get(); ra.rcodes = drcodes_.get(); ra.corr = dcorr_.get();
+    ra.out_dists = ws_.out_d.get(); ra.out_ids = ws_.out_i.get();
+    ra.nq = Bq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = ws_.ck;
+    ra.ck_pad = ws_.ck_pad; ra.k = ws_.k; ra.grid = ws_.grid;
+    refine_topk(ra, s);
+    mark(5);
+}
+
+void Index::run_batch(cudaStream_t s, int nvalid) {
+    set_int(ws_.nvalid.get(), nvalid, s);
+    if (!profiling_) {
+        JHQ_CUDA(cudaGraphLaunch(ws_.exec, s));
+        count_launch((int)ws_.graph_kernels);
+        return;
+    }
+    // profiled batch: direct launches with events between the stages
+    for (auto& e : prof_ev_)
+        if (!e) JHQ_CUDA(cudaEventCreate(&e));
+    enqueue_batch(s, prof_ev_);
+    JHQ_CUDA(cudaEventSynchronize(prof_ev_[5]));
+    for (int i = 0; i < 5; ++i) {
+        float ms = 0.0f;
+        JHQ_CUDA(cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]));
+        stage_ms_[i] += ms;
+    }
+    ++stage_batches_;
+}
+
+void Index::set_profiling(bool on) {
+    profiling_ = on;
+    for (double& v : stage_ms_) v = 0.0;
+    stage_batches_ = 0;
+}
+
+void Index::stage_times(double* ms, int64_t* batches, int n) const {
+    for (int i = 0; i < n && i < 5; ++i) {
+        if (ms) ms[i] = stage_ms_[i];
+    }
+    if (batches) *batches = stage_batches_;
+}
+
+void Index::search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t* h_ids) {
+    DeviceGuard g(dev_);
+    check_search_args(nq, k);
+    if (nq == 0) return;
+    if (!h_q || !h_dists || !h_ids) fail(JHQ_EINVAL, "search: null buffer");
+    prepare_workspace(k);
+    const int Bq = ws_.batch_cap;
+    const int64_t nb = ceil_div(nq, Bq);
+    cudaEvent_t ev[2];
+    JHQ_CUDA(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
+    JHQ_CUDA(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
+    int64_t pending[2] = {-1, -1};
+    auto drain = [&](int slot) {
+        if (pending[slot] < 0) return;
+        JHQ_CUDA(cudaEventSynchronize(ev[slot]));
+        const int64_t b = pending[slot];
+        const int64_t q0 = b * Bq, nv = std::min<int64_t>(Bq, nq - q0);
+        std::memcpy(h_dists + q0 * k, ws_.h_d.get() + (size_t)slot * Bq * k, (size_t)nv * k * 4);
+        std::memcpy(h_ids + q0 * k, ws_.h_i.get() + (size_t)slot * Bq * k, (size_t)nv * k * 4);
+        pending[slot] = -1;
+    };
+    try {
+        for (int64_t b = 0; b < nb; ++b) {
+            const int slot = (int)(b & 1);
+            drain(slot);
+            const int64_t q0 = b * Bq, nv = std::min<int64_t>(Bq, nq - q0);
+            float* hq = ws_.h_q.get() + (size_t)slot * Bq * d_;
+            std::memcpy(hq, h_q + q0 * d_, (size_t)nv * d_ * 4);
+            if (nv < Bq) std::memset(hq + nv * d_, 0, (size_t)(Bq - nv) * d_ * 4);
+            h2d(ws_.q.get(), hq, (size_t)Bq * d_, stream_);
+            run_batch(stream_, (int)nv);
+            d2h(ws_.h_d.get() + (size_t)slot * Bq * k, ws_.out_d.get(), (size_t)Bq * k, stream_);
+            d2h(ws_.h_i.get() + (size_t)slot * Bq * k, ws_.out_i.get(), (size_t)Bq * k, stream_);
+            JHQ_CUDA(cudaEventRecord(ev[slot], stream_));
+            pending[slot] = b;
+        }
+        drain((int)(nb & 1));
+        drain((int)((nb + 1) & 1));
+    } catch (...) {
+        cudaStreamSynchronize(stream_);
+        cudaEventDestroy(ev[0]);
+        cudaEventDestroy(ev[1]);
+        throw;
+    }
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
+}
+
+void Index::search_device(const float* d_q, int64_t nq, int k, float* d_dists, int32_t* d_ids,
+                          cudaStream_t stream) {
+    DeviceGuard g(dev_);
+    check_search_args(nq, k);
+    if (nq == 0) return;
+    if (!d_q || !d_dists || !d_ids) fail(JHQ_EINVAL, "search_device: null buffer");
+    prepare_workspace(k);
+    cudaStream_t s = stream ? stream : stream_;
+    const int Bq = ws_.batch_cap;
+    for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
+        const int64_t nv = std::min<int64_t>(Bq, nq - q0);
+        JHQ_CUDA(cudaMemcpyAsync(ws_.q.get(), d_q + q0 * d_, (size_t)nv * d_ * 4,
+                                 cudaMemcpyDeviceToDevice, s));
+        run_batch(s, (int)nv);
+        JHQ_CUDA(cudaMemcpyAsync(d_dists + q0 * k, ws_.out_d.get(), (size_t)nv * k * 4,
+                                 cudaMemcpyDeviceToDevice, s));
+        JHQ_CUDA(cudaMemcpyAsync(d_ids + q0 * k, ws_.out_i.get(), (size_t)nv * k * 4,
+                                 cudaMemcpyDeviceToDevice, s));
+    }
+}
+
+void Index::synchronize(double timeout_s) {
+    DeviceGuard g(dev_);
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaStreamQuery(stream_);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) JHQ_CUDA(e);
+        double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > timeout_s) fail(JHQ_ETIMEDOUT, "synchronize: stream still busy at the deadline");
+        std::this_thread::yield();
+    }
+}
+
+// ---- inspection ---------------------------------------------------------------
+void Index::get_codes(uint8_t* primary, uint8_t* residual, float* corr, int32_t* assign) const {
+    DeviceGuard g(dev_);
+    const int64_t n = ntotal_;
+    if (n == 0) return;
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    if (primary) JHQ_CUDA(cudaMemcpy(primary, dpcodes_.get(), (size_t)n * M_, cudaMemcpyDeviceToHost));
+    if (residual)
+        JHQ_CUDA(cudaMemcpy2D(residual, bpv_, drcodes_.get(), bpv_pad_, bpv_, (size_t)n,
+                              cudaMemcpyDeviceToHost));
+    if (corr) JHQ_CUDA(cudaMemcpy(corr, dcorr_.get(), (size_t)n * 4, cudaMemcpyDeviceToHost));
+    if (assign) std::memcpy(assign, h_assign_.data(), (size_t)n * 4);
+}
+
+void Index::rotate(const float* h_x, int64_t n, float* h_y) {
+    DeviceGuard g(dev_);
+    if (!trained_) fail(JHQ_ESTATE, "index is not trained");
+    if (n <= 0) return;
+    DevBuf<float> dx((size_t)n * d_), dy((size_t)n * d_);
+    h2d(dx.get(), h_x, (size_t)n * d_, stream_);
+    rotate_device(dx.get(), n, dy.get(), stream_);
+    d2h(h_y, dy.get(), (size_t)n * d_, stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+}
+
+void Index::encode(const float* h_y, int64_t n, uint8_t* primary, uint8_t* residual, float* corr) {
+    DeviceGuard g(dev_);
+    if (!trained_) fail(JHQ_ESTATE, "index is not trained");
+    if (n <= 0) return;
+    DevBuf<float> dy((size_t)n * d_);
+    DevBuf<uint8_t> pc((size_t)n * M_), rc((size_t)n * bpv_pad_);
+    DevBuf<float> co((size_t)n);
+    h2d(dy.get(), h_y, (size_t)n * d_, stream_);
+    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), dres_.get(), pc.get(), rc.get(),
+                bpv_pad_, co.get(), stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    if (primary) JHQ_CUDA(cudaMemcpy(primary, pc.get(), (size_t)n * M_, cudaMemcpyDeviceToHost));
+    if (residual)
+        JHQ_CUDA(cudaMemcpy2D(residual, bpv_, rc.get(), bpv_pad_, bpv_, (size_t)n,
+                              cudaMemcpyDeviceToHost));
+    if (corr) JHQ_CUDA(cudaMemcpy(corr, co.get(), (size_t)n * 4, cudaMemcpyDeviceToHost));
+}
+
+// ---- persistence ----------------------------------------------------------------
+namespace {
+constexpr char MAGIC[8] = {'J', 'H', 'Q', 'B', '2', '0', '0', '\0'};
+constexpr uint32_t FORMAT_VERSION = 1;
+}
+
+void Index::save(const std::string& path) const {
+    DeviceGuard g(dev_);
+    if (!trained_) fail(JHQ_ESTATE, "save: index is not trained");
+    std::ofstream f(path, std::ios::binary);
+    if (!f) fail(JHQ_EIO, "save: cannot open " + path);
+    auto put = [&](const void* p, size_t n) { f.write(static_cast<const char*>(p), (std::streamsize)n); };
+    put(MAGIC, 8);
+    put(&FORMAT_VERSION, 4);
+    int32_t hdr[12] = {d_, p_.M, p_.B, p_.Br, p_.nlist, p_.nprobe, p_.ivf_iters,
+                       p_.batch_size, p_.seed, p_.add_batch, 0, 0};
+    put(hdr, sizeof hdr);
+    put(&p_.alpha, 4);
+    put(&sigma_, 4);
+    put(&ntotal_, 8);
+    put(Pi_.data(), Pi_.size() * 4);
+    put(c1d_.data(), c1d_.size() * 4);
+    put(res_c1d_.data(), res_c1d_.size() * 4);
+    put(cents_.data(), cents_.size() * 4);
+    if (ntotal_ > 0) {
+        std::vector<uint8_t> pc((size_t)ntotal_ * M_), rc((size_t)ntotal_ * bpv_);
+        std::vector<float> co((size_t)ntotal_);
+        std::vector<int32_t> as((size_t)ntotal_);
+        get_codes(pc.data(), rc.data(), co.data(), as.data());
+        put(pc.data(), pc.size());
+        put(rc.data(), rc.size());
+        put(co.data(), co.size() * 4);
+        put(as.data(), as.size() * 4);
+    }
+    if (!f) fail(JHQ_EIO, "save: write failed for " + path);
+}
+
+Index* Index::load(const std::string& path, int device) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) fail(JHQ_EIO, "load: cannot open " + path);
+    auto get = [&](void* p, size_t n) {
+        f.read(static_cast<char*>(p), (std::streamsize)n);
+        if (!f) fail(JHQ_EIO, "load: truncated file " + path);
+    };
+    char magic[8];
+    uint32_t ver = 0;
+    get(magic, 8);
+    get(&ver, 4);
+    if (std::memcmp(magic, MAGIC, 8) != 0 || ver != FORMAT_VERSION) fail(JHQ_EIO, "load: not a JHQ-B200 index file");
+    int32_t hdr[12];
+    get(hdr, sizeof hdr);
+    Params p;
+    p.M = hdr[1]; p.B = hdr[2]; p.Br = hdr[3]; p.nlist = hdr[4]; p.nprobe = hdr[5];
+    p.ivf_iters = hdr[6]; p.batch_size = hdr[7]; p.seed = hdr[8]; p.add_batch = hdr[9];
+    p.device = device;
+    get(&p.alpha, 4);
+    float sigma;
+    int64_t n;
+    get(&sigma, 4);
+    get(&n, 8);
+    if (n < 0 || n > INT32_MAX) fail(JHQ_EIO, "load: bad vector count");
+    Index* idx = new Index(hdr[0], p);
+    try {
+        const int d = idx->d_;
+        std::vector<float> Pi((size_t)d * d), c1d(idx->K1D_), res(idx->Kr_), cents((size_t)p.nlist * d);
+        get(Pi.data(), Pi.size() * 4);
+        get(c1d.data(), c1d.size() * 4);
+        get(res.data(), res.size() * 4);
+        get(cents.data(), cents.size() * 4);
+        idx->set_trained(Pi.data(), c1d.data(), res.data(), cents.data(), sigma);
+        if (n > 0) {
+            DeviceGuard g(idx->dev_);
+            std::vector<uint8_t> pc((size_t)n * idx->M_), rc((size_t)n * idx->bpv_);
+            std::vector<float> co((size_t)n);
+            std::vector<int32_t> as((size_t)n);
+            get(pc.data(), pc.size());
+            get(rc.data(), rc.size());
+            get(co.data(), co.size() * 4);
+            get(as.data(), as.size() * 4);
+            for (int32_t a : as)
+                if (a < 0 || a >= p.nlist) fail(JHQ_EIO, "load: bad list id");
+            idx->grow_master(n);
+            JHQ_CUDA(cudaMemcpy(idx->dpcodes_.get(), pc.data(), pc.size(), cudaMemcpyHostToDevice));
+            JHQ_CUDA(cudaMemcpy2D(idx->drcodes_.get(), idx->bpv_pad_, rc.data(), idx->bpv_, idx->bpv_,
+                                  (size_t)n, cudaMemcpyHostToDevice));
+            JHQ_CUDA(cudaMemset2D(idx->drcodes_.get() + idx->bpv_, idx->bpv_pad_, 0,
+                                  idx->bpv_pad_ - idx->bpv_, (size_t)n));
+            JHQ_CUDA(cudaMemcpy(idx->dcorr_.get(), co.data(), co.size() * 4, cudaMemcpyHostToDevice));
+            JHQ_CUDA(cudaMemcpy(idx->dassign_.get(), as.data(), as.size() * 4, cudaMemcpyHostToDevice));
+            idx->h_assign_ = std::move(as);
+            idx->ntotal_ = n;
+            idx->rebuild_layout();
+        }
+    } catch (...) {
+        delete idx;
+        throw;
+    }
+    return idx;
+}
+
+}  // namespace jhq

@@ -1,0 +1,121 @@
+// index.h — jhq::Index, the B200 counterpart of the reference's
+// jhq_gpu::JHQGpuIndex (jhq_v14_streaming_add/jhq_gpu_index.cuh:14-83) with
+// its SearchWorkspace (search.cuh:24-46).
+//
+// Device data held per index (HBM):
+//   Pi [d][d] fp32 (the reference's column-major array, used as the row-major
+//   right operand of y = x . Pi), c1d [K1D], res_c1d [Kr], centroids
+//   transposed [d][nlist] and their norms [nlist];
+//   id-ordered "master" codes: primary [N][M], residual [N][bpv_pad]
+//   (bpv_pad = ceil(d*Br/8) rounded up to 16), corr [N], list [N];
+//   the scan layout: pages [npages][Mp/16][32][16] of primary codes grouped
+//   by list (each list padded to whole 32-vector pages), slot_ids
+//   [npages*32] (-1 = empty slot) and list_page_off [nlist+1].
+// The master arrays grow geometrically, so add() may be called repeatedly;
+// the page layout is rebuilt from them after every add().
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "jhq_common.h"
+
+namespace jhq {
+
+struct Params {
+    int M = 96, B = 8, Br = 4;
+    float alpha = 4.0f;
+    int nlist = 1024, nprobe = 8, ivf_iters = 8, batch_size = 256, seed = 42;
+    int add_batch = 65536;
+    int device = -1;
+};
+
+class Index {
+public:
+    Index(int d, const Params& p);
+    ~Index();
+    Index(const Index&) = delete;
+    Index& operator=(const Index&) = delete;
+
+    void train(const float* h_x, int64_t n);
+    void add(const float* h_x, int64_t n);
+    void search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t* h_ids);
+    void search_device(const float* d_q, int64_t nq, int k, float* d_dists, int32_t* d_ids,
+                       cudaStream_t stream);
+    void synchronize(double timeout_s);
+
+    int64_t ntotal() const { return ntotal_; }
+    int dim() const { return d_; }
+    bool trained() const { return trained_; }
+    const Params& params() const { return p_; }
+    int device() const { return dev_; }
+
+    void get_trained(float* Pi, float* c1d, float* res_c1d, float* cents, float* sigma) const;
+    void set_trained(const float* Pi, const float* c1d, const float* res_c1d, const float* cents,
+                     float sigma);
+    void get_codes(uint8_t* primary, uint8_t* residual, float* corr, int32_t* assign) const;
+    void rotate(const float* h_x, int64_t n, float* h_y);
+    void encode(const float* h_y, int64_t n, uint8_t* primary, uint8_t* residual, float* corr);
+    void save(const std::string& path) const;
+    static Index* load(const std::string& path, int device);
+
+    void set_profiling(bool on);
+    void stage_times(double* ms, int64_t* batches, int n) const;
+
+    int K1D() const { return K1D_; }
+    int Kr() const { return Kr_; }
+    int bpv() const { return bpv_; }
+
+private:
+    struct Workspace {                 // SearchWorkspace (search.cuh:24-46)
+        int batch_cap = 0, k = 0, ck = 0, ck_pad = 0, grid = 0;
+        PinnedBuf<float> h_q;          // [batch][d] staged queries
+        PinnedBuf<float> h_d;          // [batch][k]
+        PinnedBuf<int32_t> h_i;
+        PinnedBuf<int> h_nvalid;
+        DevBuf<float> q, q_rot, scores, out_d;
+        DevBuf<int32_t> probes, ppo, out_i;
+        DevBuf<int64_t> qpage_off;
+        DevBuf<uint64_t> cand;
+        DevBuf<int> nvalid;
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        int64_t graph_kernels = 0;
+    };
+
+    void upload_trained();
+    void rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const;
+    void assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaStream_t s);
+    void grow_master(int64_t need);
+    void rebuild_layout();
+    void prepare_workspace(int k);
+    void destroy_graph();
+    void enqueue_batch(cudaStream_t s, cudaEvent_t* ev = nullptr);
+    void run_batch(cudaStream_t s, int nvalid);
+    void check_search_args(int64_t nq, int k) const;
+
+    int d_, M_, B_, Br_, Ds_, bpd_, K1D_, Kr_, bpv_, bpv_pad_, Mp_;
+    Params p_;
+    int dev_ = 0;
+    cudaStream_t stream_ = nullptr;
+    bool trained_ = false;
+    int64_t ntotal_ = 0, cap_ = 0, npages_ = 0;
+    float sigma_ = 1.0f;
+    std::vector<float> Pi_, c1d_, res_c1d_, cents_;
+    std::vector<int32_t> h_assign_;
+    bool layout_dirty_ = true;
+    bool profiling_ = false;
+    double stage_ms_[5] = {0, 0, 0, 0, 0};
+    int64_t stage_batches_ = 0;
+    cudaEvent_t prof_ev_[6] = {};
+
+    DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dnorms_;
+    DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
+    DevBuf<float> dcorr_;
+    DevBuf<int32_t> dassign_, dslot_ids_, dlist_page_off_;
+    Workspace ws_;
+};
+
+}  // namespace jhq

@@ -1,0 +1,154 @@
+// refine.cu — per query: merge the scan's candidate slots into the exact
+// top-ck, refine them with the Br-bit residual code and return the top-k.
+// Replaces build_residual_lut_batched_kernel + residual_refine_batched_kernel
+// + batched_topk_final_kernel of the reference (jhq_v14_streaming_add/
+// search.cu:198-291) with one kernel, one CTA per query:
+//   1. the CTAs that scanned part of query q wrote slots (c + q); they are the
+//      CTAs whose page ranges [c*T/grid, (c+1)*T/grid) meet q's pages. Their
+//      sorted top-ck lists are merged pairwise (bitonic merge of two halves);
+//   2. warp per candidate: lane l reads 32-bit words l, l+32, ... of the
+//      candidate's residual row (coalesced), accumulates (q_j - res_c1d[r_j])^2
+//      as an in-order fma chain, and the warp reduces with an xor butterfly
+//      (offsets 16..1) — the order fixed in oracle/jhq_oracle.c;
+//      comp = (primary + residual) + corr (search.cu:240);
+//   3. block bitonic sort of the ck composite keys; the first k are written,
+//      missing ones as (+inf, -1) (search.cu:285-286).
+#include "device_utils.cuh"
+#include "jhq_common.h"
+#include "kernels.cuh"
+
+namespace jhq {
+namespace {
+
+constexpr int RF_THREADS = 256;
+constexpr int RF_WARPS = RF_THREADS / 32;
+
+__global__ void __launch_bounds__(RF_THREADS)
+refine_kernel(RefineArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint64_t* top = reinterpret_cast<uint64_t*>(smem);            // 2 * ck_pad
+    uint64_t* comp = top + 2 * a.ck_pad;                           // ck_pad
+    float* qs = reinterpret_cast<float*>(comp + a.ck_pad);         // d
+    float* rc1d = qs + a.d;                                        // 256
+
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (q >= a.nq) return;
+    const int Kr = 1 << a.Br;
+    for (int i = tid; i < a.ck_pad; i += RF_THREADS) top[i] = KEY_EMPTY;
+    for (int i = tid; i < a.d; i += RF_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
+    for (int i = tid; i < Kr; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
+    __syncthreads();
+
+    const int64_t T = a.qpage_off[a.nq];
+    const int64_t P0 = a.qpage_off[q], P1 = a.qpage_off[q + 1];
+    if (P1 > P0) {
+        // first CTA whose range end (c+1)*T/grid exceeds P0
+        int lo = 0, hi = a.grid - 1;
+        while (lo < hi) {
+            int mid = (lo + hi) >> 1;
+            if ((int64_t)(mid + 1) * T / a.grid > P0) hi = mid; else lo = mid + 1;
+        }
+        for (int c = lo; c < a.grid; ++c) {
+            const int64_t s0 = (int64_t)c * T / a.grid, s1 = (int64_t)(c + 1) * T / a.grid;
+            if (s0 >= P1) break;
+            if (s1 <= s0) continue;
+            const uint64_t* src = a.cand + ((int64_t)c + q) * a.ck;
+            for (int i = tid; i < a.ck_pad; i += RF_THREADS)
+                top[a.ck_pad + i] = (i < a.ck) ? src[i] : KEY_EMPTY;
+            __syncthreads();
+            block_merge_halves(top, a.ck_pad);
+        }
+    }
+
+    // residual refine, warp per candidate
+    const int words = a.bpv_pad / 4, dpw = 32 / a.Br, mask = Kr - 1;
+    for (int i = warp; i < a.ck_pad; i += RF_WARPS) {
+        const uint64_t key = (i < a.ck) ? top[i] : KEY_EMPTY;
+        if (key == KEY_EMPTY) {
+            if (lane == 0) comp[i] = KEY_EMPTY;
+            continue;
+        }
+        const int id = key_id(key);
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(a.rcodes + (int64_t)id * a.bpv_pad);
+        float acc = 0.0f;
+        for (int w = lane; w < words; w += 32) {
+            const uint32_t word = __ldg(row + w);
+            for (int t = 0; t < dpw; ++t) {
+                const int j = w * dpw + t;
+                if (j >= a.d) break;
+                const float diff = qs[j] - rc1d[(word >> (t * a.Br)) & mask];
+                acc = __fmaf_rn(diff, diff, acc);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (lane == 0) {
+            const float c = __fadd_rn(__fadd_rn(key_dist(key), acc), __ldg(a.corr + id));
+            comp[i] = make_key(c, id);
+        }
+    }
+    __syncthreads();
+    block_bitonic_sort(comp, a.ck_pad);
+    for (int i = tid; i < a.k; i += RF_THREADS) {
+        const uint64_t key = comp[i];
+        const bool ok = key != KEY_EMPTY;
+        a.out_dists[(int64_t)q * a.k + i] = ok ? key_dist(key) : __int_as_float(0x7f800000);
+        a.out_ids[(int64_t)q * a.k + i] = ok ? key_id(key) : -1;
+    }
+}
+
+__global__ void __launch_bounds__(RF_THREADS)
+merge_shards_kernel(const float* __restrict__ in_d, const int32_t* __restrict__ in_i,
+                    int nshards, int64_t nq, int k, int n_pad,
+                    float* __restrict__ out_d, int32_t* __restrict__ out_i) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    uint64_t* s = reinterpret_cast<uint64_t*>(smem);
+    const int64_t q = blockIdx.x;
+    for (int i = threadIdx.x; i < n_pad; i += RF_THREADS) {
+        uint64_t key = KEY_EMPTY;
+        if (i < nshards * k) {
+            const int sh = i / k, j = i % k;
+            const int64_t at = ((int64_t)sh * nq + q) * k + j;
+            const int32_t id = in_i[at];
+            if (id >= 0) key = make_key(in_d[at], id);
+        }
+        s[i] = key;
+    }
+    __syncthreads();
+    block_bitonic_sort(s, n_pad);
+    for (int i = threadIdx.x; i < k; i += RF_THREADS) {
+        const uint64_t key = s[i];
+        const bool ok = key != KEY_EMPTY;
+        out_d[q * k + i] = ok ? key_dist(key) : __int_as_float(0x7f800000);
+        out_i[q * k + i] = ok ? key_id(key) : -1;
+    }
+}
+
+}  // namespace
+
+void refine_topk(const RefineArgs& a, cudaStream_t st) {
+    if (a.nq <= 0) return;
+    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + 256) * 4;
+    refine_kernel<<<a.nq, RF_THREADS, smem, st>>>(a);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
+void refine_configure() {
+    JHQ_CUDA(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  227 * 1024));
+}
+
+void merge_shard_lists(const float* in_d, const int32_t* in_i, int nshards, int64_t nq,
+                       int k, float* out_d, int32_t* out_i, cudaStream_t st) {
+    if (nq <= 0 || k <= 0) return;
+    int n_pad = next_pow2(nshards * k);
+    size_t smem = (size_t)n_pad * 8;
+    if (smem > 48 * 1024) fail(JHQ_EINVAL, "merge_shards: nshards * k too large");
+    merge_shards_kernel<<<(unsigned)nq, RF_THREADS, smem, st>>>(in_d, in_i, nshards, nq, k, n_pad,
+                                                               out_d, out_i);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
+}  // namespace jhq

@@ -1,0 +1,232 @@
+"""ctypes bindings for the JHQ oracle (test infrastructure only).
+
+`Oracle` wraps oracle/_build/libjhq_oracle.so (the scalar C restatement in
+jhq_oracle.c); `RefCPU` wraps oracle/_ref/libjhq_ref.so (the reference's own
+cpu/ trainer compiled from its sources by oracle/Makefile). Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline legs import this package;
+the product (jhq_gpu_b200) never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libjhq_oracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libjhq_ref.so")
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i64 = C.c_int64
+
+
+def build(ref: bool = False) -> None:
+    """Compile the oracle (and, if asked and the reference tree exists, oracle/_ref)."""
+    targets = ["oracle"]
+    if ref and os.path.isdir(os.environ.get("REF", "/root/reference")):
+        targets.append("ref")
+    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Oracle:
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.oracle_sigma.restype = C.c_float
+        L.oracle_sigma.argtypes = [_f32p, _i64, C.c_int]
+        L.oracle_erfinv.restype = C.c_float
+        L.oracle_erfinv.argtypes = [C.c_float]
+        L.oracle_c1d.argtypes = [C.c_float, C.c_int, _f32p]
+        L.oracle_kmeans1d.argtypes = [_f32p, _i64, C.c_int, C.c_int, _f32p]
+        L.oracle_reconstruct.argtypes = [_u8p, _i64, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+        L.oracle_rotate.argtypes = [_f32p, C.c_int, _f32p, _i64, _f32p]
+        L.oracle_encode_primary.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, _f32p, _u8p]
+        L.oracle_encode_residual.argtypes = [_f32p, _u8p, _i64, C.c_int, C.c_int, C.c_int,
+                                             _f32p, _f32p, C.c_int, _u8p, _f32p]
+        L.oracle_cent_norms.argtypes = [_f32p, C.c_int, C.c_int, _f32p]
+        L.oracle_assign.argtypes = [_f32p, _i64, C.c_int, _f32p, _f32p, C.c_int, _i32p]
+        L.oracle_train_ivf.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, _f32p]
+        L.oracle_byte_lut.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _f32p, _f32p]
+        L.oracle_adc.restype = C.c_float
+        L.oracle_adc.argtypes = [_f32p, C.c_int, _u8p]
+        L.oracle_residual.restype = C.c_float
+        L.oracle_residual.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _u8p]
+        L.oracle_ck.argtypes = [C.c_int, C.c_float]
+        L.oracle_search.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, C.c_int,
+                                    _f32p, _f32p, _u8p, _u8p, _f32p, _i32p, _i64,
+                                    _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_float,
+                                    C.c_int, _f32p, _i32p]
+        self.L = L
+
+    def sigma(self, x):
+        x = _f32(x)
+        return self.L.oracle_sigma(x, x.shape[0], x.shape[1])
+
+    def c1d(self, sigma, K1D):
+        out = np.zeros(K1D, np.float32)
+        self.L.oracle_c1d(sigma, K1D, out)
+        return out
+
+    def kmeans1d(self, vals, Kr, max_iter=25):
+        vals = _f32(vals).ravel()
+        out = np.zeros(Kr, np.float32)
+        n = self.L.oracle_kmeans1d(vals, vals.size, Kr, max_iter, out)
+        return out[:n]
+
+    def reconstruct(self, codes, d, M, B, c1d):
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.zeros((codes.shape[0], d), np.float32)
+        self.L.oracle_reconstruct(codes, codes.shape[0], d, M, B, _f32(c1d), out)
+        return out
+
+    def rotate(self, P, x):
+        x = _f32(x)
+        y = np.zeros_like(x)
+        self.L.oracle_rotate(_f32(P), x.shape[1], x, x.shape[0], y)
+        return y
+
+    def encode_primary(self, y, M, B, c1d):
+        y = _f32(y)
+        codes = np.zeros((y.shape[0], M), np.uint8)
+        self.L.oracle_encode_primary(y, y.shape[0], y.shape[1], M, B, _f32(c1d), codes)
+        return codes
+
+    def encode_residual(self, y, codes, M, B, c1d, res_c1d, Br):
+        y = _f32(y)
+        n, d = y.shape
+        bpv = (d * Br + 7) // 8
+        rc = np.zeros((n, bpv), np.uint8)
+        corr = np.zeros(n, np.float32)
+        self.L.oracle_encode_residual(y, np.ascontiguousarray(codes, np.uint8), n, d, M, B,
+                                      _f32(c1d), _f32(res_c1d), Br, rc, corr)
+        return rc, corr
+
+    def cent_norms(self, cents):
+        cents = _f32(cents)
+        out = np.zeros(cents.shape[0], np.float32)
+        self.L.oracle_cent_norms(cents, cents.shape[0], cents.shape[1], out)
+        return out
+
+    def assign(self, y, cents, norms=None):
+        y, cents = _f32(y), _f32(cents)
+        if norms is None:
+            norms = self.cent_norms(cents)
+        out = np.zeros(y.shape[0], np.int32)
+        self.L.oracle_assign(y, y.shape[0], y.shape[1], cents, _f32(norms), cents.shape[0], out)
+        return out
+
+    def train_ivf(self, y, nlist, iters):
+        y = _f32(y)
+        cents = np.zeros((nlist, y.shape[1]), np.float32)
+        self.L.oracle_train_ivf(y, y.shape[0], y.shape[1], nlist, iters, cents)
+        return cents
+
+    def byte_lut(self, q_rot, M, B, c1d):
+        q = _f32(q_rot).ravel()
+        lut = np.zeros((M, 256), np.float32)
+        self.L.oracle_byte_lut(q, q.size, M, B, _f32(c1d), lut)
+        return lut
+
+    def residual(self, q_rot, Br, res_c1d, rcode):
+        q = _f32(q_rot).ravel()
+        return self.L.oracle_residual(q, q.size, Br, _f32(res_c1d), np.ascontiguousarray(rcode, np.uint8))
+
+    def ck(self, k, alpha):
+        return self.L.oracle_ck(k, alpha)
+
+    def search(self, q_rot, *, M, B, Br, c1d, res_c1d, codes, res, corr, assign,
+               cents, k, alpha, nprobe, norms=None, nthreads=0):
+        q = _f32(q_rot)
+        nq, d = q.shape
+        cents = _f32(cents)
+        if norms is None:
+            norms = self.cent_norms(cents)
+        D = np.zeros((nq, k), np.float32)
+        I = np.zeros((nq, k), np.int32)
+        rc = self.L.oracle_search(q, nq, d, M, B, Br, _f32(c1d), _f32(res_c1d),
+                                  np.ascontiguousarray(codes, np.uint8),
+                                  np.ascontiguousarray(res, np.uint8), _f32(corr),
+                                  np.ascontiguousarray(assign, np.int32), codes.shape[0],
+                                  cents, _f32(norms), cents.shape[0], nprobe, k, alpha,
+                                  nthreads, D, I)
+        if rc != 0:
+            raise ValueError("oracle_search: bad arguments")
+        return D, I
+
+
+class RefCPU:
+    """The reference's own cpu/ code (codebook.cpp, jl_transform.cpp) via oracle/_ref."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = C.CDLL(path)
+        L.ref_rotation.argtypes = [C.c_int, C.c_int, _f32p]
+        L.ref_apply.argtypes = [C.c_int, C.c_int, _f32p, C.c_int, _f32p]
+        L.ref_sigma.restype = C.c_float
+        L.ref_sigma.argtypes = [_f32p, C.c_int, C.c_int]
+        L.ref_c1d.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p]
+        L.ref_encode.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, C.c_int, _u8p]
+        L.ref_flat_lut.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, _f32p]
+        L.ref_adc.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _f32p, _u8p, C.c_int, _f32p]
+        L.ref_reconstruct.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, _u8p, C.c_int, _f32p]
+        L.ref_kmeans1d.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _f32p]
+        self.L = L
+
+    def rotation(self, d, seed=42):
+        P = np.zeros(d * d, np.float32)
+        assert self.L.ref_rotation(d, seed, P) == 0
+        return P
+
+    def apply(self, d, seed, x):
+        x = _f32(x)
+        y = np.zeros_like(x)
+        assert self.L.ref_apply(d, seed, x, x.shape[0], y) == 0
+        return y
+
+    def sigma(self, x):
+        x = _f32(x)
+        return self.L.ref_sigma(x, x.shape[0], x.shape[1])
+
+    def c1d(self, d, M, B, sigma):
+        out = np.zeros(256, np.float32)
+        K = self.L.ref_c1d(d, M, B, sigma, out)
+        return out[:K]
+
+    def encode(self, d, M, B, sigma, y):
+        y = _f32(y)
+        codes = np.zeros((y.shape[0], M), np.uint8)
+        assert self.L.ref_encode(d, M, B, sigma, y, y.shape[0], codes) == 0
+        return codes
+
+    def flat_lut(self, d, M, B, sigma, q_rot):
+        out = np.zeros((M, 256), np.float32)
+        assert self.L.ref_flat_lut(d, M, B, sigma, _f32(q_rot).ravel(), out) == 0
+        return out
+
+    def adc(self, d, M, B, sigma, q_rot, codes):
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.zeros(codes.shape[0], np.float32)
+        assert self.L.ref_adc(d, M, B, sigma, _f32(q_rot).ravel(), codes, codes.shape[0], out) == 0
+        return out
+
+    def reconstruct(self, d, M, B, sigma, codes):
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.zeros((codes.shape[0], d), np.float32)
+        assert self.L.ref_reconstruct(d, M, B, sigma, codes, codes.shape[0], out) == 0
+        return out
+
+    def kmeans1d(self, vals, Kr, max_iter=25):
+        vals = _f32(vals).ravel()
+        out = np.zeros(Kr, np.float32)
+        n = self.L.ref_kmeans1d(vals, vals.size, Kr, max_iter, out)
+        return out[:n]
