@@ -368,6 +368,22 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_profile_case(args):
+    """Short C1 run for ncu: train on 20k rows, add all 100k, one warm-up search
+    (16 batches) and one search to capture — nothing else launches kernels."""
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200 import datasets
+    base, queries = datasets.make("c1", seed=CFG["seed"])
+    p = J.Params(M=CFG["M"], B=CFG["B"], Br=CFG["Br"], alpha=CFG["alpha"], nlist=CFG["nlist"],
+                 nprobe=CFG["nprobe"], batch_size=CFG["batch"], device=0)
+    idx = J.JHQGpuIndex(CFG["d"], p)
+    idx.train(base[:20_000])
+    idx.add(base)
+    for _ in range(2):
+        D, I = idx.search(queries, CFG["k"])
+    print("profile case done", int((I >= 0).sum()))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -375,8 +391,12 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)
-    if args.impl == "reference":
+    if args.profile_run:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

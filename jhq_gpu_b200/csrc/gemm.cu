@@ -8,9 +8,10 @@
 // (oracle/jhq_oracle.c: oracle_rotate / dot_chain). Two tilings:
 //  - gemm_tiled_kernel : 128x128 CTA tile, 8x8 outputs per thread, for tall
 //                        operands (add-time rotation, k-means assignment);
-//  - gemm_skinny_kernel: 8 rows x 128 columns per CTA, rows staged in shared
-//                        memory, B streamed coalesced — for query batches,
-//                        where a 128-row tile would leave most SMs idle.
+//  - gemm_skinny_kernel: 4 rows x 128 columns per CTA, both operands staged
+//                        through shared memory by double-buffered cp.async —
+//                        for query batches, where a 128-row tile would leave
+//                        most SMs idle.
 // The product is tiny next to the ADC scan at the flat and IVF configs
 // (C1: 64x1024x1024 per batch); it is not on tensor cores because the
 // codes must stay bit-exact with the fp32 fma-chain rotation.
@@ -109,55 +110,112 @@ gemm_tiled_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
     }
 }
 
-constexpr int SK_ROWS = 8, SK_COLS = 128, SK_KC = 512;
+// Skinny path: CTA = SK_TR rows x SK_BN columns, one column per thread with
+// SK_TR independent chains. Chunks of SK_KC rows of B (and the matching SK_TR x
+// SK_KC slice of A) are staged in shared memory by cp.async, double-buffered,
+// so the L2 latency of the streamed right operand overlaps the FMAs.
+constexpr int SK_TR = 4, SK_BN = 128, SK_KC = 32;
+
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    const int n = ok ? 4 : 0;                        // 0 -> zero fill, no read
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" :: "r"(d), "l"(src), "r"(n));
+}
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, int bytes) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" :: "r"(d), "l"(src), "r"(bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n"); }
 
 template <int EPI>
-__global__ void __launch_bounds__(SK_COLS)
+__global__ void __launch_bounds__(SK_BN)
 gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
-                   int64_t R, int K, int N, const float* __restrict__ norms) {
-    __shared__ float As[SK_ROWS][SK_KC];
-    const int64_t r0 = (int64_t)blockIdx.y * SK_ROWS;
-    const int n = blockIdx.x * SK_COLS + threadIdx.x;
-    float acc[SK_ROWS];
-#pragma unroll
-    for (int r = 0; r < SK_ROWS; ++r) acc[r] = 0.0f;
-    for (int kc = 0; kc < K; kc += SK_KC) {
-        const int kl = min(SK_KC, K - kc);
-        for (int i = threadIdx.x; i < SK_ROWS * SK_KC; i += SK_COLS) {
-            int r = i / SK_KC, k = i % SK_KC;
-            int64_t gr = r0 + r;
-            As[r][k] = (gr < R && k < kl) ? A[gr * K + kc + k] : 0.0f;
+                   int64_t R, int K, int N, const float* __restrict__ norms, int vec16) {
+    __shared__ __align__(16) float Bs[2][SK_KC][SK_BN];
+    __shared__ __align__(16) float As[2][SK_TR][SK_KC];
+    const int tid = threadIdx.x;
+    const int n0 = blockIdx.x * SK_BN;
+    const int64_t r0 = (int64_t)blockIdx.y * SK_TR;
+    const int n = n0 + tid;
+
+    auto stage = [&](int buf, int k0) {
+        if (vec16) {
+            // B chunk: SK_KC rows x SK_BN cols = SK_KC * 32 16-byte pieces
+            for (int i = tid; i < SK_KC * (SK_BN / 4); i += SK_BN) {
+                const int kr = i / (SK_BN / 4), c4 = (i % (SK_BN / 4)) * 4;
+                const int gk = k0 + kr, gn = n0 + c4;
+                int bytes = 0;
+                if (gk < K && gn < N) bytes = min(4, N - gn) * 4;
+                const float* src = bytes ? B + (int64_t)gk * N + gn : B;
+                cp_async16(&Bs[buf][kr][c4], src, bytes);
+            }
+            for (int i = tid; i < SK_TR * (SK_KC / 4); i += SK_BN) {
+                const int r = i / (SK_KC / 4), c4 = (i % (SK_KC / 4)) * 4;
+                const int64_t gr = r0 + r;
+                const int gk = k0 + c4;
+                int bytes = 0;
+                if (gr < R && gk < K) bytes = min(4, K - gk) * 4;
+                const float* src = bytes ? A + gr * K + gk : A;
+                cp_async16(&As[buf][r][c4], src, bytes);
+            }
+        } else {
+            for (int i = tid; i < SK_KC * SK_BN; i += SK_BN) {
+                const int kr = i / SK_BN, c = i % SK_BN;
+                const int gk = k0 + kr, gn = n0 + c;
+                const bool ok = gk < K && gn < N;
+                cp_async4(&Bs[buf][kr][c], ok ? B + (int64_t)gk * N + gn : B, ok);
+            }
+            for (int i = tid; i < SK_TR * SK_KC; i += SK_BN) {
+                const int r = i / SK_KC, c = i % SK_KC;
+                const int64_t gr = r0 + r;
+                const int gk = k0 + c;
+                const bool ok = gr < R && gk < K;
+                cp_async4(&As[buf][r][c], ok ? A + gr * K + gk : A, ok);
+            }
         }
-        __syncthreads();
-        if (n < N) {
-            const float* bp = B + (int64_t)kc * N + n;
-            int k = 0;
-            for (; k + 4 <= kl; k += 4) {
-                float b0 = __ldg(bp + (int64_t)(k + 0) * N);
-                float b1 = __ldg(bp + (int64_t)(k + 1) * N);
-                float b2 = __ldg(bp + (int64_t)(k + 2) * N);
-                float b3 = __ldg(bp + (int64_t)(k + 3) * N);
+        cp_async_commit();
+    };
+
+    float acc[SK_TR];
 #pragma unroll
-                for (int r = 0; r < SK_ROWS; ++r) {
-                    float4 a = *reinterpret_cast<const float4*>(&As[r][k]);
+    for (int r = 0; r < SK_TR; ++r) acc[r] = 0.0f;
+    const int nchunks = (K + SK_KC - 1) / SK_KC;
+    stage(0, 0);
+    for (int ch = 0; ch < nchunks; ++ch) {
+        const int buf = ch & 1;
+        if (ch + 1 < nchunks) { stage(buf ^ 1, (ch + 1) * SK_KC); cp_async_wait1(); }
+        else cp_async_wait0();
+        __syncthreads();
+        const int kl = min(SK_KC, K - ch * SK_KC);
+        if (kl == SK_KC) {
+#pragma unroll
+            for (int k = 0; k < SK_KC; k += 4) {
+                const float b0 = Bs[buf][k][tid], b1 = Bs[buf][k + 1][tid];
+                const float b2 = Bs[buf][k + 2][tid], b3 = Bs[buf][k + 3][tid];
+#pragma unroll
+                for (int r = 0; r < SK_TR; ++r) {
+                    const float4 a = *reinterpret_cast<const float4*>(&As[buf][r][k]);
                     acc[r] = __fmaf_rn(a.x, b0, acc[r]);
                     acc[r] = __fmaf_rn(a.y, b1, acc[r]);
                     acc[r] = __fmaf_rn(a.z, b2, acc[r]);
                     acc[r] = __fmaf_rn(a.w, b3, acc[r]);
                 }
             }
-            for (; k < kl; ++k) {
-                float b = __ldg(bp + (int64_t)k * N);
+        } else {
+            for (int k = 0; k < kl; ++k) {
+                const float b = Bs[buf][k][tid];
 #pragma unroll
-                for (int r = 0; r < SK_ROWS; ++r) acc[r] = __fmaf_rn(As[r][k], b, acc[r]);
+                for (int r = 0; r < SK_TR; ++r) acc[r] = __fmaf_rn(As[buf][r][k], b, acc[r]);
             }
         }
         __syncthreads();
     }
     if (n < N) {
 #pragma unroll
-        for (int r = 0; r < SK_ROWS; ++r) {
-            int64_t gr = r0 + r;
+        for (int r = 0; r < SK_TR; ++r) {
+            const int64_t gr = r0 + r;
             if (gr < R) C[gr * N + n] = epilogue<EPI>(acc[r], norms, n);
         }
     }
@@ -169,11 +227,13 @@ void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N
                GemmEpi epi, const float* norms, cudaStream_t s) {
     if (R <= 0 || N <= 0) return;
     if (R <= 1024) {
-        dim3 grid((unsigned)ceil_div(N, SK_COLS), (unsigned)ceil_div(R, SK_ROWS));
+        dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, SK_TR));
+        const int vec16 = (N % 4 == 0) && (K % 4 == 0) && (((uintptr_t)A | (uintptr_t)B) % 16 == 0);
+        if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");
         if (epi == EPI_COARSE)
-            gemm_skinny_kernel<EPI_COARSE><<<grid, SK_COLS, 0, s>>>(A, B, C, R, K, N, norms);
+            gemm_skinny_kernel<EPI_COARSE><<<grid, SK_BN, 0, s>>>(A, B, C, R, K, N, norms, vec16);
         else
-            gemm_skinny_kernel<EPI_STORE><<<grid, SK_COLS, 0, s>>>(A, B, C, R, K, N, norms);
+            gemm_skinny_kernel<EPI_STORE><<<grid, SK_BN, 0, s>>>(A, B, C, R, K, N, norms, vec16);
     } else {
         dim3 grid((unsigned)ceil_div(N, TBN), (unsigned)ceil_div(R, TBM));
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");

@@ -6,7 +6,7 @@
 //   1. the CTAs that scanned part of query q wrote slots (c + q); they are the
 //      CTAs whose page ranges [c*T/grid, (c+1)*T/grid) meet q's pages. Their
 //      sorted top-ck lists are merged pairwise (bitonic merge of two halves);
-//   2. warp per candidate: lane l reads 32-bit words l, l+32, ... of the
+//   2. warp per candidate: lane l reads 16-byte chunks l, l+32, ... of the
 //      candidate's residual row (coalesced), accumulates (q_j - res_c1d[r_j])^2
 //      as an in-order fma chain, and the warp reduces with an xor butterfly
 //      (offsets 16..1) — the order fixed in oracle/jhq_oracle.c;
@@ -20,7 +20,7 @@
 namespace jhq {
 namespace {
 
-constexpr int RF_THREADS = 256;
+constexpr int RF_THREADS = 512;
 constexpr int RF_WARPS = RF_THREADS / 32;
 
 __global__ void __launch_bounds__(RF_THREADS)
@@ -61,7 +61,7 @@ refine_kernel(RefineArgs a) {
     }
 
     // residual refine, warp per candidate
-    const int words = a.bpv_pad / 4, dpw = 32 / a.Br, mask = Kr - 1;
+    const int chunks = a.bpv_pad / 16, dpw = 32 / a.Br, mask = Kr - 1;
     for (int i = warp; i < a.ck_pad; i += RF_WARPS) {
         const uint64_t key = (i < a.ck) ? top[i] : KEY_EMPTY;
         if (key == KEY_EMPTY) {
@@ -69,15 +69,19 @@ refine_kernel(RefineArgs a) {
             continue;
         }
         const int id = key_id(key);
-        const uint32_t* row = reinterpret_cast<const uint32_t*>(a.rcodes + (int64_t)id * a.bpv_pad);
+        const uint4* row = reinterpret_cast<const uint4*>(a.rcodes + (int64_t)id * a.bpv_pad);
         float acc = 0.0f;
-        for (int w = lane; w < words; w += 32) {
-            const uint32_t word = __ldg(row + w);
-            for (int t = 0; t < dpw; ++t) {
-                const int j = w * dpw + t;
-                if (j >= a.d) break;
-                const float diff = qs[j] - rc1d[(word >> (t * a.Br)) & mask];
-                acc = __fmaf_rn(diff, diff, acc);
+        for (int c = lane; c < chunks; c += 32) {
+            const uint4 v = __ldg(row + c);
+            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                for (int t = 0; t < dpw; ++t) {
+                    const int j = (c * 4 + w) * dpw + t;
+                    if (j >= a.d) break;
+                    const float diff = qs[j] - rc1d[(wv[w] >> (t * a.Br)) & mask];
+                    acc = __fmaf_rn(diff, diff, acc);
+                }
             }
         }
 #pragma unroll

@@ -35,7 +35,7 @@
 namespace jhq {
 namespace {
 
-constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_THREADS = 512;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 
 struct ScanSmem {
@@ -115,13 +115,13 @@ struct WarpTop {
     int count;        // buffered entries (uniform)
     int ck, ck_pad, merge_n;
 
-    __device__ void reset(int lane) {
+    __device__ __forceinline__ void reset(int lane) {
         for (int i = lane; i < merge_n; i += 32) s[i] = KEY_EMPTY;
         thr = KEY_EMPTY;
         count = 0;
         __syncwarp();
     }
-    __device__ void flush(int lane) {
+    __device__ __forceinline__ void flush(int lane) {
         const int cap = merge_n - ck_pad;
         for (int i = count + lane; i < cap; i += 32) s[ck_pad + i] = KEY_EMPTY;
         __syncwarp();
@@ -145,8 +145,9 @@ struct WarpTop {
     }
 };
 
+// Small LUTs (Mp <= 32) leave room for two CTAs per SM: cap registers at 64.
 template <int G_T>
-__global__ void __launch_bounds__(SCAN_THREADS)
+__global__ void __launch_bounds__(SCAN_THREADS, (G_T > 0 && G_T <= 2) ? 2 : 1)
 scan_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const ScanSmem L = scan_smem_layout(a.Mp, a.d, a.ck_pad);
@@ -288,14 +289,28 @@ void scan_configure() {
 
 size_t scan_smem_bytes(int Mp, int d, int ck_pad) { return scan_smem_layout(Mp, d, ck_pad).total; }
 
+template <int G_T>
+int blocks_per_sm(size_t smem) {
+    int n = 0;
+    JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_kernel<G_T>, SCAN_THREADS, smem));
+    return n;
+}
+
 int scan_grid_for(int Mp, int d, int ck_pad) {
     int dev = 0, sms = 0;
     JHQ_CUDA(cudaGetDevice(&dev));
     JHQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    size_t smem = scan_smem_layout(Mp, d, ck_pad).total;
-    int per_sm = (int)((227 * 1024) / (smem + 1024));
-    if (per_sm < 1) per_sm = 1;
-    if (per_sm > 8) per_sm = 8;                  // 8 x 256 threads = 2048 per SM
+    const size_t smem = scan_smem_layout(Mp, d, ck_pad).total;
+    int per_sm = 0;
+    switch (Mp / 16) {
+        case 1: per_sm = blocks_per_sm<1>(smem); break;
+        case 2: per_sm = blocks_per_sm<2>(smem); break;
+        case 4: per_sm = blocks_per_sm<4>(smem); break;
+        case 6: per_sm = blocks_per_sm<6>(smem); break;
+        case 8: per_sm = blocks_per_sm<8>(smem); break;
+        default: per_sm = blocks_per_sm<0>(smem); break;
+    }
+    if (per_sm < 1) fail(JHQ_EINVAL, "scan: kernel does not fit on an SM (reduce M or d)");
     return sms * per_sm;
 }
 

@@ -7,6 +7,7 @@
 #include <cmath>
 #include <limits>
 #include <random>
+#include <thread>
 
 namespace jhq::train {
 
@@ -57,30 +58,59 @@ static inline int nearest_sorted(const float* c, int n, float v) {
 }
 
 std::vector<float> kmeans_1d(const float* vals, int64_t n64, int Kr, int max_iter) {
+    // Same result as a sequential run of cpu/codebook.cpp:8-58, faster:
+    //  - the quantile seeds are order statistics, found with nth_element instead
+    //    of a full sort (the values are identical);
+    //  - the assignment (pure function of the value) runs on all host threads;
+    //  - the double sums are still accumulated in index order, one pass, so every
+    //    rounding step is the reference's.
     int n = (int)n64;
     if (n <= 0 || Kr <= 0) return {};
     if (n < Kr) Kr = n;
-    std::vector<float> sorted(vals, vals + n);
-    std::sort(sorted.begin(), sorted.end());
-    auto seed_of = [&](int i) {
-        int idx = std::min((int)((i + 0.5f) / Kr * n), n - 1);
-        return sorted[idx];
-    };
-    std::vector<float> c(Kr);
-    for (int i = 0; i < Kr; ++i) c[i] = seed_of(i);
+    std::vector<int> qpos(Kr);
+    for (int i = 0; i < Kr; ++i) qpos[i] = std::min((int)((i + 0.5f) / Kr * n), n - 1);
+    std::vector<float> quant(Kr);
+    {
+        std::vector<float> work(vals, vals + n);
+        std::vector<int> order(Kr);
+        for (int i = 0; i < Kr; ++i) order[i] = i;
+        std::sort(order.begin(), order.end(), [&](int a, int b) { return qpos[a] < qpos[b]; });
+        int lo = 0;
+        for (int oi : order) {
+            int p = qpos[oi];
+            if (p >= lo) {
+                std::nth_element(work.begin() + lo, work.begin() + p, work.end());
+                lo = p + 1;
+                quant[oi] = work[p];
+            } else {
+                quant[oi] = work[p];       // repeated position: already in place
+            }
+        }
+    }
+    std::vector<float> c(quant);
     std::vector<double> sum(Kr);
     std::vector<int> cnt(Kr);
+    std::vector<uint8_t> lab((size_t)n);
+    unsigned nth = std::max(1u, std::min(32u, std::thread::hardware_concurrency()));
     for (int iter = 0; iter < max_iter; ++iter) {
+        std::vector<std::thread> pool;
+        const int64_t chunk = ((int64_t)n + nth - 1) / nth;
+        for (unsigned t = 0; t < nth; ++t) {
+            pool.emplace_back([&, t] {
+                int64_t a = t * chunk, b = std::min<int64_t>(n, a + chunk);
+                for (int64_t i = a; i < b; ++i) lab[i] = (uint8_t)nearest_sorted(c.data(), Kr, vals[i]);
+            });
+        }
+        for (auto& th : pool) th.join();
         std::fill(sum.begin(), sum.end(), 0.0);
         std::fill(cnt.begin(), cnt.end(), 0);
         for (int i = 0; i < n; ++i) {
-            int lo = nearest_sorted(c.data(), Kr, vals[i]);
-            sum[lo] += vals[i];
-            cnt[lo]++;
+            sum[lab[i]] += vals[i];
+            cnt[lab[i]]++;
         }
         bool changed = false;
         for (int i = 0; i < Kr; ++i) {
-            float nc = cnt[i] == 0 ? seed_of(i) : (float)(sum[i] / cnt[i]);
+            float nc = cnt[i] == 0 ? quant[i] : (float)(sum[i] / cnt[i]);
             if (nc != c[i]) { c[i] = nc; changed = true; }
         }
         std::sort(c.begin(), c.end());

@@ -292,23 +292,23 @@ float oracle_adc(const float* lut, int M, const uint8_t* code) {
     return dist;
 }
 
-/* search.cu:216-242 — residual term, in the 32-lane order of the CUDA refine. */
+/* search.cu:216-242 — residual term, in the 32-lane order of the CUDA refine:
+ * lane l owns 16-byte chunks l, l+32, ...; inside a chunk the dims ascend. */
 float oracle_residual(const float* q_rot, int d, int Br, const float* res_c1d,
                       const uint8_t* rc) {
     int bpv = (d * Br + 7) / 8;
-    int nwords = (bpv + 3) / 4;
-    int dpw = 32 / Br, mask = (1 << Br) - 1;
+    int nchunks = (bpv + 15) / 16;
+    int dpc = 128 / Br, mask = (1 << Br) - 1;          /* dims per 16-byte chunk */
     float p[32];
     for (int l = 0; l < 32; ++l) {
         float acc = 0.0f;
-        for (int w = l; w < nwords; w += 32) {
-            uint32_t word = 0;
-            for (int b = 0; b < 4; ++b)
-                if (4 * w + b < bpv) word |= (uint32_t)rc[4 * w + b] << (8 * b);
-            for (int t = 0; t < dpw; ++t) {
-                int j = w * dpw + t;
+        for (int c = l; c < nchunks; c += 32) {
+            for (int t = 0; t < dpc; ++t) {
+                int j = c * dpc + t;
                 if (j >= d) break;
-                float diff = q_rot[j] - res_c1d[(word >> (t * Br)) & mask];
+                int byte = (t * Br) / 8, shift = (t * Br) % 8;
+                int ri = (rc[16 * c + byte] >> shift) & mask;
+                float diff = q_rot[j] - res_c1d[ri];
                 acc = fmaf(diff, diff, acc);
             }
         }

@@ -19,9 +19,10 @@
  *    (q_k - c1d[j_k])^2 over the dims whose bits sit in the low/high nibble of b
  *    (when bits_per_dim divides 4), otherwise one fma-chain over all Ds dims.
  *  - primary   dist = sequential float sum over m = 0..M-1 of LUT[m][code_m].
- *  - residual  32 "lanes": lane l owns 32-bit words w = l, l+32, ...; within a
- *    word, dims in ascending order; lane partial = fma-chain of (q_j - r_hat)^2;
- *    then butterfly reduction p[l] += p[l ^ o] for o = 16, 8, 4, 2, 1.
+ *  - residual  32 "lanes": lane l owns 16-byte chunks c = l, l+32, ... of the
+ *    residual code; within a chunk, dims in ascending order; lane partial =
+ *    fma-chain of (q_j - r_hat)^2; then butterfly reduction p[l] += p[l ^ o]
+ *    for o = 16, 8, 4, 2, 1.
  *  - composite comp = (primary + residual) + corr    (search.cu:240)
  *  - coarse    s_c = |c|^2 - 2 * (fma-chain dot(q_rot, c))  (search.cu:32)
  *  - ordering  top-nprobe by (s, list id); top-ck by (primary, id);
