@@ -8,7 +8,7 @@
 // (oracle/jhq_oracle.c: oracle_rotate / dot_chain). Two tilings:
 //  - gemm_tiled_kernel : 128x128 CTA tile, 8x8 outputs per thread, for tall
 //                        operands (add-time rotation, k-means assignment);
-//  - gemm_skinny_kernel: 4 rows x 128 columns per CTA, both operands staged
+//  - gemm_skinny_kernel: 2 rows x 64 columns per CTA, both operands staged
 //                        through shared memory by double-buffered cp.async —
 //                        for query batches, where a 128-row tile would leave
 //                        most SMs idle.
@@ -114,7 +114,7 @@ gemm_tiled_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
 // SK_TR independent chains. Chunks of SK_KC rows of B (and the matching SK_TR x
 // SK_KC slice of A) are staged in shared memory by cp.async, double-buffered,
 // so the L2 latency of the streamed right operand overlaps the FMAs.
-constexpr int SK_TR = 4, SK_BN = 128, SK_KC = 32;
+constexpr int SK_TR = 2, SK_BN = 64, SK_KC = 32;
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);

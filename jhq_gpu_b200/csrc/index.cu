@@ -51,7 +51,7 @@ Index::Index(int d, const Params& p) : p_(p) {
     Mp_ = (int)ceil_div(M_, 16) * 16;
     p_.nprobe = std::min(p.nprobe, p.nlist);
     if (d > 16384) fail(JHQ_EINVAL, "d must be <= 16384");
-    if (scan_smem_bytes(Mp_, d_, MAX_CK_PAD) > 227 * 1024)
+    if (scan_smem_bytes(Mp_, d_, 32, scan_uses_nibbles(d_, M_, B_)) > 227 * 1024)
         fail(JHQ_EINVAL, "M too large: the per-query byte LUT (M x 1 KB) must fit in shared memory");
     if (p.device < 0) JHQ_CUDA(cudaGetDevice(&dev_));
     else dev_ = p.device;
@@ -341,6 +341,9 @@ void Index::check_search_args(int64_t nq, int k) const {
     if (!trained_ || ntotal_ == 0) fail(JHQ_ESTATE, "index is empty");
     int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
     if (next_pow2(ck) > MAX_CK_PAD) fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) must be <= 256");
+    if (scan_smem_bytes(Mp_, d_, std::max(32, next_pow2(ck)), scan_uses_nibbles(d_, M_, B_)) > 227 * 1024)
+        fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) too large for this M: the LUT and the top-ck "
+                         "lists must fit in shared memory together");
 }
 
 void Index::prepare_workspace(int k) {
@@ -351,7 +354,7 @@ void Index::prepare_workspace(int k) {
     destroy_graph();
     scan_configure();
     refine_configure();
-    const int grid = scan_grid_for(Mp_, d_, ck_pad);
+    const int grid = scan_grid_for(Mp_, d_, ck_pad, scan_uses_nibbles(d_, M_, B_));
     ws_.q.ensure((size_t)Bq * d_);
     ws_.q_rot.ensure((size_t)Bq * d_);
     if (p_.nlist > 1) ws_.scores.ensure((size_t)Bq * p_.nlist);

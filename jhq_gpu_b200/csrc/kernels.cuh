@@ -58,8 +58,9 @@ struct ScanArgs {
     uint64_t* cand;                // [(grid + nq) * ck] output candidate keys
     int nq, d, M, Mp, B, nprobe, ck, ck_pad, grid;
 };
-size_t scan_smem_bytes(int Mp, int d, int ck_pad);   // dynamic shared memory per CTA
-int scan_grid_for(int Mp, int d, int ck_pad);        // persistent CTAs: SMs x resident CTAs
+bool scan_uses_nibbles(int d, int M, int B);        // nibble tables instead of the byte LUT
+size_t scan_smem_bytes(int Mp, int d, int ck_pad, bool nib);  // dynamic shared memory per CTA
+int scan_grid_for(int Mp, int d, int ck_pad, bool nib);       // persistent CTAs: SMs x resident CTAs
 void scan_topck(const ScanArgs& a, cudaStream_t st);
 void scan_configure();                               // opt-in shared memory, current device
 

@@ -28,14 +28,16 @@ refine_kernel(RefineArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     uint64_t* top = reinterpret_cast<uint64_t*>(smem);            // 2 * ck_pad
     uint64_t* comp = top + 2 * a.ck_pad;                           // ck_pad
-    float* qs = reinterpret_cast<float*>(comp + a.ck_pad);         // d
-    float* rc1d = qs + a.d;                                        // 256
+    // q_rot padded by one float per 32: lane l reads dims 32l.. of its chunk,
+    // and the padding puts the 32 lanes in 32 different banks.
+    float* qs = reinterpret_cast<float*>(comp + a.ck_pad);         // d + d/32 + 1
+    float* rc1d = qs + a.d + a.d / 32 + 1;                         // 256
 
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (q >= a.nq) return;
     const int Kr = 1 << a.Br;
     for (int i = tid; i < a.ck_pad; i += RF_THREADS) top[i] = KEY_EMPTY;
-    for (int i = tid; i < a.d; i += RF_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
+    for (int i = tid; i < a.d; i += RF_THREADS) qs[i + (i >> 5)] = a.q_rot[(int64_t)q * a.d + i];
     for (int i = tid; i < Kr; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
     __syncthreads();
 
@@ -79,7 +81,7 @@ refine_kernel(RefineArgs a) {
                 for (int t = 0; t < dpw; ++t) {
                     const int j = (c * 4 + w) * dpw + t;
                     if (j >= a.d) break;
-                    const float diff = qs[j] - rc1d[(wv[w] >> (t * a.Br)) & mask];
+                    const float diff = qs[j + (j >> 5)] - rc1d[(wv[w] >> (t * a.Br)) & mask];
                     acc = __fmaf_rn(diff, diff, acc);
                 }
             }
@@ -132,7 +134,7 @@ merge_shards_kernel(const float* __restrict__ in_d, const int32_t* __restrict__ 
 
 void refine_topk(const RefineArgs& a, cudaStream_t st) {
     if (a.nq <= 0) return;
-    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + 256) * 4;
+    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + 256) * 4;
     refine_kernel<<<a.nq, RF_THREADS, smem, st>>>(a);
     JHQ_LAUNCH_CHECK();
     count_launch();

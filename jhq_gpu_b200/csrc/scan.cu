@@ -14,9 +14,17 @@
 // (query-major, probe order inside a query, qpage_off = its offsets). A
 // persistent grid of `grid` CTAs splits it evenly: CTA c owns pages
 // [c*T/grid, (c+1)*T/grid). For every query segment it touches, the CTA
-//   1. builds that query's byte LUT in shared memory (LUT[m][b] = lo[m][b&15]
-//      + hi[m][b>>4], lo/hi = in-order fma chains of (q - c1d)^2 over the dims
-//      of each nibble — the order fixed in oracle/jhq_oracle.c);
+//   1. builds that query's lookup tables in shared memory. When the bits of a
+//      dimension never straddle a nibble (bits_per_dim in {1, 2, 4}, i.e. every
+//      BASELINE config), the byte LUT entry LUT[m][b] is lo[m][b&15] +
+//      hi[m][b>>4], with lo/hi in-order fma chains of (q - c1d)^2 over the dims
+//      of each nibble — the order fixed in oracle/jhq_oracle.c — and only the two
+//      16-entry tables are stored (32 floats per subspace). A 16-entry table
+//      spans 16 distinct banks, so a warp's lookups are conflict-free whatever
+//      the codes: two conflict-free loads per code byte instead of a random
+//      256-way gather (~3.5 bank-conflict wavefronts per warp load). The
+//      entry is formed as lo + hi before it is added, so the sum is bit-identical
+//      to the byte-LUT sum. Other bit widths keep the full byte LUT;
 //   2. lets each warp scan pages two at a time: lane = slot, distance = sum
 //      over m in order of LUT[m][code_m] (search.cu:146-151 order);
 //   3. keeps a per-warp exact top-ck of packed (distance, id) keys: lanes whose
@@ -32,6 +40,8 @@
 #include "jhq_common.h"
 #include "kernels.cuh"
 
+#include <type_traits>
+
 namespace jhq {
 namespace {
 
@@ -39,7 +49,7 @@ constexpr int SCAN_THREADS = 512;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 
 struct ScanSmem {
-    size_t lut, nib, qs, c1d, wl, mrg, total;
+    size_t tab, qs, c1d, wl, mrg, total;
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -50,11 +60,12 @@ __host__ __device__ inline int merge_n_of(int ck_pad) {
     return n;
 }
 
-__host__ __device__ inline ScanSmem scan_smem_layout(int Mp, int d, int ck_pad) {
+// The lookup table sits at offset 0 of dynamic shared memory, so its address
+// is a link-time constant and the lookups need no base register.
+__host__ __device__ inline ScanSmem scan_smem_layout(int Mp, int d, int ck_pad, bool nib) {
     ScanSmem s;
     size_t off = 0;
-    s.lut = off; off = align16(off + (size_t)Mp * 256 * 4);
-    s.nib = off; off = align16(off + (size_t)Mp * 32 * 4);
+    s.tab = off; off = align16(off + (size_t)Mp * (nib ? 32 : 256) * 4);
     s.qs = off;  off = align16(off + (size_t)d * 4);
     s.c1d = off; off = align16(off + 256 * 4);
     s.wl = off;  off = align16(off + (size_t)SCAN_WARPS * merge_n_of(ck_pad) * 8);
@@ -63,17 +74,18 @@ __host__ __device__ inline ScanSmem scan_smem_layout(int Mp, int d, int ck_pad) 
     return s;
 }
 
-__device__ __forceinline__ uint32_t byte_of(const uint4& v, int b) {
-    uint32_t w = (b < 4) ? v.x : (b < 8) ? v.y : (b < 12) ? v.z : v.w;
-    return (w >> ((b & 3) * 8)) & 0xffu;
+__host__ __device__ inline bool nibble_split(int d, int M, int B) {
+    const int bpd = B / (d / M);
+    return bpd <= 4 && (4 % bpd) == 0;
 }
 
-// Build the byte LUT of query q_rot (already in shared qs) into lut[Mp][256].
-__device__ void build_lut(float* lut, float* nib, const float* qs, const float* c1d,
-                          int d, int M, int Mp, int B) {
+// Tables of query q_rot (already in shared qs): nibble tables tab[Mp][32]
+// (lo at 0..15, hi at 16..31) when NIB, else the byte LUT tab[Mp][256].
+template <bool NIB>
+__device__ void build_tables(float* tab, const float* qs, const float* c1d, int d, int M, int Mp,
+                             int B) {
     const int Ds = d / M, bpd = B / Ds, kmask = (1 << bpd) - 1;
-    const bool split = (bpd <= 4) && (4 % bpd == 0);
-    if (split) {
+    if (NIB) {
         const int kpn = 4 / bpd;                      // dims per nibble
         for (int i = threadIdx.x; i < Mp * 32; i += blockDim.x) {
             const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
@@ -86,12 +98,7 @@ __device__ void build_lut(float* lut, float* nib, const float* qs, const float* 
                     acc = __fmaf_rn(diff, diff, acc);
                 }
             }
-            nib[i] = acc;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < Mp * 256; i += blockDim.x) {
-            const int m = i >> 8, b = i & 255;
-            lut[i] = (m < M) ? __fadd_rn(nib[m * 32 + (b & 15)], nib[m * 32 + 16 + (b >> 4)]) : 0.0f;
+            tab[i] = acc;
         }
     } else {
         for (int i = threadIdx.x; i < Mp * 256; i += blockDim.x) {
@@ -102,10 +109,29 @@ __device__ void build_lut(float* lut, float* nib, const float* qs, const float* 
                     const float diff = qs[m * Ds + k] - c1d[(b >> (k * bpd)) & kmask];
                     acc = __fmaf_rn(diff, diff, acc);
                 }
-            lut[i] = acc;
+            tab[i] = acc;
         }
     }
     __syncthreads();
+}
+
+// Adds the 16 subspaces of one code group (16 bytes) to dist, in m order.
+template <bool NIB>
+__device__ __forceinline__ float add_group(float dist, const float* tg, const uint4& v) {
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+        const uint32_t w = (b < 4) ? v.x : (b < 8) ? v.y : (b < 12) ? v.z : v.w;
+        const int sh = (b & 3) * 8;
+        float e;
+        if (NIB) {
+            const float* nm = tg + b * 32;
+            e = __fadd_rn(nm[(w >> sh) & 15u], nm[16 + ((w >> (sh + 4)) & 15u)]);
+        } else {
+            e = tg[b * 256 + ((w >> sh) & 255u)];
+        }
+        dist = __fadd_rn(dist, e);
+    }
+    return dist;
 }
 
 // Per-warp exact top-ck state: s[0..ck_pad) sorted list, s[ck_pad..merge_n) buffer.
@@ -145,18 +171,17 @@ struct WarpTop {
     }
 };
 
-// Small LUTs (Mp <= 32) leave room for two CTAs per SM: cap registers at 64.
-template <int G_T>
-__global__ void __launch_bounds__(SCAN_THREADS, (G_T > 0 && G_T <= 2) ? 2 : 1)
+template <int G_T, bool NIB>
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
 scan_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
-    const ScanSmem L = scan_smem_layout(a.Mp, a.d, a.ck_pad);
-    float* lut = reinterpret_cast<float*>(smem + L.lut);
-    float* nib = reinterpret_cast<float*>(smem + L.nib);
+    const ScanSmem L = scan_smem_layout(a.Mp, a.d, a.ck_pad, NIB);
+    float* tab = reinterpret_cast<float*>(smem);                 // offset 0
     float* qs = reinterpret_cast<float*>(smem + L.qs);
     float* c1d = reinterpret_cast<float*>(smem + L.c1d);
     uint64_t* wl = reinterpret_cast<uint64_t*>(smem + L.wl);
     uint64_t* mrg = reinterpret_cast<uint64_t*>(smem + L.mrg);
+    constexpr int TSTRIDE = NIB ? 32 : 256;                       // floats per subspace
 
     const int G = G_T > 0 ? G_T : a.Mp / 16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -185,11 +210,11 @@ scan_kernel(ScanArgs a) {
     while (pos < end) {
         const int64_t qbase = a.qpage_off[q];
         const int64_t seg_end = min(end, a.qpage_off[q + 1]);
-        // ---- LUT of query q
+        // ---- tables of query q
         __syncthreads();
         for (int i = tid; i < a.d; i += SCAN_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
         __syncthreads();
-        build_lut(lut, nib, qs, c1d, a.d, a.M, a.Mp, a.B);
+        build_tables<NIB>(tab, qs, c1d, a.d, a.M, a.Mp, a.B);
         top.reset(lane);
 
         // ---- scan: warp w takes page pairs (lp, lp+1), lp = first + 2*(w + W*i)
@@ -210,48 +235,28 @@ scan_kernel(ScanArgs a) {
                     phys[u] = a.list_page_off[pr[p]] + (l - ppo[p]);
                 }
             }
-            float dist[2] = {0.0f, 0.0f};
+            const int32_t id0 = __ldg(a.slot_ids + phys[0] * 32 + lane);
+            const int32_t id1 = valid[1] ? __ldg(a.slot_ids + phys[1] * 32 + lane) : -1;
+            float d0 = 0.0f, d1 = 0.0f;
             const uint4* pg0 = reinterpret_cast<const uint4*>(a.pages) + phys[0] * G * 32 + lane;
             const uint4* pg1 = reinterpret_cast<const uint4*>(a.pages) + phys[1] * G * 32 + lane;
-            if (G_T > 0) {
-                // all code groups of both pages in flight before the first lookup
-                constexpr int GG = G_T > 0 ? G_T : 1;
-                uint4 v0[GG], v1[GG];
-#pragma unroll
-                for (int g = 0; g < GG; ++g) v0[g] = __ldg(pg0 + g * 32);
-                if (valid[1]) {
-#pragma unroll
-                    for (int g = 0; g < GG; ++g) v1[g] = __ldg(pg1 + g * 32);
-                } else {
-#pragma unroll
-                    for (int g = 0; g < GG; ++g) v1[g] = make_uint4(0, 0, 0, 0);
+            // group g+1 of both pages is in flight while group g is looked up
+            uint4 c0 = __ldg(pg0), c1 = valid[1] ? __ldg(pg1) : make_uint4(0, 0, 0, 0);
+#pragma unroll (G_T > 0 ? G_T : 1)
+            for (int g = 0; g < G; ++g) {
+                uint4 n0 = c0, n1 = c1;
+                if (g + 1 < G) {
+                    n0 = __ldg(pg0 + (g + 1) * 32);
+                    if (valid[1]) n1 = __ldg(pg1 + (g + 1) * 32);
                 }
-#pragma unroll
-                for (int g = 0; g < GG; ++g) {
-                    const float* lg = lut + g * 16 * 256;
-#pragma unroll
-                    for (int b = 0; b < 16; ++b) {
-                        dist[0] = __fadd_rn(dist[0], lg[b * 256 + byte_of(v0[g], b)]);
-                        dist[1] = __fadd_rn(dist[1], lg[b * 256 + byte_of(v1[g], b)]);
-                    }
-                }
-            } else {
-                for (int g = 0; g < G; ++g) {
-                    const uint4 v0 = __ldg(pg0 + g * 32);
-                    const uint4 v1 = valid[1] ? __ldg(pg1 + g * 32) : make_uint4(0, 0, 0, 0);
-                    const float* lg = lut + g * 16 * 256;
-#pragma unroll
-                    for (int b = 0; b < 16; ++b) {
-                        dist[0] = __fadd_rn(dist[0], lg[b * 256 + byte_of(v0, b)]);
-                        dist[1] = __fadd_rn(dist[1], lg[b * 256 + byte_of(v1, b)]);
-                    }
-                }
+                const float* tg = tab + g * 16 * TSTRIDE;
+                d0 = add_group<NIB>(d0, tg, c0);
+                d1 = add_group<NIB>(d1, tg, c1);
+                c0 = n0;
+                c1 = n1;
             }
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                int32_t id = valid[u] ? __ldg(a.slot_ids + phys[u] * 32 + lane) : -1;
-                top.push(id >= 0 ? make_key(dist[u], id) : KEY_EMPTY, lane);
-            }
+            top.push(id0 >= 0 ? make_key(d0, id0) : KEY_EMPTY, lane);
+            top.push(id1 >= 0 ? make_key(d1, id1) : KEY_EMPTY, lane);
         }
         top.flush(lane);
         __syncwarp();
@@ -269,62 +274,73 @@ scan_kernel(ScanArgs a) {
     }
 }
 
-template <int G_T>
+template <int G_T, bool NIB>
 void launch_scan(const ScanArgs& a, size_t smem, cudaStream_t st) {
-    scan_kernel<G_T><<<a.grid, SCAN_THREADS, smem, st>>>(a);
+    scan_kernel<G_T, NIB><<<a.grid, SCAN_THREADS, smem, st>>>(a);
 }
 
-template <int G_T>
+template <int G_T, bool NIB>
 void configure_one() {
-    JHQ_CUDA(cudaFuncSetAttribute(scan_kernel<G_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  227 * 1024));
+    JHQ_CUDA(cudaFuncSetAttribute(scan_kernel<G_T, NIB>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+}
+
+template <int G_T, bool NIB>
+int blocks_per_sm(size_t smem) {
+    int n = 0;
+    JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_kernel<G_T, NIB>, SCAN_THREADS,
+                                                           smem));
+    return n;
+}
+
+// Dispatch on (Mp/16, nibble) to the compile-time instantiations.
+template <class F>
+auto dispatch(int Mp, bool nib, F&& f) {
+    switch (Mp / 16) {
+        case 1: return nib ? f(std::integral_constant<int, 1>{}, std::true_type{})
+                           : f(std::integral_constant<int, 1>{}, std::false_type{});
+        case 2: return nib ? f(std::integral_constant<int, 2>{}, std::true_type{})
+                           : f(std::integral_constant<int, 2>{}, std::false_type{});
+        case 4: return nib ? f(std::integral_constant<int, 4>{}, std::true_type{})
+                           : f(std::integral_constant<int, 4>{}, std::false_type{});
+        case 6: return nib ? f(std::integral_constant<int, 6>{}, std::true_type{})
+                           : f(std::integral_constant<int, 6>{}, std::false_type{});
+        case 8: return nib ? f(std::integral_constant<int, 8>{}, std::true_type{})
+                           : f(std::integral_constant<int, 8>{}, std::false_type{});
+        default: return nib ? f(std::integral_constant<int, 0>{}, std::true_type{})
+                            : f(std::integral_constant<int, 0>{}, std::false_type{});
+    }
 }
 
 }  // namespace
 
 void scan_configure() {
-    configure_one<0>(); configure_one<1>(); configure_one<2>();
-    configure_one<4>(); configure_one<6>(); configure_one<8>();
+    for (int g : {1, 2, 4, 6, 8, 0})
+        for (bool nib : {true, false})
+            dispatch(g * 16, nib, [](auto G, auto N) { configure_one<G.value, N.value>(); return 0; });
 }
 
-size_t scan_smem_bytes(int Mp, int d, int ck_pad) { return scan_smem_layout(Mp, d, ck_pad).total; }
-
-template <int G_T>
-int blocks_per_sm(size_t smem) {
-    int n = 0;
-    JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_kernel<G_T>, SCAN_THREADS, smem));
-    return n;
+size_t scan_smem_bytes(int Mp, int d, int ck_pad, bool nib) {
+    return scan_smem_layout(Mp, d, ck_pad, nib).total;
 }
 
-int scan_grid_for(int Mp, int d, int ck_pad) {
+bool scan_uses_nibbles(int d, int M, int B) { return nibble_split(d, M, B); }
+
+int scan_grid_for(int Mp, int d, int ck_pad, bool nib) {
     int dev = 0, sms = 0;
     JHQ_CUDA(cudaGetDevice(&dev));
     JHQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const size_t smem = scan_smem_layout(Mp, d, ck_pad).total;
-    int per_sm = 0;
-    switch (Mp / 16) {
-        case 1: per_sm = blocks_per_sm<1>(smem); break;
-        case 2: per_sm = blocks_per_sm<2>(smem); break;
-        case 4: per_sm = blocks_per_sm<4>(smem); break;
-        case 6: per_sm = blocks_per_sm<6>(smem); break;
-        case 8: per_sm = blocks_per_sm<8>(smem); break;
-        default: per_sm = blocks_per_sm<0>(smem); break;
-    }
+    const size_t smem = scan_smem_layout(Mp, d, ck_pad, nib).total;
+    const int per_sm = dispatch(Mp, nib, [&](auto G, auto N) { return blocks_per_sm<G.value, N.value>(smem); });
     if (per_sm < 1) fail(JHQ_EINVAL, "scan: kernel does not fit on an SM (reduce M or d)");
     return sms * per_sm;
 }
 
 void scan_topck(const ScanArgs& a, cudaStream_t st) {
-    const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad).total;
+    const bool nib = nibble_split(a.d, a.M, a.B);
+    const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad, nib).total;
     if (smem > 227 * 1024) fail(JHQ_EINVAL, "scan: shared-memory LUT too large (reduce M)");
-    switch (a.Mp / 16) {
-        case 1: launch_scan<1>(a, smem, st); break;
-        case 2: launch_scan<2>(a, smem, st); break;
-        case 4: launch_scan<4>(a, smem, st); break;
-        case 6: launch_scan<6>(a, smem, st); break;
-        case 8: launch_scan<8>(a, smem, st); break;
-        default: launch_scan<0>(a, smem, st); break;
-    }
+    dispatch(a.Mp, nib, [&](auto G, auto N) { launch_scan<G.value, N.value>(a, smem, st); return 0; });
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

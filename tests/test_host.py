@@ -56,7 +56,8 @@ def test_training_primitives_bit_exact(jhq, golden):
     (128, dict(M=32, batch_size=0), "batch_size"),
     (128, dict(M=32, add_batch=0), "add_batch"),
     (128, dict(M=32, alpha=0.0), "alpha"),
-    (1024, dict(M=512, B=8), "M too large"),
+    (4096, dict(M=2048, B=8), "M too large"),
+    (1024, dict(M=1024, B=8), "M too large"),
 ])
 def test_param_validation_like_reference(jhq, d, kw, msg):
     """JHQGpuIndex ctor throws std::invalid_argument (jhq_gpu_index.cu:110-121)."""
@@ -76,3 +77,15 @@ def test_null_and_error_paths(jhq):
     assert L.jhq_search(None, None, 0, 10, None, None) == jhq.JHQ_EINVAL
     assert b"null index" in L.jhq_last_error()
     assert L.jhq_load(b"/nonexistent/file.jhq", -1, None) == jhq.JHQ_EINVAL
+
+
+@pytest.mark.parametrize("d,M,nlist", [(128, 32, 1), (1024, 128, 1), (1024, 128, 1024),
+                                       (128, 32, 65536), (104, 26, 65536), (768, 96, 1024)])
+def test_benchmark_shapes_pass_validation(jhq, d, M, nlist):
+    """BASELINE configs pass parameter validation (on a GPU-less host the
+    constructor then fails at device selection with JHQ_EDEVICE, not EINVAL)."""
+    try:
+        idx = jhq.JHQGpuIndex(d, jhq.Params(M=M, nlist=nlist, nprobe=min(64, nlist)))
+        idx.close()
+    except jhq.JHQError as e:
+        assert e.code == jhq.JHQ_EDEVICE
