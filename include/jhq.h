@@ -80,6 +80,19 @@ int jhq_search(jhq_index* idx, const float* q, int64_t nq, int k,
 int jhq_search_device(jhq_index* idx, const float* d_q, int64_t nq, int k,
                       float* d_dists, int32_t* d_ids, void* stream);
 
+/* Same as jhq_search_device, but allocates nothing: every temporary of a
+ * batch (rotated queries, coarse scores, probe lists, candidate lists) lives in
+ * one fixed 16 MiB device array built into the library, which each GPU that
+ * loads the library keeps until exit. For callers that may not allocate device
+ * memory while serving (a host that owns a fixed pool, real-time paths, a
+ * framework that reserved the whole GPU). No counterpart in the reference.
+ * The first call on a device looks up that array (cudaGetSymbolAddress); make
+ * it before any stream capture. A batch needing more than 16 MiB of
+ * temporaries returns JHQ_EINVAL. All calls on a device share the array, so
+ * calls that overlap on the GPU race: serialise them. */
+int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int k,
+                              float* d_dists, int32_t* d_ids, void* stream);
+
 /* Waits for the index's stream with a deadline (replaces the unbounded
  * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
 int jhq_synchronize(jhq_index* idx, double timeout_s);

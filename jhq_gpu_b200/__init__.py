@@ -35,6 +35,7 @@ EXPORTED = [
     "jhq_encode", "jhq_save", "jhq_load", "jhq_merge_shards", "jhq_kernel_launches",
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
+    "jhq_search_device_noalloc",
 ]
 STAGES = ["rotate", "coarse+probes", "partition", "scan", "refine"]
 
@@ -92,6 +93,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     L.jhq_add.argtypes = [vp, f32p, i64]
     L.jhq_search.argtypes = [vp, f32p, i64, C.c_int, f32p, i32p]
     L.jhq_search_device.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
+    L.jhq_search_device_noalloc.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_synchronize.argtypes = [vp, C.c_double]
     L.jhq_ntotal.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_dim.argtypes = [vp, C.POINTER(C.c_int)]
@@ -233,6 +235,13 @@ class JHQGpuIndex:
                       stream: int = 0) -> None:
         """Device-buffer search (raw CUDA pointers, e.g. torch tensor.data_ptr())."""
         _check(self._L.jhq_search_device(self._h, q_ptr, nq, k, d_ptr, i_ptr, stream))
+
+    def search_device_noalloc(self, q_ptr: int, nq: int, k: int, d_ptr: int, i_ptr: int,
+                              stream: int = 0) -> None:
+        """Device-buffer search that allocates no device memory: its temporaries sit
+        in a fixed 16 MiB array inside the library (for callers that must not
+        allocate while serving). Calls that overlap on the GPU race; serialise them."""
+        _check(self._L.jhq_search_device_noalloc(self._h, q_ptr, nq, k, d_ptr, i_ptr, stream))
 
     def synchronize(self, timeout_s: float = 60.0) -> None:
         _check(self._L.jhq_synchronize(self._h, timeout_s))

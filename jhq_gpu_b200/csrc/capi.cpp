@@ -107,6 +107,14 @@ int jhq_search_device(jhq_index* idx, const float* d_q, int64_t nq, int k, float
     });
 }
 
+int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int k,
+                              float* d_dists, int32_t* d_ids, void* stream) {
+    return guarded([&] {
+        need(idx)->search_device_noalloc(d_q, nq, k, d_dists, d_ids,
+                                         static_cast<cudaStream_t>(stream));
+    });
+}
+
 int jhq_synchronize(jhq_index* idx, double timeout_s) {
     return guarded([&] { need(idx)->synchronize(timeout_s); });
 }

@@ -44,6 +44,10 @@ public:
     void search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t* h_ids);
     void search_device(const float* d_q, int64_t nq, int k, float* d_dists, int32_t* d_ids,
                        cudaStream_t stream);
+    // Same search as search_device, but every temporary lives in a fixed
+    // device array compiled into the library (noalloc.cu); nothing is allocated.
+    void search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_dists,
+                               int32_t* d_ids, cudaStream_t stream);
     void synchronize(double timeout_s);
 
     int64_t ntotal() const { return ntotal_; }
