@@ -146,7 +146,7 @@ int jhq_merge_shards(const float* d_in_dists, const int32_t* d_in_ids,
  * events, jhq_v13_step_timing/search.cu:456-491) -------------------------
  * With profiling on, search runs each batch as direct launches (no CUDA
  * graph) with CUDA events between the stages and accumulates per-stage device
- * time. Stages: 0 rotate, 1 coarse scores + probe selection, 2 scan partition,
+ * time. Stages: 0 rotate, 1 coarse scores + probe selection, 2 scan plan,
  * 3 LUT + ADC scan + top-ck, 4 refine + final top-k. jhq_set_profiling resets
  * the totals; jhq_stage_times copies min(n, 5) totals (ms) and batch counts. */
 #define JHQ_NUM_STAGES 5

@@ -37,7 +37,7 @@ EXPORTED = [
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc",
 ]
-STAGES = ["rotate", "coarse+probes", "partition", "scan", "refine"]
+STAGES = ["rotate", "coarse+probes", "plan", "scan", "refine"]
 
 
 class JHQError(RuntimeError):

@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <thread>
 
 #include "kernels.cuh"
@@ -51,7 +52,7 @@ Index::Index(int d, const Params& p) : p_(p) {
     Mp_ = (int)ceil_div(M_, 16) * 16;
     p_.nprobe = std::min(p.nprobe, p.nlist);
     if (d > 16384) fail(JHQ_EINVAL, "d must be <= 16384");
-    if (scan_smem_bytes(Mp_, d_, 32, scan_uses_nibbles(d_, M_, B_)) > 227 * 1024)
+    if (scan_smem_bytes(Mp_, d_, 32, scan_mode_for(d_, M_, B_, 1.0)) > 227 * 1024)
         fail(JHQ_EINVAL, "M too large: the per-query byte LUT (M x 1 KB) must fit in shared memory");
     if (p.device < 0) JHQ_CUDA(cudaGetDevice(&dev_));
     else dev_ = p.device;
@@ -74,8 +75,9 @@ Index::~Index() {
     dpcodes_.release(); drcodes_.release(); dpages_.release(); dcorr_.release();
     dassign_.release(); dslot_ids_.release(); dlist_page_off_.release();
     ws_.q.release(); ws_.q_rot.release(); ws_.scores.release(); ws_.out_d.release();
-    ws_.probes.release(); ws_.ppo.release(); ws_.out_i.release(); ws_.qpage_off.release();
-    ws_.cand.release(); ws_.nvalid.release();
+    ws_.probes.release(); ws_.out_i.release(); ws_.cnt.release(); ws_.bucket_off.release();
+    ws_.unit_off.release(); ws_.fill.release(); ws_.cpo.release(); ws_.bucket.release();
+    ws_.qslot_off.release(); ws_.cand.release(); ws_.gthr.release(); ws_.nvalid.release();
     ws_.h_q.release(); ws_.h_d.release(); ws_.h_i.release(); ws_.h_nvalid.release();
     cudaSetDevice(prev);
 }
@@ -322,6 +324,9 @@ void Index::rebuild_layout() {
     for (int c = 0; c < nl; ++c) cur[c] = (int64_t)lpo[c] * 32;
     for (int64_t i = 0; i < ntotal_; ++i) slots[(size_t)cur[h_assign_[(size_t)i]]++] = (int32_t)i;
     npages_ = pages;
+    h_list_pages_sorted_.resize(nl);
+    for (int c = 0; c < nl; ++c) h_list_pages_sorted_[c] = lpo[c + 1] - lpo[c];
+    std::sort(h_list_pages_sorted_.begin(), h_list_pages_sorted_.end(), std::greater<int32_t>());
     dlist_page_off_.resize(nl + 1);
     dslot_ids_.resize(std::max<size_t>(1, slots.size()));
     dpages_.resize(std::max<size_t>(16, (size_t)pages * Mp_ * 32));
@@ -341,40 +346,73 @@ void Index::check_search_args(int64_t nq, int k) const {
     if (!trained_ || ntotal_ == 0) fail(JHQ_ESTATE, "index is empty");
     int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
     if (next_pow2(ck) > MAX_CK_PAD) fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) must be <= 256");
-    if (scan_smem_bytes(Mp_, d_, std::max(32, next_pow2(ck)), scan_uses_nibbles(d_, M_, B_)) > 227 * 1024)
+    if (scan_smem_bytes(Mp_, d_, std::max(32, next_pow2(ck)), scan_mode_for(d_, M_, B_, 1.0)) > 227 * 1024)
         fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) too large for this M: the LUT and the top-ck "
                          "lists must fit in shared memory together");
 }
 
+Index::BatchShape Index::batch_shape(int Bq, int k) const {
+    BatchShape sh;
+    sh.Bq = Bq;
+    sh.k = k;
+    sh.ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
+    sh.ck_pad = std::max(32, next_pow2(sh.ck));
+    // queries per list decide the query-group size; shrink it while the tables
+    // and top-ck lists do not fit in shared memory
+    const double qpl = (double)Bq * p_.nprobe / p_.nlist;
+    sh.mode = scan_mode_for(d_, M_, B_, qpl);
+    while (sh.mode > 1 && scan_smem_bytes(Mp_, d_, sh.ck_pad, sh.mode) > 227 * 1024) sh.mode /= 2;
+    sh.grid = scan_grid_for(Mp_, d_, sh.ck_pad, sh.mode);
+    // chunk size: about four units per CTA for the expected page visits
+    const int qg = sh.mode == 0 ? 1 : sh.mode;
+    const double avg_pages = (double)npages_ / p_.nlist;
+    const double visits = std::max(1.0, (double)Bq * p_.nprobe * avg_pages / qg);
+    sh.chunk_pages = (int)std::min(256.0, std::max(16.0, visits / (4.0 * sh.grid)));
+    // slots: per query, one per chunk of each probed list; bounded by nprobe
+    // plus the chunks of the nprobe largest lists
+    int64_t top_pages = 0;
+    for (int i = 0; i < p_.nprobe && i < (int)h_list_pages_sorted_.size(); ++i)
+        top_pages += h_list_pages_sorted_[i];
+    sh.max_slots = (int64_t)Bq * (p_.nprobe + ceil_div(top_pages, sh.chunk_pages));
+    return sh;
+}
+
 void Index::prepare_workspace(int k) {
-    const int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
-    const int ck_pad = std::max(32, next_pow2(ck));
     const int Bq = p_.batch_size;
     if (ws_.batch_cap == Bq && ws_.k == k && ws_.exec) return;
     destroy_graph();
     scan_configure();
     refine_configure();
-    const int grid = scan_grid_for(Mp_, d_, ck_pad, scan_uses_nibbles(d_, M_, B_));
+    const BatchShape sh = batch_shape(Bq, k);
+    const int nl = p_.nlist, np = p_.nprobe;
     ws_.q.ensure((size_t)Bq * d_);
     ws_.q_rot.ensure((size_t)Bq * d_);
-    if (p_.nlist > 1) ws_.scores.ensure((size_t)Bq * p_.nlist);
-    ws_.probes.ensure((size_t)Bq * p_.nprobe);
-    ws_.ppo.ensure((size_t)Bq * (p_.nprobe + 1));
-    ws_.qpage_off.ensure((size_t)Bq + 1);
-    ws_.cand.ensure((size_t)(grid + Bq) * ck);
+    if (nl > 1) ws_.scores.ensure((size_t)Bq * nl);
+    ws_.probes.ensure((size_t)Bq * np);
+    ws_.cnt.ensure((size_t)nl + 1);
+    ws_.bucket_off.ensure((size_t)nl + 1);
+    ws_.unit_off.ensure((size_t)nl + 1);
+    ws_.fill.ensure((size_t)nl);
+    ws_.bucket.ensure((size_t)Bq * np);
+    ws_.cpo.ensure((size_t)Bq * (np + 1));
+    ws_.qslot_off.ensure((size_t)Bq + 1);
+    ws_.gthr.ensure((size_t)Bq);
+    ws_.cand.ensure((size_t)sh.max_slots * sh.ck);
     ws_.out_d.ensure((size_t)Bq * k);
     ws_.out_i.ensure((size_t)Bq * k);
     ws_.nvalid.ensure(1);
     ws_.h_q.ensure((size_t)2 * Bq * d_);
     ws_.h_d.ensure((size_t)2 * Bq * k);
     ws_.h_i.ensure((size_t)2 * Bq * k);
-    if (p_.nlist == 1)
-        JHQ_CUDA(cudaMemsetAsync(ws_.probes.get(), 0, (size_t)Bq * p_.nprobe * 4, stream_));
+    if (nl == 1) JHQ_CUDA(cudaMemsetAsync(ws_.probes.get(), 0, (size_t)Bq * np * 4, stream_));
     ws_.batch_cap = Bq;
     ws_.k = k;
-    ws_.ck = ck;
-    ws_.ck_pad = ck_pad;
-    ws_.grid = grid;
+    ws_.ck = sh.ck;
+    ws_.ck_pad = sh.ck_pad;
+    ws_.grid = sh.grid;
+    ws_.mode = sh.mode;
+    ws_.chunk_pages = sh.chunk_pages;
+    ws_.max_slots = sh.max_slots;
     // capture the per-batch pipeline once (capture_graph, search.cu:315-386)
     const int64_t before = g_kernel_launches.load();
     JHQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
@@ -393,39 +431,56 @@ void Index::prepare_workspace(int k) {
     JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
-// Kernel sequence of one query batch on the workspace buffers.
-void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
+// Kernel sequence of one query batch: rotate -> coarse scores + probes ->
+// plan -> scan -> refine, with optional events between the stages.
+void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
+                             const BatchShape& sh, const BatchBufs& b, float* out_d,
+                             int32_t* out_i, cudaStream_t s, cudaEvent_t* ev) {
     auto mark = [&](int i) { if (ev) JHQ_CUDA(cudaEventRecord(ev[i], s)); };
-    const int Bq = ws_.batch_cap;
     mark(0);
-    rotate_device(ws_.q.get(), Bq, ws_.q_rot.get(), s);
+    rotate_device(q_in, nq, b.q_rot, s);
     mark(1);
     if (p_.nlist > 1) {
-        gemm_rows(ws_.q_rot.get(), dcentsT_.get(), ws_.scores.get(), Bq, d_, p_.nlist, EPI_COARSE,
-                  dnorms_.get(), s);
-        select_probes(ws_.scores.get(), Bq, p_.nlist, p_.nprobe, ws_.probes.get(), s);
+        gemm_rows(b.q_rot, dcentsT_.get(), b.scores, nq, d_, p_.nlist, EPI_COARSE, dnorms_.get(), s);
+        select_probes(b.scores, nq, p_.nlist, p_.nprobe, b.probes, s);
     }
     mark(2);
-    scan_prepare(ws_.probes.get(), Bq, p_.nprobe, dlist_page_off_.get(), ws_.nvalid.get(),
-                 ws_.ppo.get(), ws_.qpage_off.get(), s);
+    const int qg = sh.mode == 0 ? 1 : sh.mode;
+    plan_build(b.probes, nq, p_.nprobe, p_.nlist, dlist_page_off_.get(), d_nvalid, sh.chunk_pages,
+               qg, b.plan, s);
     ScanArgs sa;
-    sa.q_rot = ws_.q_rot.get(); sa.c1d = dc1d_.get(); sa.probes = ws_.probes.get();
-    sa.probe_page_off = ws_.ppo.get(); sa.qpage_off = ws_.qpage_off.get();
-    sa.list_page_off = dlist_page_off_.get(); sa.pages = dpages_.get();
-    sa.slot_ids = dslot_ids_.get(); sa.cand = ws_.cand.get();
-    sa.nq = Bq; sa.d = d_; sa.M = M_; sa.Mp = Mp_; sa.B = B_; sa.nprobe = p_.nprobe;
-    sa.ck = ws_.ck; sa.ck_pad = ws_.ck_pad; sa.grid = ws_.grid;
+    sa.q_rot = b.q_rot; sa.c1d = dc1d_.get(); sa.list_page_off = dlist_page_off_.get();
+    sa.pages = dpages_.get(); sa.slot_ids = dslot_ids_.get();
+    sa.unit_off = b.plan.unit_off; sa.bucket_off = b.plan.bucket_off; sa.bucket = b.plan.bucket;
+    sa.cpo = b.plan.cpo; sa.qslot_off = b.plan.qslot_off; sa.gthr = b.plan.gthr; sa.cand = b.cand;
+    sa.nq = nq; sa.nlist = p_.nlist; sa.d = d_; sa.M = M_; sa.Mp = Mp_; sa.B = B_;
+    sa.nprobe = p_.nprobe; sa.ck = sh.ck; sa.ck_pad = sh.ck_pad; sa.grid = sh.grid;
+    sa.chunk_pages = sh.chunk_pages; sa.mode = sh.mode;
     mark(3);
     scan_topck(sa, s);
     mark(4);
     RefineArgs ra;
-    ra.q_rot = ws_.q_rot.get(); ra.res_c1d = dres_.get(); ra.cand = ws_.cand.get();
-    ra.qpage_off = ws_.qpage_off.get(); ra.rcodes = drcodes_.get(); ra.corr = dcorr_.get();
-    ra.out_dists = ws_.out_d.get(); ra.out_ids = ws_.out_i.get();
-    ra.nq = Bq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = ws_.ck;
-    ra.ck_pad = ws_.ck_pad; ra.k = ws_.k; ra.grid = ws_.grid;
+    ra.q_rot = b.q_rot; ra.res_c1d = dres_.get(); ra.cand = b.cand;
+    ra.qslot_off = b.plan.qslot_off; ra.gthr = b.plan.gthr; ra.rcodes = drcodes_.get();
+    ra.corr = dcorr_.get(); ra.out_dists = out_d; ra.out_ids = out_i;
+    ra.nq = nq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = sh.ck;
+    ra.ck_pad = sh.ck_pad; ra.k = sh.k;
     refine_topk(ra, s);
     mark(5);
+}
+
+void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
+    BatchShape sh;
+    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.ck = ws_.ck; sh.ck_pad = ws_.ck_pad;
+    sh.grid = ws_.grid; sh.mode = ws_.mode; sh.chunk_pages = ws_.chunk_pages;
+    sh.max_slots = ws_.max_slots;
+    BatchBufs b;
+    b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
+    b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
+                      ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
+    b.cand = ws_.cand.get();
+    enqueue_pipeline(ws_.q.get(), ws_.batch_cap, ws_.nvalid.get(), sh, b, ws_.out_d.get(),
+                     ws_.out_i.get(), s, ev);
 }
 
 void Index::run_batch(cudaStream_t s, int nvalid) {

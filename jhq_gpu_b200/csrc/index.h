@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "jhq_common.h"
+#include "kernels.cuh"
 
 namespace jhq {
 
@@ -75,14 +76,17 @@ public:
 private:
     struct Workspace {                 // SearchWorkspace (search.cuh:24-46)
         int batch_cap = 0, k = 0, ck = 0, ck_pad = 0, grid = 0;
+        int mode = 0, chunk_pages = 64;
+        int64_t max_slots = 0;         // candidate slots a batch can need
         PinnedBuf<float> h_q;          // [batch][d] staged queries
         PinnedBuf<float> h_d;          // [batch][k]
         PinnedBuf<int32_t> h_i;
         PinnedBuf<int> h_nvalid;
         DevBuf<float> q, q_rot, scores, out_d;
-        DevBuf<int32_t> probes, ppo, out_i;
-        DevBuf<int64_t> qpage_off;
-        DevBuf<uint64_t> cand;
+        DevBuf<int32_t> probes, out_i, cnt, bucket_off, unit_off, fill, cpo;
+        DevBuf<int2> bucket;
+        DevBuf<int64_t> qslot_off;
+        DevBuf<uint64_t> cand, gthr;
         DevBuf<int> nvalid;
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
@@ -96,6 +100,23 @@ private:
     void rebuild_layout();
     void prepare_workspace(int k);
     void destroy_graph();
+    // Shapes of one search batch: ck, scan mode / grid / chunking, slot bound.
+    struct BatchShape {
+        int Bq, k, ck, ck_pad, grid, mode, chunk_pages;
+        int64_t max_slots;
+    };
+    // Device temporaries of one batch (workspace or fixed scratch array).
+    struct BatchBufs {
+        float* q_rot;
+        float* scores;
+        int32_t* probes;
+        PlanBufs plan;
+        uint64_t* cand;
+    };
+    BatchShape batch_shape(int Bq, int k) const;
+    void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
+                          const BatchBufs& b, float* out_d, int32_t* out_i, cudaStream_t s,
+                          cudaEvent_t* ev);
     void enqueue_batch(cudaStream_t s, cudaEvent_t* ev = nullptr);
     void run_batch(cudaStream_t s, int nvalid);
     void check_search_args(int64_t nq, int k) const;
@@ -106,6 +127,7 @@ private:
     cudaStream_t stream_ = nullptr;
     bool trained_ = false;
     int64_t ntotal_ = 0, cap_ = 0, npages_ = 0;
+    std::vector<int32_t> h_list_pages_sorted_;   // list page counts, descending
     float sigma_ = 1.0f;
     std::vector<float> Pi_, c1d_, res_c1d_, cents_;
     std::vector<int32_t> h_assign_;

@@ -9,12 +9,13 @@
 // winners — ties at the threshold resolved by ascending list id — and sorts
 // them by (score, list id), the exact order of jhq_v3_ivf/search.cu:46-85.
 //
-// scan_prepare_kernel turns the chosen lists into page counts: per query the
-// prefix sums of pages over its probes, and over queries the exclusive scan
-// qpage_off that the persistent scan kernel partitions evenly across CTAs.
+// The plan kernels invert the (query, probe) pairs into per-list buckets and
+// number the scan's work units and candidate slots (see kernels.cuh).
 #include "device_utils.cuh"
 #include "jhq_common.h"
 #include "kernels.cuh"
+
+#include <algorithm>
 
 namespace jhq {
 namespace {
@@ -99,48 +100,90 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int np_
     }
 }
 
-constexpr int PREP_THREADS = 1024;
+constexpr int PLAN_THREADS = 1024;
 
-__global__ void __launch_bounds__(PREP_THREADS)
-scan_prepare_kernel(const int32_t* __restrict__ probes, int nq, int nprobe,
-                    const int32_t* __restrict__ list_page_off, const int* __restrict__ d_nvalid,
-                    int32_t* __restrict__ probe_page_off, int64_t* __restrict__ qpage_off) {
-    __shared__ int64_t part[PREP_THREADS];
-    __shared__ int64_t carry;
+__device__ __forceinline__ int chunks_of(const int32_t* lpo, int l, int chunk_pages) {
+    return (lpo[l + 1] - lpo[l] + chunk_pages - 1) / chunk_pages;
+}
+
+// Per pair: count per list. Per query: chunk prefix over its probes, slot
+// count (into qslot_off[q+1]) and a fresh pruning bound.
+__global__ void plan_count_kernel(const int32_t* __restrict__ probes, int nq, int nprobe,
+                                  const int32_t* __restrict__ lpo, const int* __restrict__ d_nvalid,
+                                  int chunk_pages, PlanBufs b) {
     const int nvalid = d_nvalid ? *d_nvalid : nq;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < (int64_t)nq * nprobe) {
+        const int q = (int)(t / nprobe);
+        if (q < nvalid) atomicAdd(&b.cnt[probes[t]], 1);
+    }
+    if (t < nq) {
+        const int q = (int)t;
+        int32_t* po = b.cpo + (int64_t)q * (nprobe + 1);
+        int acc = 0;
+        po[0] = 0;
+        for (int p = 0; p < nprobe; ++p) {
+            if (q < nvalid) acc += chunks_of(lpo, probes[(int64_t)q * nprobe + p], chunk_pages);
+            po[p + 1] = acc;
+        }
+        b.qslot_off[q + 1] = acc;
+        b.gthr[q] = KEY_EMPTY;
+    }
+}
+
+// In-place exclusive scan of v[0..n) with one block; returns the total.
+template <class T, class F>
+__device__ T block_exclusive_scan(int n, F&& value_of, T* out) {
+    __shared__ T part[PLAN_THREADS];
+    __shared__ T carry;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
-    for (int base = 0; base < nq; base += PREP_THREADS) {
-        int q = base + threadIdx.x;
-        int64_t tot = 0;
-        if (q < nq) {
-            int32_t* po = probe_page_off + (int64_t)q * (nprobe + 1);
-            int acc = 0;
-            po[0] = 0;
-            for (int p = 0; p < nprobe; ++p) {
-                if (q < nvalid) {
-                    int l = probes[(int64_t)q * nprobe + p];
-                    acc += list_page_off[l + 1] - list_page_off[l];
-                }
-                po[p + 1] = acc;
-            }
-            tot = acc;
-        }
-        part[threadIdx.x] = tot;
+    for (int base = 0; base < n; base += PLAN_THREADS) {
+        const int i = base + threadIdx.x;
+        const T v = i < n ? value_of(i) : T(0);
+        part[threadIdx.x] = v;
         __syncthreads();
-        // inclusive Hillis-Steele scan of this chunk
-        for (int o = 1; o < PREP_THREADS; o <<= 1) {
-            int64_t v = (threadIdx.x >= o) ? part[threadIdx.x - o] : 0;
+        for (int o = 1; o < PLAN_THREADS; o <<= 1) {
+            T x = threadIdx.x >= o ? part[threadIdx.x - o] : T(0);
             __syncthreads();
-            part[threadIdx.x] += v;
+            part[threadIdx.x] += x;
             __syncthreads();
         }
-        if (q < nq) qpage_off[q + 1] = carry + part[threadIdx.x];
+        if (i < n) out[i] = carry + part[threadIdx.x] - v;
         __syncthreads();
-        if (threadIdx.x == PREP_THREADS - 1) carry += part[PREP_THREADS - 1];
+        if (threadIdx.x == PLAN_THREADS - 1) carry += part[PLAN_THREADS - 1];
         __syncthreads();
     }
-    if (threadIdx.x == 0) qpage_off[0] = 0;
+    return carry;
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS)
+plan_scan_kernel(int nq, int nlist, const int32_t* __restrict__ lpo, int chunk_pages, int qg,
+                 PlanBufs b) {
+    const int32_t nb = block_exclusive_scan<int32_t>(nlist, [&](int l) { return b.cnt[l]; },
+                                                     b.bucket_off);
+    if (threadIdx.x == 0) b.bucket_off[nlist] = nb;
+    const int32_t nu = block_exclusive_scan<int32_t>(nlist, [&](int l) {
+        const int c = b.cnt[l];
+        return c ? ((c + qg - 1) / qg) * chunks_of(lpo, l, chunk_pages) : 0;
+    }, b.unit_off);
+    if (threadIdx.x == 0) b.unit_off[nlist] = nu;
+    for (int l = threadIdx.x; l < nlist; l += PLAN_THREADS) b.fill[l] = b.bucket_off[l];
+    // qslot_off[q+1] holds the count of query q: turn it into offsets
+    const int64_t ns = block_exclusive_scan<int64_t>(nq, [&](int q) { return b.qslot_off[q + 1]; },
+                                                     b.qslot_off);
+    if (threadIdx.x == 0) b.qslot_off[nq] = ns;
+}
+
+__global__ void plan_fill_kernel(const int32_t* __restrict__ probes, int nq, int nprobe,
+                                 const int* __restrict__ d_nvalid, PlanBufs b) {
+    const int nvalid = d_nvalid ? *d_nvalid : nq;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= (int64_t)nq * nprobe) return;
+    const int q = (int)(t / nprobe), p = (int)(t % nprobe);
+    if (q >= nvalid) return;
+    const int pos = atomicAdd(&b.fill[probes[t]], 1);
+    b.bucket[pos] = make_int2(q, p);
 }
 
 }  // namespace
@@ -155,13 +198,21 @@ void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probe
     count_launch();
 }
 
-void scan_prepare(const int32_t* probes, int nq, int nprobe, const int32_t* list_page_off,
-                  const int* d_nvalid, int32_t* probe_page_off, int64_t* qpage_off,
-                  cudaStream_t st) {
-    scan_prepare_kernel<<<1, PREP_THREADS, 0, st>>>(probes, nq, nprobe, list_page_off, d_nvalid,
-                                                    probe_page_off, qpage_off);
+void plan_build(const int32_t* probes, int nq, int nprobe, int nlist,
+                const int32_t* list_page_off, const int* d_nvalid, int chunk_pages, int qg,
+                const PlanBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    JHQ_CUDA(cudaMemsetAsync(b.cnt, 0, (size_t)(nlist + 1) * sizeof(int32_t), st));
+    const int64_t pairs = std::max<int64_t>((int64_t)nq * nprobe, nq);
+    plan_count_kernel<<<(unsigned)ceil_div(pairs, 256), 256, 0, st>>>(
+        probes, nq, nprobe, list_page_off, d_nvalid, chunk_pages, b);
     JHQ_LAUNCH_CHECK();
-    count_launch();
+    plan_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(nq, nlist, list_page_off, chunk_pages, qg, b);
+    JHQ_LAUNCH_CHECK();
+    plan_fill_kernel<<<(unsigned)ceil_div((int64_t)nq * nprobe, 256), 256, 0, st>>>(
+        probes, nq, nprobe, d_nvalid, b);
+    JHQ_LAUNCH_CHECK();
+    count_launch(3);
 }
 
 }  // namespace jhq

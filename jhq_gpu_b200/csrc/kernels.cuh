@@ -39,28 +39,47 @@ void scatter_pages(const int32_t* slot_ids, int64_t nslots, const uint8_t* pcode
 // written ascending into probes [nq][nprobe].
 void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probes,
                    cudaStream_t st);
-// Page counts per (query, probe) -> qpage_off [nq+1] (exclusive scan over
-// queries) and probe_page_off [nq][nprobe+1]; queries >= *d_nvalid get 0 pages.
-void scan_prepare(const int32_t* probes, int nq, int nprobe, const int32_t* list_page_off,
-                  const int* d_nvalid, int32_t* probe_page_off, int64_t* qpage_off,
-                  cudaStream_t st);
+// ---- scan plan (ivf.cu): list-major work units over query groups ----------
+// The (query, probe) pairs of a batch are inverted into per-list buckets; the
+// queries of list l are taken QG at a time and each list is cut into chunks of
+// at most chunk_pages pages. A unit = (list, query group, chunk); units are
+// numbered list-major then group-major then chunk. Every (query, probe, chunk)
+// gets its own candidate slot: slot = qslot_off[q] + cpo[q][p] + chunk.
+struct PlanBufs {
+    int32_t* cnt;          // [nlist + 1]  pairs per list (zeroed by plan_build)
+    int32_t* bucket_off;   // [nlist + 1]
+    int32_t* unit_off;     // [nlist + 1]
+    int32_t* fill;         // [nlist]
+    int2* bucket;          // [nq * nprobe]  (query, probe index)
+    int32_t* cpo;          // [nq][nprobe + 1]  chunk prefix over a query's probes
+    int64_t* qslot_off;    // [nq + 1]
+    uint64_t* gthr;        // [nq]  global pruning bound per query
+};
+// Queries >= *d_nvalid (when given) take part in nothing.
+void plan_build(const int32_t* probes, int nq, int nprobe, int nlist,
+                const int32_t* list_page_off, const int* d_nvalid, int chunk_pages, int qg,
+                const PlanBufs& b, cudaStream_t st);
 
 // ---- LUT + ADC scan + exact top-ck (scan.cu) -------------------------------
 struct ScanArgs {
     const float* q_rot;            // [nq][d]
     const float* c1d;              // [K1D]
-    const int32_t* probes;         // [nq][nprobe]
-    const int32_t* probe_page_off; // [nq][nprobe+1]
-    const int64_t* qpage_off;      // [nq+1]
     const int32_t* list_page_off;  // [nlist+1]
     const uint8_t* pages;          // [npages][Mp/16][32][16]
     const int32_t* slot_ids;       // [npages*32]
-    uint64_t* cand;                // [(grid + nq) * ck] output candidate keys
-    int nq, d, M, Mp, B, nprobe, ck, ck_pad, grid;
+    const int32_t* unit_off;       // plan
+    const int32_t* bucket_off;
+    const int2* bucket;
+    const int32_t* cpo;
+    const int64_t* qslot_off;
+    uint64_t* gthr;                // [nq] lowered by the scan
+    uint64_t* cand;                // [slots][ck] output candidate keys
+    int nq, nlist, d, M, Mp, B, nprobe, ck, ck_pad, grid, chunk_pages, mode;
 };
-bool scan_uses_nibbles(int d, int M, int B);        // nibble tables instead of the byte LUT
-size_t scan_smem_bytes(int Mp, int d, int ck_pad, bool nib);  // dynamic shared memory per CTA
-int scan_grid_for(int Mp, int d, int ck_pad, bool nib);       // persistent CTAs: SMs x resident CTAs
+// mode 0: byte LUT, one query per unit; 1/2/4: nibble tables, 1/2/4 queries.
+int scan_mode_for(int d, int M, int B, double queries_per_list);
+size_t scan_smem_bytes(int Mp, int d, int ck_pad, int mode);  // dynamic shared memory per CTA
+int scan_grid_for(int Mp, int d, int ck_pad, int mode);       // persistent CTAs: SMs x resident
 void scan_topck(const ScanArgs& a, cudaStream_t st);
 void scan_configure();                               // opt-in shared memory, current device
 
@@ -69,12 +88,13 @@ struct RefineArgs {
     const float* q_rot;        // [nq][d]
     const float* res_c1d;      // [Kr]
     const uint64_t* cand;      // scan output
-    const int64_t* qpage_off;  // [nq+1]
+    const int64_t* qslot_off;  // [nq+1] slots of each query
+    const uint64_t* gthr;      // [nq] final pruning bound per query
     const uint8_t* rcodes;     // [N][bpv_pad] id order
     const float* corr;         // [N]
     float* out_dists;          // [nq][k]
     int32_t* out_ids;          // [nq][k]
-    int nq, d, Br, bpv_pad, ck, ck_pad, k, grid;
+    int nq, d, Br, bpv_pad, ck, ck_pad, k;
 };
 void refine_topk(const RefineArgs& a, cudaStream_t st);
 void refine_configure();

@@ -3,9 +3,9 @@
 // Replaces build_residual_lut_batched_kernel + residual_refine_batched_kernel
 // + batched_topk_final_kernel of the reference (jhq_v14_streaming_add/
 // search.cu:198-291) with one kernel, one CTA per query:
-//   1. the CTAs that scanned part of query q wrote slots (c + q); they are the
-//      CTAs whose page ranges [c*T/grid, (c+1)*T/grid) meet q's pages. Their
-//      sorted top-ck lists are merged pairwise (bitonic merge of two halves);
+//   1. the scan wrote one sorted top-ck list per (probe, chunk) of query q into
+//      its slots; the keys at or below the query's final bound are gathered and
+//      sorted (slot-by-slot bitonic merges when ties make them too many);
 //   2. warp per candidate: lane l reads 16-byte chunks l, l+32, ... of the
 //      candidate's residual row (coalesced), accumulates (q_j - res_c1d[r_j])^2
 //      as an in-order fma chain, and the warp reduces with an xor butterfly
@@ -22,15 +22,18 @@ namespace {
 
 constexpr int RF_THREADS = 512;
 constexpr int RF_WARPS = RF_THREADS / 32;
+constexpr int RF_CAP = 2048;          // gathered candidates kept for the sort
 
 __global__ void __launch_bounds__(RF_THREADS)
 refine_kernel(RefineArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     uint64_t* top = reinterpret_cast<uint64_t*>(smem);            // 2 * ck_pad
     uint64_t* comp = top + 2 * a.ck_pad;                           // ck_pad
+    uint64_t* buf = comp + a.ck_pad;                               // RF_CAP
+    int* nbuf = reinterpret_cast<int*>(buf + RF_CAP);              // 1 (16 bytes reserved)
     // q_rot padded by one float per 32: lane l reads dims 32l.. of its chunk,
     // and the padding puts the 32 lanes in 32 different banks.
-    float* qs = reinterpret_cast<float*>(comp + a.ck_pad);         // d + d/32 + 1
+    float* qs = reinterpret_cast<float*>(buf + RF_CAP + 2);        // d + d/32 + 1
     float* rc1d = qs + a.d + a.d / 32 + 1;                         // 256
 
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -41,22 +44,37 @@ refine_kernel(RefineArgs a) {
     for (int i = tid; i < Kr; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
     __syncthreads();
 
-    const int64_t T = a.qpage_off[a.nq];
-    const int64_t P0 = a.qpage_off[q], P1 = a.qpage_off[q + 1];
-    if (P1 > P0) {
-        // first CTA whose range end (c+1)*T/grid exceeds P0
-        int lo = 0, hi = a.grid - 1;
-        while (lo < hi) {
-            int mid = (lo + hi) >> 1;
-            if ((int64_t)(mid + 1) * T / a.grid > P0) hi = mid; else lo = mid + 1;
+    // candidates of query q: its slots [qslot_off[q], qslot_off[q+1]), ck keys
+    // each. Keys above the query's final bound gthr[q] cannot be in its top-ck
+    // (ck keys <= gthr[q] sit in one slot), so only the others are gathered.
+    const int64_t s0 = a.qslot_off[q], s1 = a.qslot_off[q + 1];
+    const uint64_t bound = a.gthr[q];
+    if (tid == 0) *nbuf = 0;
+    __syncthreads();
+    const int64_t nkeys = (s1 - s0) * a.ck;
+    const uint64_t* src = a.cand + s0 * a.ck;
+    for (int64_t i = tid; i < nkeys; i += RF_THREADS) {
+        const uint64_t key = src[i];
+        if (key != KEY_EMPTY && key <= bound) {
+            const int pos = atomicAdd(nbuf, 1);
+            if (pos < RF_CAP) buf[pos] = key;
         }
-        for (int c = lo; c < a.grid; ++c) {
-            const int64_t s0 = (int64_t)c * T / a.grid, s1 = (int64_t)(c + 1) * T / a.grid;
-            if (s0 >= P1) break;
-            if (s1 <= s0) continue;
-            const uint64_t* src = a.cand + ((int64_t)c + q) * a.ck;
+    }
+    __syncthreads();
+    const int n = *nbuf;
+    if (n <= RF_CAP) {
+        int P = a.ck_pad;
+        while (P < n) P <<= 1;
+        for (int i = n + tid; i < P; i += RF_THREADS) buf[i] = KEY_EMPTY;
+        __syncthreads();
+        block_bitonic_sort(buf, P);
+        for (int i = tid; i < a.ck_pad; i += RF_THREADS) top[i] = buf[i];
+        __syncthreads();
+    } else {                                   // many ties at the bound: merge slot by slot
+        for (int64_t sl = s0; sl < s1; ++sl) {
+            const uint64_t* sp = a.cand + sl * a.ck;
             for (int i = tid; i < a.ck_pad; i += RF_THREADS)
-                top[a.ck_pad + i] = (i < a.ck) ? src[i] : KEY_EMPTY;
+                top[a.ck_pad + i] = (i < a.ck) ? sp[i] : KEY_EMPTY;
             __syncthreads();
             block_merge_halves(top, a.ck_pad);
         }
@@ -134,7 +152,8 @@ merge_shards_kernel(const float* __restrict__ in_d, const int32_t* __restrict__ 
 
 void refine_topk(const RefineArgs& a, cudaStream_t st) {
     if (a.nq <= 0) return;
-    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + 256) * 4;
+    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + 256) * 4 +
+                  (size_t)RF_CAP * 8 + 16;
     refine_kernel<<<a.nq, RF_THREADS, smem, st>>>(a);
     JHQ_LAUNCH_CHECK();
     count_launch();

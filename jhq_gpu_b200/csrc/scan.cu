@@ -1,41 +1,47 @@
-// scan.cu — per-query byte LUT in shared memory + ADC scan over page-tiled
-// primary codes + exact top-ck selection. Replaces build_byte_lut_kernel and
-// scan_ivf_coalesced_kernel of the reference (jhq_v14_streaming_add/
-// search.cu:65-195) and the full-N thrust::sort of the flat path
-// (jhq_v1_plain/search.cu:193-194).
+// scan.cu — ADC scan over page-tiled primary codes with exact top-ck
+// selection, list-major and amortised over query groups. Replaces
+// build_byte_lut_kernel + scan_ivf_coalesced_kernel of the reference
+// (jhq_v14_streaming_add/search.cu:65-195) and the full-N thrust::sort of its
+// flat path (jhq_v1_plain/search.cu:193-194).
 //
-// Layout. Primary codes live in pages of 32 vectors. A page holds the codes
-// of its 32 slots as [Mp/16][32 lanes][16 bytes]: lane l of a warp loads its
+// Layout. Primary codes live in pages of 32 vectors. A page holds the codes of
+// its 32 slots as [Mp/16][32 lanes][16 bytes]: lane l of a warp loads its
 // vector's 16 codes of subspace group g with one 16-byte load, and the warp's
 // 32 loads cover 512 contiguous bytes (fully coalesced). Mp = M rounded up to
-// 16; pad subspaces have code 0 and a zero LUT row, so they add exactly 0.
+// 16; pad subspaces have code 0 and zero tables, so they add exactly 0.
 //
-// Work split. The probed pages of all queries of a batch form one sequence
-// (query-major, probe order inside a query, qpage_off = its offsets). A
-// persistent grid of `grid` CTAs splits it evenly: CTA c owns pages
-// [c*T/grid, (c+1)*T/grid). For every query segment it touches, the CTA
-//   1. builds that query's lookup tables in shared memory. When the bits of a
-//      dimension never straddle a nibble (bits_per_dim in {1, 2, 4}, i.e. every
-//      BASELINE config), the byte LUT entry LUT[m][b] is lo[m][b&15] +
-//      hi[m][b>>4], with lo/hi in-order fma chains of (q - c1d)^2 over the dims
-//      of each nibble — the order fixed in oracle/jhq_oracle.c — and only the two
-//      16-entry tables are stored (32 floats per subspace). A 16-entry table
-//      spans 16 distinct banks, so a warp's lookups are conflict-free whatever
-//      the codes: two conflict-free loads per code byte instead of a random
-//      256-way gather (~3.5 bank-conflict wavefronts per warp load). The
-//      entry is formed as lo + hi before it is added, so the sum is bit-identical
-//      to the byte-LUT sum. Other bit widths keep the full byte LUT;
-//   2. lets each warp scan pages two at a time: lane = slot, distance = sum
-//      over m in order of LUT[m][code_m] (search.cu:146-151 order);
-//   3. keeps a per-warp exact top-ck of packed (distance, id) keys: lanes whose
-//      key beats the warp's current ck-th key append to a shared buffer (ballot
-//      + popc), and a full buffer is merged into the list by a warp bitonic
-//      sort — the replacement of the reference's per-thread top-4 + ck serial
-//      block-argmin rounds (search.cu:153-194), which can drop true top-ck;
-//   4. merges its warps' lists with a block bitonic sort and writes the
-//      segment's top-ck keys to slot (c + q) of the candidate buffer. Slots are
-//      unique because (c, q) pairs advance monotonically in both coordinates.
-// refine.cu merges the slots of each query.
+// Work units (built on the device by plan_build in ivf.cu). The queries that
+// probe list l are grouped QG at a time; a unit is (list l, one query group,
+// one chunk of at most chunk_pages pages of l). Units are numbered list-major,
+// group-major, so a CTA's contiguous range of units mostly keeps one query
+// group and rebuilds its tables only when the group changes. For each unit the
+// CTA
+//   1. (re)builds the QG queries' lookup tables in shared memory. When the bits
+//      of a dimension never straddle a nibble (bits_per_dim in {1, 2, 4}: every
+//      BASELINE config) the byte-LUT entry LUT[m][b] is lo[m][b & 15] +
+//      hi[m][b >> 4], lo/hi being in-order fma chains of (q - c1d)^2 over the
+//      dims of each nibble (the order fixed in oracle/jhq_oracle.c), and only
+//      these 16-entry tables are stored, for two queries side by side
+//      (float2). A 16-entry table of float2 fills one 128-byte bank row, so a
+//      warp's 64-bit lookups are conflict-free whatever the codes (a random
+//      256-entry gather costs ~3.5 bank-conflict wavefronts per warp load).
+//      The entry is formed as lo + hi before it is added, so every distance is
+//      bit-identical to the byte-LUT sum. Other bit widths keep the byte LUT
+//      (one query per unit);
+//   2. lets each warp score pages two at a time: lane = slot, one distance per
+//      query of the group, each the in-order sum over m (search.cu:146-151).
+//      The nibble offsets of four codes come from two shift+mask ops and one
+//      byte-permute per code, shared by all queries of the group;
+//   3. keeps per warp and query an exact top-ck of packed (distance, id) keys
+//      (ballot + popc append into a shared buffer, merged by a warp bitonic
+//      sort when full) — the replacement of the reference's per-thread top-4
+//      + ck serial block-argmin rounds (search.cu:153-194), which can drop
+//      true top-ck. Candidates are pruned against min(warp ck-th, CTA ck-th,
+//      the query's global ck-th): a key above any of them has ck better keys
+//      already kept somewhere, so it cannot reach the query's top-ck;
+//   4. merges its warps' lists per query and writes the unit's top-ck to the
+//      query's slot (probe, chunk) of the candidate buffer, then lowers the
+//      query's global bound (64-bit atomicMin). refine.cu merges the slots.
 #include "device_utils.cuh"
 #include "jhq_common.h"
 #include "kernels.cuh"
@@ -45,12 +51,8 @@
 namespace jhq {
 namespace {
 
-constexpr int SCAN_THREADS = 512;
+constexpr int SCAN_THREADS = 256;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
-
-struct ScanSmem {
-    size_t tab, qs, c1d, wl, mrg, total;
-};
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -60,16 +62,28 @@ __host__ __device__ inline int merge_n_of(int ck_pad) {
     return n;
 }
 
-// The lookup table sits at offset 0 of dynamic shared memory, so its address
-// is a link-time constant and the lookups need no base register.
-__host__ __device__ inline ScanSmem scan_smem_layout(int Mp, int d, int ck_pad, bool nib) {
+// MODE: 0 = byte LUT (one query), 1/2/4 = nibble tables for 1/2/4 queries.
+__host__ __device__ constexpr int qg_of(int mode) { return mode == 0 ? 1 : mode; }
+__host__ __device__ inline size_t table_floats(int Mp, int mode) {
+    return (size_t)Mp * (mode == 0 ? 256 : 32 * qg_of(mode));
+}
+
+struct ScanSmem {
+    size_t tab, qs, c1d, wl, mrg, tau, total;
+};
+
+// The table sits at offset 0 of dynamic shared memory, so its address is a
+// link-time constant and the lookups need no base register.
+__host__ __device__ inline ScanSmem scan_smem_layout(int Mp, int d, int ck_pad, int mode) {
     ScanSmem s;
     size_t off = 0;
-    s.tab = off; off = align16(off + (size_t)Mp * (nib ? 32 : 256) * 4);
+    const int qg = qg_of(mode);
+    s.tab = off; off = align16(off + table_floats(Mp, mode) * 4);
     s.qs = off;  off = align16(off + (size_t)d * 4);
     s.c1d = off; off = align16(off + 256 * 4);
-    s.wl = off;  off = align16(off + (size_t)SCAN_WARPS * merge_n_of(ck_pad) * 8);
+    s.wl = off;  off = align16(off + (size_t)SCAN_WARPS * qg * merge_n_of(ck_pad) * 8);
     s.mrg = off; off = align16(off + (size_t)SCAN_WARPS * ck_pad * 8);
+    s.tau = off; off = align16(off + (size_t)qg * 8);
     s.total = off;
     return s;
 }
@@ -79,88 +93,125 @@ __host__ __device__ inline bool nibble_split(int d, int M, int B) {
     return bpd <= 4 && (4 % bpd) == 0;
 }
 
-// Tables of query q_rot (already in shared qs): nibble tables tab[Mp][32]
-// (lo at 0..15, hi at 16..31) when NIB, else the byte LUT tab[Mp][256].
-template <bool NIB>
-__device__ void build_tables(float* tab, const float* qs, const float* c1d, int d, int M, int Mp,
-                             int B) {
+// Tables of query slot j (q_rot already in shared qs).
+//  mode 0: tab[m][256] byte LUT;  mode 1: tab[m][32] (lo 0..15, hi 16..31);
+//  mode 2/4: tab[m][pair][32][2] — queries 2*pair and 2*pair+1 side by side.
+template <int MODE>
+__device__ void build_tables(float* tab, int j, const float* qs, const float* c1d, int d, int M,
+                             int Mp, int B, bool valid) {
     const int Ds = d / M, bpd = B / Ds, kmask = (1 << bpd) - 1;
-    if (NIB) {
-        const int kpn = 4 / bpd;                      // dims per nibble
-        for (int i = threadIdx.x; i < Mp * 32; i += blockDim.x) {
-            const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
-            float acc = 0.0f;
-            if (m < M) {
-                const int k0 = half ? kpn : 0;
-                const int k1 = half ? Ds : min(kpn, Ds);
-                for (int k = k0; k < k1; ++k) {
-                    const float diff = qs[m * Ds + k] - c1d[(n >> ((k - k0) * bpd)) & kmask];
-                    acc = __fmaf_rn(diff, diff, acc);
-                }
-            }
-            tab[i] = acc;
-        }
-    } else {
+    if (MODE == 0) {
         for (int i = threadIdx.x; i < Mp * 256; i += blockDim.x) {
             const int m = i >> 8, b = i & 255;
             float acc = 0.0f;
-            if (m < M)
+            if (valid && m < M)
                 for (int k = 0; k < Ds; ++k) {
                     const float diff = qs[m * Ds + k] - c1d[(b >> (k * bpd)) & kmask];
                     acc = __fmaf_rn(diff, diff, acc);
                 }
             tab[i] = acc;
         }
+        return;
     }
-    __syncthreads();
-}
-
-// Adds the 16 subspaces of one code group (16 bytes) to dist, in m order.
-template <bool NIB>
-__device__ __forceinline__ float add_group(float dist, const float* tg, const uint4& v) {
-#pragma unroll
-    for (int b = 0; b < 16; ++b) {
-        const uint32_t w = (b < 4) ? v.x : (b < 8) ? v.y : (b < 12) ? v.z : v.w;
-        const int sh = (b & 3) * 8;
-        float e;
-        if (NIB) {
-            const float* nm = tg + b * 32;
-            e = __fadd_rn(nm[(w >> sh) & 15u], nm[16 + ((w >> (sh + 4)) & 15u)]);
-        } else {
-            e = tg[b * 256 + ((w >> sh) & 255u)];
+    constexpr int QG = qg_of(MODE);
+    const int kpn = 4 / bpd;                          // dims per nibble
+    for (int i = threadIdx.x; i < Mp * 32; i += blockDim.x) {
+        const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
+        float acc = 0.0f;
+        if (valid && m < M) {
+            const int k0 = half ? kpn : 0;
+            const int k1 = half ? Ds : min(kpn, Ds);
+            for (int k = k0; k < k1; ++k) {
+                const float diff = qs[m * Ds + k] - c1d[(n >> ((k - k0) * bpd)) & kmask];
+                acc = __fmaf_rn(diff, diff, acc);
+            }
         }
-        dist = __fadd_rn(dist, e);
+        if (QG == 1) tab[i] = acc;
+        else tab[((m * (QG / 2) + (j >> 1)) * 32 + t) * 2 + (j & 1)] = acc;
     }
-    return dist;
 }
 
-// Per-warp exact top-ck state: s[0..ck_pad) sorted list, s[ck_pad..merge_n) buffer.
+// Adds the 16 subspaces of one code group (16 bytes of one vector) to the
+// group's QG distances, in m order. tg points at subspace g*16 of the table.
+template <int MODE>
+__device__ __forceinline__ void add_group(float* dist, const unsigned char* tg, const uint4& v) {
+    constexpr int QG = qg_of(MODE);
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t w = wi == 0 ? v.x : wi == 1 ? v.y : wi == 2 ? v.z : v.w;
+        if (MODE == 0) {
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                const int b = wi * 4 + bb;
+                const float* row = reinterpret_cast<const float*>(tg) + b * 256;
+                dist[0] = __fadd_rn(dist[0], row[(w >> (bb * 8)) & 255u]);
+            }
+        } else {
+            // byte offsets of the lo / hi nibble entries of the 4 codes of w
+            constexpr int SH = QG == 1 ? 2 : 3;           // entry size 4 or 8 bytes
+            constexpr uint32_t MASK = QG == 1 ? 0x3C3C3C3Cu : 0x78787878u;
+            const uint32_t Lo = (w << SH) & MASK;
+            const uint32_t Hi = (w >> (4 - SH)) & MASK;
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                const int b = wi * 4 + bb;
+                const uint32_t olo = __byte_perm(Lo, 0u, 0x4440u | bb);
+                const uint32_t ohi = __byte_perm(Hi, 0u, 0x4440u | bb);
+                if (QG == 1) {
+                    const unsigned char* row = tg + b * 128;
+                    const float lo = *reinterpret_cast<const float*>(row + olo);
+                    const float hi = *reinterpret_cast<const float*>(row + 64 + ohi);
+                    dist[0] = __fadd_rn(dist[0], __fadd_rn(lo, hi));
+                } else {
+#pragma unroll
+                    for (int pr = 0; pr < QG / 2; ++pr) {
+                        const unsigned char* row = tg + (b * (QG / 2) + pr) * 256;
+                        const float2 lo = *reinterpret_cast<const float2*>(row + olo);
+                        const float2 hi = *reinterpret_cast<const float2*>(row + 128 + ohi);
+                        dist[2 * pr] = __fadd_rn(dist[2 * pr], __fadd_rn(lo.x, hi.x));
+                        dist[2 * pr + 1] = __fadd_rn(dist[2 * pr + 1], __fadd_rn(lo.y, hi.y));
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Per-warp exact top-ck of one query: s[0..ck_pad) sorted list,
+// s[ck_pad..merge_n) append buffer. thr = pruning bound (uniform in the warp).
 struct WarpTop {
     uint64_t* s;
-    uint64_t thr;     // current ck-th key (uniform in the warp)
-    int count;        // buffered entries (uniform)
-    int ck, ck_pad, merge_n;
+    uint64_t thr;
+    int count;
 
-    __device__ __forceinline__ void reset(int lane) {
+    __device__ __forceinline__ void reset(int lane, int merge_n, uint64_t bound) {
         for (int i = lane; i < merge_n; i += 32) s[i] = KEY_EMPTY;
-        thr = KEY_EMPTY;
+        thr = bound;
         count = 0;
         __syncwarp();
     }
-    __device__ __forceinline__ void flush(int lane) {
+    // Merge the buffer into the list; publish the warp's ck-th key to the CTA
+    // bound and pick up the tightest bound.
+    __device__ __forceinline__ void flush(int lane, int ck, int ck_pad, int merge_n, uint64_t* tau) {
         const int cap = merge_n - ck_pad;
         for (int i = count + lane; i < cap; i += 32) s[ck_pad + i] = KEY_EMPTY;
         __syncwarp();
         warp_bitonic_sort(s, merge_n, lane);
-        thr = s[ck - 1];
+        const uint64_t kth = s[ck - 1];
+        if (lane == 0 && kth != KEY_EMPTY)
+            atomicMin(reinterpret_cast<unsigned long long*>(tau), (unsigned long long)kth);
+        __syncwarp();
+        const uint64_t t = *reinterpret_cast<volatile uint64_t*>(tau);
+        thr = kth < t ? kth : t;
         count = 0;
     }
-    __device__ __forceinline__ void push(uint64_t key, int lane) {
+    __device__ __forceinline__ void push(uint64_t key, int lane, int ck, int ck_pad, int merge_n,
+                                         uint64_t* tau) {
         bool take = key < thr;
         unsigned mask = __ballot_sync(0xffffffffu, take);
         if (mask == 0) return;
         if (count + __popc(mask) > merge_n - ck_pad) {
-            flush(lane);
+            flush(lane, ck, ck_pad, merge_n, tau);
             take = key < thr;
             mask = __ballot_sync(0xffffffffu, take);
             if (mask == 0) return;
@@ -171,144 +222,189 @@ struct WarpTop {
     }
 };
 
-template <int G_T, bool NIB>
+struct UnitInfo {
+    int64_t pb, pe;          // physical page range
+    int q[4];                // member queries (-1 = none)
+    int64_t slot[4];         // candidate slot of each member
+};
+
+template <int G_T, int MODE>
 __global__ void __launch_bounds__(SCAN_THREADS, 1)
 scan_kernel(ScanArgs a) {
+    constexpr int QG = qg_of(MODE);
+    constexpr int TROW = MODE == 0 ? 1024 : (QG == 1 ? 128 : 256 * (QG / 2));  // bytes per m
     extern __shared__ __align__(16) unsigned char smem[];
-    const ScanSmem L = scan_smem_layout(a.Mp, a.d, a.ck_pad, NIB);
+    __shared__ UnitInfo unit;
+    __shared__ int cur_q[4];
+    const ScanSmem L = scan_smem_layout(a.Mp, a.d, a.ck_pad, MODE);
     float* tab = reinterpret_cast<float*>(smem);                 // offset 0
     float* qs = reinterpret_cast<float*>(smem + L.qs);
     float* c1d = reinterpret_cast<float*>(smem + L.c1d);
     uint64_t* wl = reinterpret_cast<uint64_t*>(smem + L.wl);
     uint64_t* mrg = reinterpret_cast<uint64_t*>(smem + L.mrg);
-    constexpr int TSTRIDE = NIB ? 32 : 256;                       // floats per subspace
+    uint64_t* tau = reinterpret_cast<uint64_t*>(smem + L.tau);
 
     const int G = G_T > 0 ? G_T : a.Mp / 16;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int merge_n = merge_n_of(a.ck_pad);
-    const int64_t T = a.qpage_off[a.nq];
-    const int64_t c = blockIdx.x;
-    const int64_t start = c * T / a.grid, end = (c + 1) * T / a.grid;
-    if (start >= end) return;
+    const int nunits = a.unit_off[a.nlist];
+    const int u0 = (int)((int64_t)blockIdx.x * nunits / a.grid);
+    const int u1 = (int)((int64_t)(blockIdx.x + 1) * nunits / a.grid);
+    if (u0 >= u1) return;
 
     const int K1D = 1 << (a.B / (a.d / a.M));
     for (int i = tid; i < K1D; i += SCAN_THREADS) c1d[i] = a.c1d[i];
+    if (tid < 4) cur_q[tid] = -2;
 
-    // query containing page `start`: last q with qpage_off[q] <= start
-    int lo = 0, hi = a.nq;                                   // qpage_off[hi] > start
-    while (hi - lo > 1) {
-        int mid = (lo + hi) >> 1;
-        if (a.qpage_off[mid] <= start) lo = mid; else hi = mid;
+    // list of unit u0: last l with unit_off[l] <= u0
+    int lst = 0;
+    {
+        int lo = 0, hi = a.nlist;
+        while (hi - lo > 1) {
+            int mid = (lo + hi) >> 1;
+            if (a.unit_off[mid] <= u0) lo = mid; else hi = mid;
+        }
+        lst = lo;
     }
-    int q = lo;
-
-    WarpTop top;
-    top.s = wl + (size_t)warp * merge_n;
-    top.ck = a.ck; top.ck_pad = a.ck_pad; top.merge_n = merge_n;
-
-    int64_t pos = start;
-    while (pos < end) {
-        const int64_t qbase = a.qpage_off[q];
-        const int64_t seg_end = min(end, a.qpage_off[q + 1]);
-        // ---- tables of query q
-        __syncthreads();
-        for (int i = tid; i < a.d; i += SCAN_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
-        __syncthreads();
-        build_tables<NIB>(tab, qs, c1d, a.d, a.M, a.Mp, a.B);
-        top.reset(lane);
-
-        // ---- scan: warp w takes page pairs (lp, lp+1), lp = first + 2*(w + W*i)
-        const int32_t* ppo = a.probe_page_off + (int64_t)q * (a.nprobe + 1);
-        const int32_t* pr = a.probes + (int64_t)q * a.nprobe;
-        const int first = (int)(pos - qbase), last = (int)(seg_end - qbase);
-        int p = 0;                                        // probe cursor (monotone per warp)
-        for (int lp = first + 2 * warp; lp < last; lp += 2 * SCAN_WARPS) {
-            int64_t phys[2];
-            bool valid[2];
+    WarpTop top[QG];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                int l = lp + u;
-                valid[u] = l < last;
-                phys[u] = 0;
-                if (valid[u]) {
-                    while (l >= ppo[p + 1]) ++p;
-                    phys[u] = a.list_page_off[pr[p]] + (l - ppo[p]);
+    for (int j = 0; j < QG; ++j) top[j].s = wl + ((size_t)warp * QG + j) * merge_n;
+
+    for (int u = u0; u < u1; ++u) {
+        __syncthreads();                       // previous unit done with unit/tables/mrg
+        if (tid == 0) {
+            while (a.unit_off[lst + 1] <= u) ++lst;
+            const int pages0 = a.list_page_off[lst], pages1 = a.list_page_off[lst + 1];
+            const int nch = (pages1 - pages0 + a.chunk_pages - 1) / a.chunk_pages;
+            const int v = u - a.unit_off[lst];
+            const int grp = v / nch, ch = v % nch;
+            const int b0 = a.bucket_off[lst], cnt = a.bucket_off[lst + 1] - b0;
+            unit.pb = pages0 + (int64_t)ch * a.chunk_pages;
+            unit.pe = min((int64_t)pages1, unit.pb + a.chunk_pages);
+            for (int j = 0; j < 4; ++j) {
+                unit.q[j] = -1;
+                unit.slot[j] = -1;
+                if (j < QG && grp * QG + j < cnt) {
+                    const int2 qp = a.bucket[b0 + grp * QG + j];
+                    unit.q[j] = qp.x;
+                    unit.slot[j] = a.qslot_off[qp.x] + a.cpo[(int64_t)qp.x * (a.nprobe + 1) + qp.y] + ch;
                 }
             }
-            const int32_t id0 = __ldg(a.slot_ids + phys[0] * 32 + lane);
-            const int32_t id1 = valid[1] ? __ldg(a.slot_ids + phys[1] * 32 + lane) : -1;
-            float d0 = 0.0f, d1 = 0.0f;
-            const uint4* pg0 = reinterpret_cast<const uint4*>(a.pages) + phys[0] * G * 32 + lane;
-            const uint4* pg1 = reinterpret_cast<const uint4*>(a.pages) + phys[1] * G * 32 + lane;
+        }
+        __syncthreads();
+        bool same = true;
+#pragma unroll
+        for (int j = 0; j < QG; ++j) same = same && (unit.q[j] == cur_q[j]);
+        if (!same) {                           // tables of the new query group
+            for (int j = 0; j < QG; ++j) {
+                const int q = unit.q[j];
+                if (q >= 0)
+                    for (int i = tid; i < a.d; i += SCAN_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
+                __syncthreads();
+                build_tables<MODE>(tab, j, qs, c1d, a.d, a.M, a.Mp, a.B, q >= 0);
+                __syncthreads();
+            }
+            __syncthreads();
+            if (tid < QG) cur_q[tid] = unit.q[tid];
+        }
+        if (tid < QG) tau[tid] = unit.q[tid] >= 0 ? a.gthr[unit.q[tid]] : KEY_EMPTY;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < QG; ++j) top[j].reset(lane, merge_n, tau[j]);
+
+        // ---- score pages two at a time: warp w takes pb + 2*(w + W*i)
+        const int64_t pb = unit.pb, pe = unit.pe;
+        for (int64_t pg = pb + 2 * warp; pg < pe; pg += 2 * SCAN_WARPS) {
+            const bool v1 = pg + 1 < pe;
+            const int32_t id0 = __ldg(a.slot_ids + pg * 32 + lane);
+            const int32_t id1 = v1 ? __ldg(a.slot_ids + (pg + 1) * 32 + lane) : -1;
+            float d0[QG], d1[QG];
+#pragma unroll
+            for (int j = 0; j < QG; ++j) { d0[j] = 0.0f; d1[j] = 0.0f; }
+            const uint4* p0 = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
+            const uint4* p1 = p0 + G * 32;
             // group g+1 of both pages is in flight while group g is looked up
-            uint4 c0 = __ldg(pg0), c1 = valid[1] ? __ldg(pg1) : make_uint4(0, 0, 0, 0);
+            uint4 c0 = __ldg(p0), c1 = v1 ? __ldg(p1) : make_uint4(0, 0, 0, 0);
 #pragma unroll (G_T > 0 ? G_T : 1)
             for (int g = 0; g < G; ++g) {
                 uint4 n0 = c0, n1 = c1;
                 if (g + 1 < G) {
-                    n0 = __ldg(pg0 + (g + 1) * 32);
-                    if (valid[1]) n1 = __ldg(pg1 + (g + 1) * 32);
+                    n0 = __ldg(p0 + (g + 1) * 32);
+                    if (v1) n1 = __ldg(p1 + (g + 1) * 32);
                 }
-                const float* tg = tab + g * 16 * TSTRIDE;
-                d0 = add_group<NIB>(d0, tg, c0);
-                d1 = add_group<NIB>(d1, tg, c1);
+                const unsigned char* tg = smem + (size_t)g * 16 * TROW;
+                add_group<MODE>(d0, tg, c0);
+                add_group<MODE>(d1, tg, c1);
                 c0 = n0;
                 c1 = n1;
             }
-            top.push(id0 >= 0 ? make_key(d0, id0) : KEY_EMPTY, lane);
-            top.push(id1 >= 0 ? make_key(d1, id1) : KEY_EMPTY, lane);
+#pragma unroll
+            for (int j = 0; j < QG; ++j) {
+                if (unit.q[j] < 0) continue;
+                top[j].push(id0 >= 0 ? make_key(d0[j], id0) : KEY_EMPTY, lane, a.ck, a.ck_pad,
+                            merge_n, tau + j);
+                top[j].push(id1 >= 0 ? make_key(d1[j], id1) : KEY_EMPTY, lane, a.ck, a.ck_pad,
+                            merge_n, tau + j);
+            }
         }
-        top.flush(lane);
-        __syncwarp();
-        for (int i = lane; i < a.ck_pad; i += 32) mrg[warp * a.ck_pad + i] = top.s[i];
-        __syncthreads();
-        block_bitonic_sort(mrg, SCAN_WARPS * a.ck_pad);
-        uint64_t* out = a.cand + (c + q) * a.ck;
-        for (int i = tid; i < a.ck; i += SCAN_THREADS) out[i] = mrg[i];
+#pragma unroll
+        for (int j = 0; j < QG; ++j) top[j].flush(lane, a.ck, a.ck_pad, merge_n, tau + j);
 
-        pos = seg_end;
-        if (pos < end) {                                   // next query with pages
-            ++q;
-            while (a.qpage_off[q + 1] <= pos) ++q;
+        // ---- per member: merge the warps' lists, write the slot, lower the bound
+        for (int j = 0; j < QG; ++j) {
+            if (unit.q[j] < 0) continue;       // uniform across the block
+            __syncthreads();
+            for (int i = lane; i < a.ck_pad; i += 32) mrg[warp * a.ck_pad + i] = top[j].s[i];
+            __syncthreads();
+            block_bitonic_sort(mrg, SCAN_WARPS * a.ck_pad);
+            uint64_t* out = a.cand + unit.slot[j] * a.ck;
+            for (int i = tid; i < a.ck; i += SCAN_THREADS) out[i] = mrg[i];
+            if (tid == 0 && mrg[a.ck - 1] != KEY_EMPTY)
+                atomicMin(reinterpret_cast<unsigned long long*>(a.gthr + unit.q[j]),
+                          (unsigned long long)mrg[a.ck - 1]);
         }
     }
 }
 
-template <int G_T, bool NIB>
+template <int G_T, int MODE>
 void launch_scan(const ScanArgs& a, size_t smem, cudaStream_t st) {
-    scan_kernel<G_T, NIB><<<a.grid, SCAN_THREADS, smem, st>>>(a);
+    scan_kernel<G_T, MODE><<<a.grid, SCAN_THREADS, smem, st>>>(a);
 }
 
-template <int G_T, bool NIB>
+template <int G_T, int MODE>
 void configure_one() {
-    JHQ_CUDA(cudaFuncSetAttribute(scan_kernel<G_T, NIB>,
+    JHQ_CUDA(cudaFuncSetAttribute(scan_kernel<G_T, MODE>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
 }
 
-template <int G_T, bool NIB>
+template <int G_T, int MODE>
 int blocks_per_sm(size_t smem) {
     int n = 0;
-    JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_kernel<G_T, NIB>, SCAN_THREADS,
+    JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, scan_kernel<G_T, MODE>, SCAN_THREADS,
                                                            smem));
     return n;
 }
 
-// Dispatch on (Mp/16, nibble) to the compile-time instantiations.
+template <int G, class F>
+auto dispatch_mode(int mode, F&& f) {
+    switch (mode) {
+        case 0: return f(std::integral_constant<int, G>{}, std::integral_constant<int, 0>{});
+        case 1: return f(std::integral_constant<int, G>{}, std::integral_constant<int, 1>{});
+        case 2: return f(std::integral_constant<int, G>{}, std::integral_constant<int, 2>{});
+        default: return f(std::integral_constant<int, G>{}, std::integral_constant<int, 4>{});
+    }
+}
+
+// Dispatch on (Mp/16, mode) to the compile-time instantiations.
 template <class F>
-auto dispatch(int Mp, bool nib, F&& f) {
+auto dispatch(int Mp, int mode, F&& f) {
     switch (Mp / 16) {
-        case 1: return nib ? f(std::integral_constant<int, 1>{}, std::true_type{})
-                           : f(std::integral_constant<int, 1>{}, std::false_type{});
-        case 2: return nib ? f(std::integral_constant<int, 2>{}, std::true_type{})
-                           : f(std::integral_constant<int, 2>{}, std::false_type{});
-        case 4: return nib ? f(std::integral_constant<int, 4>{}, std::true_type{})
-                           : f(std::integral_constant<int, 4>{}, std::false_type{});
-        case 6: return nib ? f(std::integral_constant<int, 6>{}, std::true_type{})
-                           : f(std::integral_constant<int, 6>{}, std::false_type{});
-        case 8: return nib ? f(std::integral_constant<int, 8>{}, std::true_type{})
-                           : f(std::integral_constant<int, 8>{}, std::false_type{});
-        default: return nib ? f(std::integral_constant<int, 0>{}, std::true_type{})
-                            : f(std::integral_constant<int, 0>{}, std::false_type{});
+        case 1: return dispatch_mode<1>(mode, f);
+        case 2: return dispatch_mode<2>(mode, f);
+        case 4: return dispatch_mode<4>(mode, f);
+        case 6: return dispatch_mode<6>(mode, f);
+        case 8: return dispatch_mode<8>(mode, f);
+        default: return dispatch_mode<0>(mode, f);
     }
 }
 
@@ -316,31 +412,35 @@ auto dispatch(int Mp, bool nib, F&& f) {
 
 void scan_configure() {
     for (int g : {1, 2, 4, 6, 8, 0})
-        for (bool nib : {true, false})
-            dispatch(g * 16, nib, [](auto G, auto N) { configure_one<G.value, N.value>(); return 0; });
+        for (int mode : {0, 1, 2, 4})
+            dispatch(g * 16, mode, [](auto G, auto Md) { configure_one<G.value, Md.value>(); return 0; });
 }
 
-size_t scan_smem_bytes(int Mp, int d, int ck_pad, bool nib) {
-    return scan_smem_layout(Mp, d, ck_pad, nib).total;
+int scan_mode_for(int d, int M, int B, double queries_per_list) {
+    if (!nibble_split(d, M, B)) return 0;
+    if (queries_per_list >= 3.0) return 4;
+    if (queries_per_list >= 1.5) return 2;
+    return 1;
 }
 
-bool scan_uses_nibbles(int d, int M, int B) { return nibble_split(d, M, B); }
+size_t scan_smem_bytes(int Mp, int d, int ck_pad, int mode) {
+    return scan_smem_layout(Mp, d, ck_pad, mode).total;
+}
 
-int scan_grid_for(int Mp, int d, int ck_pad, bool nib) {
+int scan_grid_for(int Mp, int d, int ck_pad, int mode) {
     int dev = 0, sms = 0;
     JHQ_CUDA(cudaGetDevice(&dev));
     JHQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const size_t smem = scan_smem_layout(Mp, d, ck_pad, nib).total;
-    const int per_sm = dispatch(Mp, nib, [&](auto G, auto N) { return blocks_per_sm<G.value, N.value>(smem); });
+    const size_t smem = scan_smem_layout(Mp, d, ck_pad, mode).total;
+    const int per_sm = dispatch(Mp, mode, [&](auto G, auto Md) { return blocks_per_sm<G.value, Md.value>(smem); });
     if (per_sm < 1) fail(JHQ_EINVAL, "scan: kernel does not fit on an SM (reduce M or d)");
     return sms * per_sm;
 }
 
 void scan_topck(const ScanArgs& a, cudaStream_t st) {
-    const bool nib = nibble_split(a.d, a.M, a.B);
-    const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad, nib).total;
-    if (smem > 227 * 1024) fail(JHQ_EINVAL, "scan: shared-memory LUT too large (reduce M)");
-    dispatch(a.Mp, nib, [&](auto G, auto N) { launch_scan<G.value, N.value>(a, smem, st); return 0; });
+    const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad, a.mode).total;
+    if (smem > 227 * 1024) fail(JHQ_EINVAL, "scan: shared-memory tables too large (reduce M)");
+    dispatch(a.Mp, a.mode, [&](auto G, auto Md) { launch_scan<G.value, Md.value>(a, smem, st); return 0; });
     JHQ_LAUNCH_CHECK();
     count_launch();
 }
