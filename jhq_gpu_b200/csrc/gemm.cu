@@ -8,7 +8,7 @@
 // (oracle/jhq_oracle.c: oracle_rotate / dot_chain). Two tilings:
 //  - gemm_tiled_kernel : 128x128 CTA tile, 8x8 outputs per thread, for tall
 //                        operands (add-time rotation, k-means assignment);
-//  - gemm_skinny_kernel: 2 rows x 64 columns per CTA, both operands staged
+//  - gemm_skinny_kernel: 16 rows x 64 columns per CTA, both operands staged
 //                        through shared memory by double-buffered cp.async —
 //                        for query batches, where a 128-row tile would leave
 //                        most SMs idle.
@@ -110,11 +110,14 @@ gemm_tiled_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
     }
 }
 
-// Skinny path: CTA = SK_TR rows x SK_BN columns, one column per thread with
-// SK_TR independent chains. Chunks of SK_KC rows of B (and the matching SK_TR x
-// SK_KC slice of A) are staged in shared memory by cp.async, double-buffered,
-// so the L2 latency of the streamed right operand overlaps the FMAs.
-constexpr int SK_TR = 2, SK_BN = 64, SK_KC = 32;
+// Skinny path: CTA = SK_ROWS rows x SK_BN columns, 256 threads; thread
+// (column c, row group r) owns rows r*SK_TR .. r*SK_TR+SK_TR-1 of column c:
+// SK_TR independent chains. Chunks of SK_KC rows of B (and the matching
+// SK_ROWS x SK_KC slice of A) are staged in shared memory by cp.async,
+// double-buffered. 16 rows per CTA keep the L2 re-reads of B (the d x d
+// rotation) at a quarter of a 4-row tiling.
+constexpr int SK_TR = 4, SK_RG = 4, SK_ROWS = SK_TR * SK_RG, SK_BN = 64, SK_KC = 32;
+constexpr int SK_THREADS = SK_BN * SK_RG;
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
@@ -130,44 +133,41 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n"); }
 
 template <int EPI>
-__global__ void __launch_bounds__(SK_BN)
+__global__ void __launch_bounds__(SK_THREADS)
 gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
                    int64_t R, int K, int N, const float* __restrict__ norms, int vec16) {
     __shared__ __align__(16) float Bs[2][SK_KC][SK_BN];
-    __shared__ __align__(16) float As[2][SK_TR][SK_KC];
-    const int tid = threadIdx.x;
+    __shared__ __align__(16) float As[2][SK_ROWS][SK_KC];
+    const int tid = threadIdx.x, col = tid % SK_BN, rg = tid / SK_BN;
     const int n0 = blockIdx.x * SK_BN;
-    const int64_t r0 = (int64_t)blockIdx.y * SK_TR;
-    const int n = n0 + tid;
+    const int64_t r0 = (int64_t)blockIdx.y * SK_ROWS;
+    const int n = n0 + col;
 
     auto stage = [&](int buf, int k0) {
         if (vec16) {
-            // B chunk: SK_KC rows x SK_BN cols = SK_KC * 32 16-byte pieces
-            for (int i = tid; i < SK_KC * (SK_BN / 4); i += SK_BN) {
+            for (int i = tid; i < SK_KC * (SK_BN / 4); i += SK_THREADS) {
                 const int kr = i / (SK_BN / 4), c4 = (i % (SK_BN / 4)) * 4;
                 const int gk = k0 + kr, gn = n0 + c4;
                 int bytes = 0;
                 if (gk < K && gn < N) bytes = min(4, N - gn) * 4;
-                const float* src = bytes ? B + (int64_t)gk * N + gn : B;
-                cp_async16(&Bs[buf][kr][c4], src, bytes);
+                cp_async16(&Bs[buf][kr][c4], bytes ? B + (int64_t)gk * N + gn : B, bytes);
             }
-            for (int i = tid; i < SK_TR * (SK_KC / 4); i += SK_BN) {
+            for (int i = tid; i < SK_ROWS * (SK_KC / 4); i += SK_THREADS) {
                 const int r = i / (SK_KC / 4), c4 = (i % (SK_KC / 4)) * 4;
                 const int64_t gr = r0 + r;
                 const int gk = k0 + c4;
                 int bytes = 0;
                 if (gr < R && gk < K) bytes = min(4, K - gk) * 4;
-                const float* src = bytes ? A + gr * K + gk : A;
-                cp_async16(&As[buf][r][c4], src, bytes);
+                cp_async16(&As[buf][r][c4], bytes ? A + gr * K + gk : A, bytes);
             }
         } else {
-            for (int i = tid; i < SK_KC * SK_BN; i += SK_BN) {
+            for (int i = tid; i < SK_KC * SK_BN; i += SK_THREADS) {
                 const int kr = i / SK_BN, c = i % SK_BN;
                 const int gk = k0 + kr, gn = n0 + c;
                 const bool ok = gk < K && gn < N;
                 cp_async4(&Bs[buf][kr][c], ok ? B + (int64_t)gk * N + gn : B, ok);
             }
-            for (int i = tid; i < SK_TR * SK_KC; i += SK_BN) {
+            for (int i = tid; i < SK_ROWS * SK_KC; i += SK_THREADS) {
                 const int r = i / SK_KC, c = i % SK_KC;
                 const int64_t gr = r0 + r;
                 const int gk = k0 + c;
@@ -192,11 +192,11 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
         if (kl == SK_KC) {
 #pragma unroll
             for (int k = 0; k < SK_KC; k += 4) {
-                const float b0 = Bs[buf][k][tid], b1 = Bs[buf][k + 1][tid];
-                const float b2 = Bs[buf][k + 2][tid], b3 = Bs[buf][k + 3][tid];
+                const float b0 = Bs[buf][k][col], b1 = Bs[buf][k + 1][col];
+                const float b2 = Bs[buf][k + 2][col], b3 = Bs[buf][k + 3][col];
 #pragma unroll
                 for (int r = 0; r < SK_TR; ++r) {
-                    const float4 a = *reinterpret_cast<const float4*>(&As[buf][r][k]);
+                    const float4 a = *reinterpret_cast<const float4*>(&As[buf][rg * SK_TR + r][k]);
                     acc[r] = __fmaf_rn(a.x, b0, acc[r]);
                     acc[r] = __fmaf_rn(a.y, b1, acc[r]);
                     acc[r] = __fmaf_rn(a.z, b2, acc[r]);
@@ -205,9 +205,10 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
             }
         } else {
             for (int k = 0; k < kl; ++k) {
-                const float b = Bs[buf][k][tid];
+                const float b = Bs[buf][k][col];
 #pragma unroll
-                for (int r = 0; r < SK_TR; ++r) acc[r] = __fmaf_rn(As[buf][r][k], b, acc[r]);
+                for (int r = 0; r < SK_TR; ++r)
+                    acc[r] = __fmaf_rn(As[buf][rg * SK_TR + r][k], b, acc[r]);
             }
         }
         __syncthreads();
@@ -215,7 +216,7 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
     if (n < N) {
 #pragma unroll
         for (int r = 0; r < SK_TR; ++r) {
-            const int64_t gr = r0 + r;
+            const int64_t gr = r0 + rg * SK_TR + r;
             if (gr < R) C[gr * N + n] = epilogue<EPI>(acc[r], norms, n);
         }
     }
@@ -227,13 +228,13 @@ void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N
                GemmEpi epi, const float* norms, cudaStream_t s) {
     if (R <= 0 || N <= 0) return;
     if (R <= 1024) {
-        dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, SK_TR));
+        dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, SK_ROWS));
         const int vec16 = (N % 4 == 0) && (K % 4 == 0) && (((uintptr_t)A | (uintptr_t)B) % 16 == 0);
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");
         if (epi == EPI_COARSE)
-            gemm_skinny_kernel<EPI_COARSE><<<grid, SK_BN, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            gemm_skinny_kernel<EPI_COARSE><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
         else
-            gemm_skinny_kernel<EPI_STORE><<<grid, SK_BN, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            gemm_skinny_kernel<EPI_STORE><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
     } else {
         dim3 grid((unsigned)ceil_div(N, TBN), (unsigned)ceil_div(R, TBM));
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <functional>
@@ -361,6 +362,10 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
     // and top-ck lists do not fit in shared memory
     const double qpl = (double)Bq * p_.nprobe / p_.nlist;
     sh.mode = scan_mode_for(d_, M_, B_, qpl);
+    // tuning override: JHQ_SCAN_MODE=1|2|4 forces the query-group width
+    if (const char* e = std::getenv("JHQ_SCAN_MODE"))
+        if (sh.mode != 0 && (!std::strcmp(e, "1") || !std::strcmp(e, "2") || !std::strcmp(e, "4")))
+            sh.mode = std::atoi(e);
     while (sh.mode > 1 && scan_smem_bytes(Mp_, d_, sh.ck_pad, sh.mode) > 227 * 1024) sh.mode /= 2;
     sh.grid = scan_grid_for(Mp_, d_, sh.ck_pad, sh.mode);
     // chunk size: about four units per CTA for the expected page visits

@@ -131,27 +131,40 @@ __global__ void plan_count_kernel(const int32_t* __restrict__ probes, int nq, in
     }
 }
 
-// In-place exclusive scan of v[0..n) with one block; returns the total.
+// Exclusive scan of value_of(0..n) into out[0..n) with one block (warp
+// shuffles inside a warp, one shared round across warps); returns the total.
 template <class T, class F>
 __device__ T block_exclusive_scan(int n, F&& value_of, T* out) {
-    __shared__ T part[PLAN_THREADS];
+    __shared__ T wsum[PLAN_THREADS / 32];
     __shared__ T carry;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
     for (int base = 0; base < n; base += PLAN_THREADS) {
         const int i = base + threadIdx.x;
         const T v = i < n ? value_of(i) : T(0);
-        part[threadIdx.x] = v;
-        __syncthreads();
-        for (int o = 1; o < PLAN_THREADS; o <<= 1) {
-            T x = threadIdx.x >= o ? part[threadIdx.x - o] : T(0);
-            __syncthreads();
-            part[threadIdx.x] += x;
-            __syncthreads();
+        T x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const T y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
         }
-        if (i < n) out[i] = carry + part[threadIdx.x] - v;
+        if (lane == 31) wsum[warp] = x;
         __syncthreads();
-        if (threadIdx.x == PLAN_THREADS - 1) carry += part[PLAN_THREADS - 1];
+        if (warp == 0) {
+            T t = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const T y = __shfl_up_sync(0xffffffffu, t, o);
+                if (lane >= o) t += y;
+            }
+            wsum[lane] = t;                    // inclusive over warps
+        }
+        __syncthreads();
+        const T before = carry + (warp ? wsum[warp - 1] : T(0));
+        if (i < n) out[i] = before + x - v;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += wsum[PLAN_THREADS / 32 - 1];
         __syncthreads();
     }
     return carry;

@@ -39,9 +39,10 @@
 //      true top-ck. Candidates are pruned against min(warp ck-th, CTA ck-th,
 //      the query's global ck-th): a key above any of them has ck better keys
 //      already kept somewhere, so it cannot reach the query's top-ck;
-//   4. merges its warps' lists per query and writes the unit's top-ck to the
-//      query's slot (probe, chunk) of the candidate buffer, then lowers the
-//      query's global bound (64-bit atomicMin). refine.cu merges the slots.
+//   4. at the end of a run (consecutive units of one list and query group on
+//      this CTA) merges its warps' lists per query, writes the top-ck to the
+//      run's first slot (the run's other slots hold empty lists) and lowers
+//      the query's global bound (64-bit atomicMin). refine.cu merges the slots.
 #include "device_utils.cuh"
 #include "jhq_common.h"
 #include "kernels.cuh"
@@ -51,8 +52,12 @@
 namespace jhq {
 namespace {
 
+#ifndef JHQ_SCAN_MIN_BLOCKS
+#define JHQ_SCAN_MIN_BLOCKS 2
+#endif
 constexpr int SCAN_THREADS = 256;
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
+constexpr size_t SCAN_SMEM_LIMIT = 227 * 1024 - 1024;   // dynamic bytes left after statics
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -177,6 +182,15 @@ __device__ __forceinline__ void add_group(float* dist, const unsigned char* tg, 
     }
 }
 
+#ifdef JHQ_SCAN_STATS
+}  // namespace
+__device__ unsigned long long g_scan_stats[8];
+namespace {   // pushes, inserts, flushes, runs, units
+#define SCAN_STAT(i, v) atomicAdd(&g_scan_stats[i], (unsigned long long)(v))
+#else
+#define SCAN_STAT(i, v) ((void)0)
+#endif
+
 // Per-warp exact top-ck of one query: s[0..ck_pad) sorted list,
 // s[ck_pad..merge_n) append buffer. thr = pruning bound (uniform in the warp).
 struct WarpTop {
@@ -194,6 +208,7 @@ struct WarpTop {
     // bound and pick up the tightest bound.
     __device__ __forceinline__ void flush(int lane, int ck, int ck_pad, int merge_n, uint64_t* tau) {
         const int cap = merge_n - ck_pad;
+        if (lane == 0) SCAN_STAT(2, 1);
         for (int i = count + lane; i < cap; i += 32) s[ck_pad + i] = KEY_EMPTY;
         __syncwarp();
         warp_bitonic_sort(s, merge_n, lane);
@@ -209,6 +224,7 @@ struct WarpTop {
                                          uint64_t* tau) {
         bool take = key < thr;
         unsigned mask = __ballot_sync(0xffffffffu, take);
+        if (lane == 0) { SCAN_STAT(0, 32); SCAN_STAT(1, __popc(mask)); }
         if (mask == 0) return;
         if (count + __popc(mask) > merge_n - ck_pad) {
             flush(lane, ck, ck_pad, merge_n, tau);
@@ -224,12 +240,15 @@ struct WarpTop {
 
 struct UnitInfo {
     int64_t pb, pe;          // physical page range
+    int list;
     int q[4];                // member queries (-1 = none)
     int64_t slot[4];         // candidate slot of each member
 };
 
+// Two CTAs per SM (registers capped at 128): the lookups are latency-bound
+// at 8 warps per SM.
 template <int G_T, int MODE>
-__global__ void __launch_bounds__(SCAN_THREADS, 1)
+__global__ void __launch_bounds__(SCAN_THREADS, JHQ_SCAN_MIN_BLOCKS)
 scan_kernel(ScanArgs a) {
     constexpr int QG = qg_of(MODE);
     constexpr int TROW = MODE == 0 ? 1024 : (QG == 1 ? 128 : 256 * (QG / 2));  // bytes per m
@@ -270,6 +289,30 @@ scan_kernel(ScanArgs a) {
 #pragma unroll
     for (int j = 0; j < QG; ++j) top[j].s = wl + ((size_t)warp * QG + j) * merge_n;
 
+    // A run = consecutive units of this CTA with the same list and query group
+    // (chunks of one list). The warps' top-ck lists live across the whole run;
+    // the merged result goes to the run's first slot, the other slots of the
+    // run get empty lists.
+    __shared__ int64_t run_slot[4];
+    __shared__ int run_list;
+    bool run_open = false;
+    auto close_run = [&]() {
+#pragma unroll
+        for (int j = 0; j < QG; ++j) top[j].flush(lane, a.ck, a.ck_pad, merge_n, tau + j);
+        for (int j = 0; j < QG; ++j) {
+            if (cur_q[j] < 0) continue;        // uniform across the block
+            __syncthreads();
+            for (int i = lane; i < a.ck_pad; i += 32) mrg[warp * a.ck_pad + i] = top[j].s[i];
+            __syncthreads();
+            block_bitonic_sort(mrg, SCAN_WARPS * a.ck_pad);
+            uint64_t* out = a.cand + run_slot[j] * a.ck;
+            for (int i = tid; i < a.ck; i += SCAN_THREADS) out[i] = mrg[i];
+            if (tid == 0 && mrg[a.ck - 1] != KEY_EMPTY)
+                atomicMin(reinterpret_cast<unsigned long long*>(a.gthr + cur_q[j]),
+                          (unsigned long long)mrg[a.ck - 1]);
+        }
+    };
+
     for (int u = u0; u < u1; ++u) {
         __syncthreads();                       // previous unit done with unit/tables/mrg
         if (tid == 0) {
@@ -281,6 +324,7 @@ scan_kernel(ScanArgs a) {
             const int b0 = a.bucket_off[lst], cnt = a.bucket_off[lst + 1] - b0;
             unit.pb = pages0 + (int64_t)ch * a.chunk_pages;
             unit.pe = min((int64_t)pages1, unit.pb + a.chunk_pages);
+            unit.list = lst;
             for (int j = 0; j < 4; ++j) {
                 unit.q[j] = -1;
                 unit.slot[j] = -1;
@@ -295,22 +339,38 @@ scan_kernel(ScanArgs a) {
         bool same = true;
 #pragma unroll
         for (int j = 0; j < QG; ++j) same = same && (unit.q[j] == cur_q[j]);
-        if (!same) {                           // tables of the new query group
-            for (int j = 0; j < QG; ++j) {
-                const int q = unit.q[j];
-                if (q >= 0)
-                    for (int i = tid; i < a.d; i += SCAN_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
-                __syncthreads();
-                build_tables<MODE>(tab, j, qs, c1d, a.d, a.M, a.Mp, a.B, q >= 0);
-                __syncthreads();
-            }
+        const bool cont = run_open && same && unit.list == run_list;
+        if (!cont) {
+            if (run_open) close_run();
             __syncthreads();
-            if (tid < QG) cur_q[tid] = unit.q[tid];
-        }
-        if (tid < QG) tau[tid] = unit.q[tid] >= 0 ? a.gthr[unit.q[tid]] : KEY_EMPTY;
-        __syncthreads();
+            if (!same) {                       // tables of the new query group
+                for (int j = 0; j < QG; ++j) {
+                    const int q = unit.q[j];
+                    if (q >= 0)
+                        for (int i = tid; i < a.d; i += SCAN_THREADS) qs[i] = a.q_rot[(int64_t)q * a.d + i];
+                    __syncthreads();
+                    build_tables<MODE>(tab, j, qs, c1d, a.d, a.M, a.Mp, a.B, q >= 0);
+                    __syncthreads();
+                }
+            }
+            if (tid < QG) {
+                cur_q[tid] = unit.q[tid];
+                run_slot[tid] = unit.slot[tid];
+                tau[tid] = unit.q[tid] >= 0 ? a.gthr[unit.q[tid]] : KEY_EMPTY;
+            }
+            if (tid == 0) run_list = unit.list;
+            __syncthreads();
 #pragma unroll
-        for (int j = 0; j < QG; ++j) top[j].reset(lane, merge_n, tau[j]);
+            for (int j = 0; j < QG; ++j) top[j].reset(lane, merge_n, tau[j]);
+            run_open = true;
+            if (tid == 0) SCAN_STAT(3, 1);
+        } else {                               // continuation: this unit's slots stay empty
+            for (int j = 0; j < QG; ++j) {
+                if (unit.q[j] < 0) continue;
+                uint64_t* out = a.cand + unit.slot[j] * a.ck;
+                for (int i = tid; i < a.ck; i += SCAN_THREADS) out[i] = KEY_EMPTY;
+            }
+        }
 
         // ---- score pages two at a time: warp w takes pb + 2*(w + W*i)
         const int64_t pb = unit.pb, pe = unit.pe;
@@ -347,23 +407,8 @@ scan_kernel(ScanArgs a) {
                             merge_n, tau + j);
             }
         }
-#pragma unroll
-        for (int j = 0; j < QG; ++j) top[j].flush(lane, a.ck, a.ck_pad, merge_n, tau + j);
-
-        // ---- per member: merge the warps' lists, write the slot, lower the bound
-        for (int j = 0; j < QG; ++j) {
-            if (unit.q[j] < 0) continue;       // uniform across the block
-            __syncthreads();
-            for (int i = lane; i < a.ck_pad; i += 32) mrg[warp * a.ck_pad + i] = top[j].s[i];
-            __syncthreads();
-            block_bitonic_sort(mrg, SCAN_WARPS * a.ck_pad);
-            uint64_t* out = a.cand + unit.slot[j] * a.ck;
-            for (int i = tid; i < a.ck; i += SCAN_THREADS) out[i] = mrg[i];
-            if (tid == 0 && mrg[a.ck - 1] != KEY_EMPTY)
-                atomicMin(reinterpret_cast<unsigned long long*>(a.gthr + unit.q[j]),
-                          (unsigned long long)mrg[a.ck - 1]);
-        }
     }
+    if (run_open) close_run();
 }
 
 template <int G_T, int MODE>
@@ -371,10 +416,15 @@ void launch_scan(const ScanArgs& a, size_t smem, cudaStream_t st) {
     scan_kernel<G_T, MODE><<<a.grid, SCAN_THREADS, smem, st>>>(a);
 }
 
+// Opt-in dynamic shared memory: the per-block limit (227 KB) minus the
+// kernel's static shared variables.
 template <int G_T, int MODE>
 void configure_one() {
+    cudaFuncAttributes fa;
+    JHQ_CUDA(cudaFuncGetAttributes(&fa, scan_kernel<G_T, MODE>));
     JHQ_CUDA(cudaFuncSetAttribute(scan_kernel<G_T, MODE>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  227 * 1024 - (int)fa.sharedSizeBytes));
 }
 
 template <int G_T, int MODE>
@@ -416,15 +466,18 @@ void scan_configure() {
             dispatch(g * 16, mode, [](auto G, auto Md) { configure_one<G.value, Md.value>(); return 0; });
 }
 
+// Query groups of 2 or 4 (float2 tables) issue fewer instructions per lookup
+// but measured slower on B200 than one query per lane (C1: 7.4 / 11.4 ms vs
+// 6.4 ms per 1,000 queries), so one query per unit is the default; the wider
+// groups stay selectable (JHQ_SCAN_MODE) for tuning.
 int scan_mode_for(int d, int M, int B, double queries_per_list) {
-    if (!nibble_split(d, M, B)) return 0;
-    if (queries_per_list >= 3.0) return 4;
-    if (queries_per_list >= 1.5) return 2;
-    return 1;
+    (void)queries_per_list;
+    return nibble_split(d, M, B) ? 1 : 0;
 }
 
 size_t scan_smem_bytes(int Mp, int d, int ck_pad, int mode) {
-    return scan_smem_layout(Mp, d, ck_pad, mode).total;
+    // reported with the static-variable reserve, so callers compare with 227 KB
+    return scan_smem_layout(Mp, d, ck_pad, mode).total + 1024;
 }
 
 int scan_grid_for(int Mp, int d, int ck_pad, int mode) {
@@ -439,10 +492,21 @@ int scan_grid_for(int Mp, int d, int ck_pad, int mode) {
 
 void scan_topck(const ScanArgs& a, cudaStream_t st) {
     const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad, a.mode).total;
-    if (smem > 227 * 1024) fail(JHQ_EINVAL, "scan: shared-memory tables too large (reduce M)");
+    if (smem > SCAN_SMEM_LIMIT) fail(JHQ_EINVAL, "scan: shared-memory tables too large (reduce M)");
     dispatch(a.Mp, a.mode, [&](auto G, auto Md) { launch_scan<G.value, Md.value>(a, smem, st); return 0; });
     JHQ_LAUNCH_CHECK();
     count_launch();
 }
 
 }  // namespace jhq
+
+#ifdef JHQ_SCAN_STATS
+extern "C" int jhq_debug_scan_stats(unsigned long long* out, int reset) {
+    cudaMemcpyFromSymbol(out, jhq::g_scan_stats, sizeof(unsigned long long) * 8);
+    if (reset) {
+        unsigned long long z[8] = {};
+        cudaMemcpyToSymbol(jhq::g_scan_stats, z, sizeof z);
+    }
+    return 0;
+}
+#endif
