@@ -279,6 +279,24 @@ def run_ours(args):
                "sample": f"{ns} of the {nq} C1 queries against the same 100k index "
                          f"({dt:.1f} s, OpenMP over queries)"}
 
+    # ---- the reference's own CUDA build (v14, flat via nlist=1), same data
+    ref_cuda = None
+    if ws == 1 and not args.no_ref_cuda:
+        try:
+            from oracle import RefGPU
+            r = RefGPU("v14")
+            Dr, Ir, tm = r.run(base, queries, M=CFG["M"], B=CFG["B"], Br=CFG["Br"],
+                               alpha=CFG["alpha"], k=k, nlist=1, nprobe=1, batch=CFG["batch"])
+            ref_cuda = {"build": "reference jhq_v14_streaming_add (nvcc sm_100a, its CMake "
+                                 "flags), nlist=1 nprobe=1 batch 64",
+                        "qps": round(nq / (tm["search_ms"] / 1000.0), 1),
+                        "recall_at_10": round(datasets.recall_at_k(Ir, gt, k), 4),
+                        "timing": "mean wall time of 5 search() calls after one warm-up, "
+                                  "host buffers (the reference demo's method)",
+                        "train_ms": round(tm["train_ms"], 1)}
+        except Exception as e:                      # not built / not runnable here
+            ref_cuda = {"unavailable": str(e)[:200]}
+
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "QPS", "n_gpus": ws,
         "steps": args.steps, "warmup": max(3, args.warmup),
@@ -296,7 +314,7 @@ def run_ours(args):
                      "algorithmic_bytes_per_step": int(scan_bytes),
                      "launches_per_step": nbatch},
         "stage_ms_per_step": {kk: round(v / args.steps, 4) for kk, v in stages.items()},
-        "clocks": clocks, "cpu_baseline": cpu,
+        "clocks": clocks, "cpu_baseline": cpu, "reference_cuda": ref_cuda,
         "train_s": round(t_train, 2), "add_s": round(t_add, 3),
     }
     print(json.dumps(out), flush=True)
@@ -391,6 +409,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--no-ref-cuda", action="store_true",
+                    help="skip timing the reference's own CUDA build (oracle/_ref)")
     ap.add_argument("--profile-run", action="store_true",
                     help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)

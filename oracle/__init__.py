@@ -230,3 +230,34 @@ class RefCPU:
         out = np.zeros(Kr, np.float32)
         n = self.L.ref_kmeans1d(vals, vals.size, Kr, max_iter, out)
         return out[:n]
+
+
+class RefGPU:
+    """The reference's own CUDA JHQGpuIndex (v14 or v1), built from its sources by
+    `make -C oracle ref_gpu`, driven through its public train/add/search API."""
+
+    def __init__(self, version: str = "v14"):
+        path = os.path.join(HERE, "_ref", f"libref_{version}.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = C.CDLL(path)
+        dp = C.POINTER(C.c_double)
+        L.ref_gpu_run.argtypes = [_f32p, C.c_int, C.c_int, _f32p, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_int, _f32p, _i32p, dp, dp, dp]
+        self.L = L
+        self.version = version
+
+    def run(self, x, q, *, M, B=8, Br=4, alpha=4.0, k=10, nlist=1, nprobe=1, batch=64,
+            reps=5, n_train=None):
+        x, q = _f32(x), _f32(q)
+        n, d = x.shape
+        nt = min(n, 100_000) if n_train is None else n_train
+        D = np.zeros((len(q), k), np.float32)
+        I = np.zeros((len(q), k), np.int32)
+        tr, ad, se = C.c_double(), C.c_double(), C.c_double()
+        rc = self.L.ref_gpu_run(x, n, nt, q, len(q), d, M, B, Br, alpha, k, nlist, nprobe, batch,
+                                reps, D, I, C.byref(tr), C.byref(ad), C.byref(se))
+        if rc != 0:
+            raise RuntimeError(f"reference {self.version} run failed")
+        return D, I, dict(train_ms=tr.value, add_ms=ad.value, search_ms=se.value)

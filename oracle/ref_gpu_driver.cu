@@ -1,0 +1,44 @@
+// Test/baseline infrastructure (oracle/_ref only): a C-ABI shim that runs the
+// reference's own CUDA index (jhq_gpu::JHQGpuIndex of the version directory
+// this file is compiled against, e.g. jhq_v14_streaming_add or jhq_v1_plain)
+// through its public API — train, add, one warm-up search, then timed
+// searches — exactly as the reference's demo mains do
+// (examples/demo_jhq_v14_streaming_add.cu:78-106). Built by oracle/Makefile
+// from the reference tree; the product never links it.
+#include <chrono>
+#include <cstring>
+#include <exception>
+#include <vector>
+
+#include REF_INDEX_HEADER
+
+extern "C" int ref_gpu_run(const float* x, int n, int n_train, const float* q, int nq, int d,
+                           int M, int B, int Br, float alpha, int k, int nlist, int nprobe,
+                           int batch, int reps, float* out_d, int* out_i,
+                           double* train_ms, double* add_ms, double* search_ms) {
+    using Clock = std::chrono::high_resolution_clock;
+    using Ms = std::chrono::duration<double, std::milli>;
+    try {
+        jhq_gpu::JHQGpuIndex::Params p;
+        p.M = M; p.B = B; p.Br = Br; p.alpha = alpha;
+#ifdef REF_HAS_IVF
+        p.nlist = nlist; p.nprobe = nprobe; p.batch_size = batch;
+#else
+        (void)nlist; (void)nprobe; (void)batch;
+#endif
+        jhq_gpu::JHQGpuIndex idx(d, p);
+        auto t0 = Clock::now();
+        idx.train(x, n_train);
+        *train_ms = Ms(Clock::now() - t0).count();
+        t0 = Clock::now();
+        idx.add(x, n);
+        *add_ms = Ms(Clock::now() - t0).count();
+        idx.search(q, nq, k, out_d, out_i);               // warm-up (graph capture)
+        t0 = Clock::now();
+        for (int r = 0; r < reps; ++r) idx.search(q, nq, k, out_d, out_i);
+        *search_ms = Ms(Clock::now() - t0).count() / reps;
+        return 0;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}
