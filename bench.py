@@ -255,6 +255,8 @@ def run_ours(args):
     peak, peak_kind = peaks()
     achieved = scan_bytes / (scan_ms / 1000.0) / 1e9
     nbatch = -(-nq // CFG["batch"])
+    # DRAM bytes of one scan launch from the committed ncu capture (per launch,
+    # like achieved below: achieved is algorithmic bytes per launch / launch time)
     traffic = None
     tr_path = os.path.join(ROOT, "profiles", "scan_c1_traffic.json")
     if os.path.exists(tr_path):
