@@ -75,11 +75,13 @@ class Params:
 _lib: Optional[C.CDLL] = None
 
 
-def load_library(path: str = LIB_PATH) -> C.CDLL:
-    """Load libjhq_b200.so (raises if it has not been built)."""
+def load_library(path: str = "") -> C.CDLL:
+    """Load libjhq_b200.so (raises if it has not been built). The JHQ_LIBRARY
+    environment variable selects another build of the same library."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("JHQ_LIBRARY") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(f"{path} is missing: run `python -m jhq_gpu_b200.build` "
                            "(the CUDA library is required; there is no CPU fallback)")

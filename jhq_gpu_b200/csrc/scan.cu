@@ -28,7 +28,7 @@
 //      The entry is formed as lo + hi before it is added, so every distance is
 //      bit-identical to the byte-LUT sum. Other bit widths keep the byte LUT
 //      (one query per unit);
-//   2. lets each warp score pages two at a time: lane = slot, one distance per
+//   2. lets each warp score PPW pages at a time: lane = slot, one distance per
 //      query of the group, each the in-order sum over m (search.cu:146-151).
 //      The nibble offsets of four codes come from two shift+mask ops and one
 //      byte-permute per code, shared by all queries of the group;
@@ -53,9 +53,13 @@ namespace jhq {
 namespace {
 
 #ifndef JHQ_SCAN_MIN_BLOCKS
-#define JHQ_SCAN_MIN_BLOCKS 2
+#define JHQ_SCAN_MIN_BLOCKS 3
+#endif
+#ifndef JHQ_SCAN_PPW
+#define JHQ_SCAN_PPW 1
 #endif
 constexpr int SCAN_THREADS = 256;
+constexpr int PPW = JHQ_SCAN_PPW;                      // pages per warp step
 constexpr int SCAN_WARPS = SCAN_THREADS / 32;
 constexpr size_t SCAN_SMEM_LIMIT = 227 * 1024 - 1024;   // dynamic bytes left after statics
 
@@ -245,8 +249,8 @@ struct UnitInfo {
     int64_t slot[4];         // candidate slot of each member
 };
 
-// Two CTAs per SM (registers capped at 128): the lookups are latency-bound
-// at 8 warps per SM.
+// Three CTAs per SM (registers capped at 85): the lookups are latency-bound;
+// measured on C1, 2 / 3 / 4 CTAs per SM give 6.36 / 5.78 / 6.53 ms per step.
 template <int G_T, int MODE>
 __global__ void __launch_bounds__(SCAN_THREADS, JHQ_SCAN_MIN_BLOCKS)
 scan_kernel(ScanArgs a) {
@@ -372,39 +376,44 @@ scan_kernel(ScanArgs a) {
             }
         }
 
-        // ---- score pages two at a time: warp w takes pb + 2*(w + W*i)
+        // ---- score PPW pages at a time: warp w takes pb + PPW*(w + W*i)
         const int64_t pb = unit.pb, pe = unit.pe;
-        for (int64_t pg = pb + 2 * warp; pg < pe; pg += 2 * SCAN_WARPS) {
-            const bool v1 = pg + 1 < pe;
-            const int32_t id0 = __ldg(a.slot_ids + pg * 32 + lane);
-            const int32_t id1 = v1 ? __ldg(a.slot_ids + (pg + 1) * 32 + lane) : -1;
-            float d0[QG], d1[QG];
+        for (int64_t pg = pb + PPW * warp; pg < pe; pg += PPW * SCAN_WARPS) {
+            int32_t id[PPW];
+            float dd[PPW][QG];
+            const uint4* pp[PPW];
+            uint4 cur[PPW];
 #pragma unroll
-            for (int j = 0; j < QG; ++j) { d0[j] = 0.0f; d1[j] = 0.0f; }
-            const uint4* p0 = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
-            const uint4* p1 = p0 + G * 32;
-            // group g+1 of both pages is in flight while group g is looked up
-            uint4 c0 = __ldg(p0), c1 = v1 ? __ldg(p1) : make_uint4(0, 0, 0, 0);
+            for (int u = 0; u < PPW; ++u) {
+                const bool ok = pg + u < pe;
+                id[u] = ok ? __ldg(a.slot_ids + (pg + u) * 32 + lane) : -1;
+                pp[u] = reinterpret_cast<const uint4*>(a.pages) + (pg + u) * G * 32 + lane;
+                cur[u] = ok ? __ldg(pp[u]) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int j = 0; j < QG; ++j) dd[u][j] = 0.0f;
+            }
+            // group g+1 of every page is in flight while group g is looked up
 #pragma unroll (G_T > 0 ? G_T : 1)
             for (int g = 0; g < G; ++g) {
-                uint4 n0 = c0, n1 = c1;
-                if (g + 1 < G) {
-                    n0 = __ldg(p0 + (g + 1) * 32);
-                    if (v1) n1 = __ldg(p1 + (g + 1) * 32);
+                uint4 nxt[PPW];
+#pragma unroll
+                for (int u = 0; u < PPW; ++u) {
+                    nxt[u] = cur[u];
+                    if (g + 1 < G && pg + u < pe) nxt[u] = __ldg(pp[u] + (g + 1) * 32);
                 }
                 const unsigned char* tg = smem + (size_t)g * 16 * TROW;
-                add_group<MODE>(d0, tg, c0);
-                add_group<MODE>(d1, tg, c1);
-                c0 = n0;
-                c1 = n1;
+#pragma unroll
+                for (int u = 0; u < PPW; ++u) add_group<MODE>(dd[u], tg, cur[u]);
+#pragma unroll
+                for (int u = 0; u < PPW; ++u) cur[u] = nxt[u];
             }
 #pragma unroll
             for (int j = 0; j < QG; ++j) {
                 if (unit.q[j] < 0) continue;
-                top[j].push(id0 >= 0 ? make_key(d0[j], id0) : KEY_EMPTY, lane, a.ck, a.ck_pad,
-                            merge_n, tau + j);
-                top[j].push(id1 >= 0 ? make_key(d1[j], id1) : KEY_EMPTY, lane, a.ck, a.ck_pad,
-                            merge_n, tau + j);
+#pragma unroll
+                for (int u = 0; u < PPW; ++u)
+                    top[j].push(id[u] >= 0 ? make_key(dd[u][j], id[u]) : KEY_EMPTY, lane, a.ck,
+                                a.ck_pad, merge_n, tau + j);
             }
         }
     }
