@@ -388,6 +388,105 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+C2 = dict(n=1_000_000, nq=10_000, d=1024, M=128, B=8, Br=4, alpha=4.0, k=10, nlist=1024,
+          batch=256, nprobes=(8, 16, 32, 64, 128), seed=0)
+
+
+def run_c2(args):
+    """BASELINE configs[2] (C2): IVF-JHQ, 1M base + 10k queries, D=1024 normalised GMM
+    (4,096 components), nlist 1,024 by k-means on a 100k sample, nprobe sweep
+    {8..128}, M=128 B=8 Br=4 alpha=4 k=10, query batch 256. One JSON line with
+    per-nprobe QPS / recall for this build and for the reference's own v14 build."""
+    import torch
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200 import datasets
+    dev = torch.device("cuda", 0)
+    base, queries = datasets.make("c2", seed=C2["seed"])
+    nq, k, M = len(queries), C2["k"], C2["M"]
+    p = J.Params(M=M, B=C2["B"], Br=C2["Br"], alpha=C2["alpha"], nlist=C2["nlist"],
+                 nprobe=max(C2["nprobes"]), batch_size=C2["batch"], device=0)
+    idx = J.JHQGpuIndex(C2["d"], p)
+    t0 = time.perf_counter(); idx.train(base[:100_000]); t_train = time.perf_counter() - t0
+    t0 = time.perf_counter(); idx.add(base); t_add = time.perf_counter() - t0
+    gt = datasets.ground_truth_torch(base, queries, k)
+    # probed vectors per query (for the algorithmic code bytes of the scan)
+    t = idx.get_trained()
+    _, _, _, asg = idx.get_codes()
+    sizes = np.bincount(asg, minlength=C2["nlist"]).astype(np.int64)
+    qr = torch.from_numpy(idx.rotate(queries)).to(dev)
+    ct = torch.from_numpy(t["cents"]).to(dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    score = (ct * ct).sum(1)[None, :] - 2.0 * qr @ ct.T
+    order = score.argsort(dim=1).cpu().numpy()
+    q_dev = torch.from_numpy(queries).to(dev)
+    D = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    I = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    peak, peak_kind = peaks()
+    sweep = []
+    for npb in C2["nprobes"]:
+        idx.set_nprobe(npb)
+        for _ in range(args.warmup):
+            idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(), stream.cuda_stream)
+        torch.cuda.synchronize()
+        ms = 0.0
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(), stream.cuda_stream)
+            e.record(stream)
+            torch.cuda.synchronize()
+            ms += a.elapsed_time(e)
+        rec = datasets.recall_at_k(I.cpu().numpy(), gt, k)
+        t0 = time.perf_counter()
+        idx.search(queries, k)
+        e2e = nq / (time.perf_counter() - t0)
+        idx.set_profiling(True)
+        idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(), stream.cuda_stream)
+        torch.cuda.synchronize()
+        st, _ = idx.stage_times()
+        idx.set_profiling(False)
+        probed = sizes[order[:, :npb]].sum()
+        code_bytes = probed * M * C2["B"] / 8
+        ach = code_bytes / (st["scan"] / 1000.0) / 1e9
+        sweep.append({"nprobe": npb, "qps": round(args.steps * nq / (ms / 1000.0), 1),
+                      "e2e_qps": round(e2e, 1), "recall_at_10": round(rec, 4),
+                      "stage_ms_per_search": {kk: round(v, 3) for kk, v in st.items()},
+                      "scan_achieved_gbs": round(ach, 1), "scan_frac": round(ach / peak, 4),
+                      "code_bytes_per_query": int(code_bytes / nq)})
+    ref = None
+    if not args.no_ref_cuda:
+        try:
+            from oracle import RefGPU
+            Ir, sms, tm = RefGPU("v14").sweep(base, queries, M=M, nlist=C2["nlist"],
+                                               nprobes=C2["nprobes"], batch=C2["batch"])
+            ref = [{"nprobe": npb, "qps": round(nq / (s / 1000.0), 1),
+                    "recall_at_10": round(datasets.recall_at_k(Ir[i], gt, k), 4)}
+                   for i, (npb, s) in enumerate(zip(C2["nprobes"], sms))]
+            ref = {"build": "reference jhq_v14_streaming_add (nvcc sm_100a, its CMake flags)",
+                   "timing": "mean wall time of 3 search() calls after one warm-up, host buffers",
+                   "train_ms": round(tm["train_ms"], 1), "sweep": ref}
+        except Exception as ex:
+            ref = {"unavailable": str(ex)[:200]}
+    ok = [s for s in sweep if s["recall_at_10"] >= 0.95]
+    best = max(ok, key=lambda s: s["qps"]) if ok else None
+    out = {"metric": "QPS at recall@10>=0.95 (C2 IVF-JHQ, 1M x 1024, nlist 1024, 1 B200)",
+           "value": best["qps"] if best else None, "unit": "QPS", "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+           "dtype": "u8 codes / f32 accumulate", "vs_baseline": None,
+           "data": "synthetic (seeded normalised Gaussian mixture, BASELINE configs[2] shape)",
+           "config": {"workload": "C2 IVF-JHQ 1M + 10k, D=1024, GMM(4096, 0.35), nlist 1024 "
+                                  "(k-means on 100k), M=128 B=8 Br=4 alpha=4 k=10, batch 256",
+                      "l2": "flushed (256 MiB write) before every timed step"},
+           "operating_point": best, "sweep": sweep, "reference_cuda": ref,
+           "peak_gbs": peak, "peak_kind": peak_kind,
+           "train_s": round(t_train, 1), "add_s": round(t_add, 2)}
+    print(json.dumps(out), flush=True)
+
+
 def run_profile_case(args):
     """Short C1 run for ncu: train on 20k rows, add all 100k, one warm-up search
     (16 batches) and one search to capture — nothing else launches kernels."""
@@ -413,11 +512,15 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-ref-cuda", action="store_true",
                     help="skip timing the reference's own CUDA build (oracle/_ref)")
+    ap.add_argument("--config", choices=["c1", "c2"], default="c1",
+                    help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep")
     ap.add_argument("--profile-run", action="store_true",
                     help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)
     if args.profile_run:
         run_profile_case(args)
+    elif args.config == "c2":
+        run_c2(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -97,6 +97,11 @@ int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int 
  * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
 int jhq_synchronize(jhq_index* idx, double timeout_s);
 
+/* Changes the number of probed lists of later searches (clamped to nlist,
+ * like the constructor, jhq_gpu_index.cu:128). The reference fixes nprobe at
+ * construction; this allows an nprobe sweep on one trained index. */
+int jhq_set_nprobe(jhq_index* idx, int nprobe);
+
 /* Accessors: JHQGpuIndex::ntotal() / dim() (jhq_gpu_index.cuh:44-45). */
 int jhq_ntotal(const jhq_index* idx, int64_t* n);
 int jhq_dim(const jhq_index* idx, int* d);

@@ -35,7 +35,7 @@ EXPORTED = [
     "jhq_encode", "jhq_save", "jhq_load", "jhq_merge_shards", "jhq_kernel_launches",
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
-    "jhq_search_device_noalloc",
+    "jhq_search_device_noalloc", "jhq_set_nprobe",
 ]
 STAGES = ["rotate", "coarse+probes", "plan", "scan", "refine"]
 
@@ -97,6 +97,7 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_search_device.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_search_device_noalloc.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_synchronize.argtypes = [vp, C.c_double]
+    L.jhq_set_nprobe.argtypes = [vp, C.c_int]
     L.jhq_ntotal.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_dim.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_is_trained.argtypes = [vp, C.POINTER(C.c_int)]
@@ -244,6 +245,11 @@ class JHQGpuIndex:
         in a fixed 16 MiB array inside the library (for callers that must not
         allocate while serving). Calls that overlap on the GPU race; serialise them."""
         _check(self._L.jhq_search_device_noalloc(self._h, q_ptr, nq, k, d_ptr, i_ptr, stream))
+
+    def set_nprobe(self, nprobe: int) -> None:
+        """Probe count of later searches (clamped to nlist)."""
+        _check(self._L.jhq_set_nprobe(self._h, nprobe))
+        self.params.nprobe = min(nprobe, self.params.nlist)
 
     def synchronize(self, timeout_s: float = 60.0) -> None:
         _check(self._L.jhq_synchronize(self._h, timeout_s))

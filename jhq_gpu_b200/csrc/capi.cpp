@@ -119,6 +119,10 @@ int jhq_synchronize(jhq_index* idx, double timeout_s) {
     return guarded([&] { need(idx)->synchronize(timeout_s); });
 }
 
+int jhq_set_nprobe(jhq_index* idx, int nprobe) {
+    return guarded([&] { need(idx)->set_nprobe(nprobe); });
+}
+
 int jhq_ntotal(const jhq_index* idx, int64_t* n) {
     return guarded([&] {
         if (!n) jhq::fail(JHQ_EINVAL, "null output");

@@ -590,6 +590,15 @@ void Index::search_device(const float* d_q, int64_t nq, int k, float* d_dists, i
     }
 }
 
+void Index::set_nprobe(int nprobe) {
+    DeviceGuard g(dev_);
+    if (nprobe <= 0) fail(JHQ_EINVAL, "nprobe must be positive");
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    p_.nprobe = std::min(nprobe, p_.nlist);
+    destroy_graph();
+    ws_.batch_cap = 0;                         // workspace and graph are rebuilt
+}
+
 void Index::synchronize(double timeout_s) {
     DeviceGuard g(dev_);
     auto t0 = std::chrono::steady_clock::now();

@@ -50,6 +50,7 @@ public:
     void search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_dists,
                                int32_t* d_ids, cudaStream_t stream);
     void synchronize(double timeout_s);
+    void set_nprobe(int nprobe);
 
     int64_t ntotal() const { return ntotal_; }
     int dim() const { return d_; }

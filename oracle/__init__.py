@@ -261,3 +261,25 @@ class RefGPU:
         if rc != 0:
             raise RuntimeError(f"reference {self.version} run failed")
         return D, I, dict(train_ms=tr.value, add_ms=ad.value, search_ms=se.value)
+
+    def sweep(self, x, q, *, M, nlist, nprobes, B=8, Br=4, alpha=4.0, k=10, batch=256, reps=3,
+              n_train=None):
+        """IVF nprobe sweep on one trained reference index (v14 only)."""
+        x, q = _f32(x), _f32(q)
+        n, d = x.shape
+        nt = min(n, 100_000) if n_train is None else n_train
+        nps = np.ascontiguousarray(nprobes, np.int32)
+        I = np.zeros((len(nps), len(q), k), np.int32)
+        ms = np.zeros(len(nps), np.float64)
+        tr, ad = C.c_double(), C.c_double()
+        L = self.L
+        L.ref_gpu_sweep.argtypes = [_f32p, C.c_int, C.c_int, _f32p, C.c_int, C.c_int, C.c_int,
+                                    C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, _i32p, C.c_int,
+                                    C.c_int, C.c_int, _i32p, C.POINTER(C.c_double),
+                                    C.POINTER(C.c_double),
+                                    np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        rc = L.ref_gpu_sweep(x, n, nt, q, len(q), d, M, B, Br, alpha, k, nlist, nps, len(nps),
+                             batch, reps, I.reshape(-1), C.byref(tr), C.byref(ad), ms)
+        if rc != 0:
+            raise RuntimeError("reference sweep failed")
+        return I, ms, dict(train_ms=tr.value, add_ms=ad.value)
