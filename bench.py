@@ -487,6 +487,132 @@ def run_c2(args):
     print(json.dumps(out), flush=True)
 
 
+SHARDED = {
+    "c3": dict(d=128, M=32, nlist=65_536, nprobe=64, n=100_000_000, nq=10_000, batch=10_000,
+               workload="C3 IVF-JHQ 100M uint8 D=128, GMM(16384) centres U(0,120) sigma 18, "
+                        "nlist 65536 nprobe 64, M=32 B=8 Br=4 alpha=4 k=10"),
+    "c4": dict(d=104, M=26, nlist=65_536, nprobe=64, n=100_000_000, nq=10_000, batch=10_000,
+               workload="C4 IVF-JHQ 100M int8 D=100 padded to 104, Student-t(4) GMM(16384), "
+                        "nlist 65536 nprobe 64, M=26 B=8 Br=4 alpha=4 k=10"),
+}
+
+
+def run_sharded(args):
+    """BASELINE configs[3]/[4]: the database is split in contiguous id ranges over the
+    ranks (one process per GPU); every rank trains the same index (deterministic) on
+    the first 100k rows, adds its shard, searches all queries; per-shard top-k lists
+    are all-gathered over NCCL and merged on the device (jhq_merge_shards)."""
+    import torch
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200 import datasets
+    from jhq_gpu_b200.sharded import ShardedSearch, contiguous_shard, index_local_search
+    cfg = SHARDED[args.config]
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    n = args.n or cfg["n"]
+    nq, k = cfg["nq"], 10
+    lo, hi = contiguous_shard(n, ws, rank)
+    p = J.Params(M=cfg["M"], B=8, Br=4, alpha=4.0, nlist=cfg["nlist"], nprobe=cfg["nprobe"],
+                 batch_size=cfg["batch"], add_batch=1 << 20, device=local)
+    idx = J.JHQGpuIndex(cfg["d"], p)
+    t0 = time.perf_counter()
+    idx.train(datasets.rows_torch(args.config, 0, min(n, 100_000), dev).cpu().numpy())
+    t_train = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    step = 2_000_000
+    for s in range(lo, hi, step):
+        idx.add(datasets.rows_torch(args.config, s, min(hi, s + step), dev).cpu().numpy())
+    t_add = time.perf_counter() - t0
+    q_dev = datasets.rows_torch(args.config, 0, nq, dev, sub=2)
+    # exact ground truth of this shard (fp64 distances of exact integers), then merged
+    qd = q_dev.double()
+    qn = (qd * qd).sum(1, keepdim=True)
+    bd = torch.full((nq, k), float("inf"), dtype=torch.float64, device=dev)
+    bi = torch.full((nq, k), -1, dtype=torch.int64, device=dev)
+    for s in range(lo, hi, 50_000):
+        x = datasets.rows_torch(args.config, s, min(hi, s + 50_000), dev).double()
+        dd = qn - 2.0 * qd @ x.T + (x * x).sum(1)[None, :]
+        ids = torch.arange(s, s + x.shape[0], device=dev).expand(nq, -1)
+        cd, pos = torch.cat([bd, dd], 1).topk(k, dim=1, largest=False)
+        bi = torch.cat([bi, ids], 1).gather(1, pos)
+        bd = cd
+    if ws > 1:
+        import torch.distributed as dist
+        gd = [torch.empty_like(bd) for _ in range(ws)]
+        gi = [torch.empty_like(bi) for _ in range(ws)]
+        dist.all_gather(gd, bd)
+        dist.all_gather(gi, bi)
+        cd, pos = torch.cat(gd, 1).topk(k, dim=1, largest=False)
+        bi = torch.cat(gi, 1).gather(1, pos)
+    gt = bi.cpu().numpy().astype(np.int32)
+    del qd, bd
+
+    D = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    I = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)          # a real stream: handle 0 means "index's own"
+    ss = ShardedSearch(index_local_search(idx), lo) if ws > 1 else None
+
+    def search():
+        with torch.cuda.stream(stream):
+            if ss is None:
+                idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(),
+                                  stream.cuda_stream)
+                return D, I
+            return ss.search(q_dev, k, stream)
+
+    def barrier():
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(1, args.warmup)):
+        Dr, Ir = search()
+    torch.cuda.synchronize(dev)
+    recall = datasets.recall_at_k(Ir.cpu().numpy(), gt, k)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev = []
+    for _ in range(args.steps):
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        search()
+        e.record(stream)
+        ev.append((a, e))
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(e) for a, e in ev)
+    barrier()
+    idx.set_profiling(True)
+    search()
+    torch.cuda.synchronize(dev)
+    st, _ = idx.stage_times()
+    idx.set_profiling(False)
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        out = {"metric": f"QPS (C{args.config[1]} sharded IVF-JHQ, {n // 1_000_000}M vectors)",
+               "value": round(args.steps * nq / (ms / 1000.0), 1), "unit": "QPS", "n_gpus": ws,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "u8 codes / f32 accumulate",
+               "data": "synthetic (seeded, generated on the GPU per 500k-row block)",
+               "config": {"workload": cfg["workload"], "n_base": n, "n_queries": nq,
+                          "batch": cfg["batch"], "parallelism": f"db shards x{ws}"},
+               "recall_at_10": round(recall, 4), "stage_ms_rank0": {kk: round(v, 3) for kk, v in st.items()},
+               "train_s": round(t_train, 1), "add_s_rank0": round(t_add, 1),
+               "shard_vectors_rank0": hi - lo}
+        print(json.dumps(out), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def run_profile_case(args):
     """Short C1 run for ncu: train on 20k rows, add all 100k, one warm-up search
     (16 batches) and one search to capture — nothing else launches kernels."""
@@ -512,8 +638,10 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--no-ref-cuda", action="store_true",
                     help="skip timing the reference's own CUDA build (oracle/_ref)")
-    ap.add_argument("--config", choices=["c1", "c2"], default="c1",
-                    help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep")
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4"], default="c1",
+                    help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep; "
+                         "c3 / c4 = 100M-vector sharded IVF (one process per GPU)")
+    ap.add_argument("--n", type=int, default=0, help="c3/c4: database size (default 100M)")
     ap.add_argument("--profile-run", action="store_true",
                     help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)
@@ -521,6 +649,8 @@ def main(argv=None):
         run_profile_case(args)
     elif args.config == "c2":
         run_c2(args)
+    elif args.config in ("c3", "c4"):
+        run_sharded(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

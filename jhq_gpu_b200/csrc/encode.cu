@@ -1,5 +1,5 @@
-// encode.cu — database-side kernels of add(): primary + residual encode,
-// IVF assignment and the scatter of primary codes into the page layout.
+// encode.cu — database-side kernels of add(): primary + residual encode
+// and the scatter of primary codes into the page layout.
 //
 // encode_kernel restates primary_encode_kernel + residual_encode_kernel
 // (jhq_v14_streaming_add/encode.cu:20-86) as one pass over each rotated row:
@@ -69,27 +69,6 @@ __global__ void encode_kernel(const float* __restrict__ y, int64_t n, int d, int
     corr[v] = 2.0f * dot;
 }
 
-// Warp per row: first minimum of s[row][0..nlist) (assign_from_dots_kernel,
-// jhq_gpu_index.cu:23-39: strict <, lowest list id wins ties).
-__global__ void argmin_kernel(const float* __restrict__ s, int64_t n, int nlist, int32_t* assign) {
-    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
-    const int lane = threadIdx.x & 31;
-    if (row >= n) return;
-    const float* sr = s + row * nlist;
-    float best = __int_as_float(0x7f800000);
-    int bi = 0x7fffffff;
-    for (int c = lane; c < nlist; c += 32) {
-        float v = sr[c];
-        if (v < best) { best = v; bi = c; }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov < best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    if (lane == 0) assign[row] = (bi == 0x7fffffff) ? 0 : bi;
-}
-
 // Thread per (slot, 16-byte group): pages[p][g][lane][0..15].
 __global__ void scatter_pages_kernel(const int32_t* __restrict__ slot_ids, int64_t nslots,
                                      const uint8_t* __restrict__ pcodes, int M, int Mp,
@@ -132,13 +111,6 @@ void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
     if (n <= 0) return;
     encode_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, s>>>(y, n, d, M, B, Br, c1d, res_c1d,
                                                              pcodes, rcodes, bpv_pad, corr);
-    JHQ_LAUNCH_CHECK();
-    count_launch();
-}
-
-void argmin_rows(const float* s, int64_t n, int nlist, int32_t* assign, cudaStream_t st) {
-    if (n <= 0) return;
-    argmin_kernel<<<(unsigned)ceil_div(n * 32, 256), 256, 0, st>>>(s, n, nlist, assign);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

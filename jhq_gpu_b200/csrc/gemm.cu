@@ -110,6 +110,94 @@ gemm_tiled_kernel(const float* __restrict__ A, const float* __restrict__ B, floa
     }
 }
 
+// Fused assignment: argmin_n (norms[n] - 2 <A_r, B[:, n]>) over all N columns
+// without materialising the scores (assign_from_dots_kernel semantics,
+// jhq_gpu_index.cu:23-39: strict <, lowest column wins ties). CTA = 128 rows;
+// it sweeps the columns in 128-wide tiles with the same 8x8-per-thread fma
+// chains as gemm_tiled_kernel, keeps a running (best, index) per thread-row,
+// then reduces the 16 threads that share a row.
+__global__ void __launch_bounds__(256)
+gemm_argmin_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                   const float* __restrict__ norms, int64_t R, int K, int N,
+                   int32_t* __restrict__ out) {
+    __shared__ float As[TBK][TBM + 4];
+    __shared__ float Bs[TBK][TBN + 4];
+    __shared__ float red_v[TBM][17];
+    __shared__ int red_i[TBM][17];
+    const int tid = threadIdx.x, tx = tid % 16, ty = tid / 16;
+    const int64_t r0 = (int64_t)blockIdx.x * TBM;
+    float best[8];
+    int bidx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { best[i] = __int_as_float(0x7f800000); bidx[i] = 0x7fffffff; }
+    for (int n0 = 0; n0 < N; n0 += TBN) {
+        float acc[8][8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+        for (int k0 = 0; k0 < K; k0 += TBK) {
+            {
+                int r = tid / 2, kq = (tid % 2) * 4;
+                int64_t gr = r0 + r;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    int gk = k0 + kq + t;
+                    As[kq + t][r] = (gr < R && gk < K) ? A[gr * K + gk] : 0.0f;
+                }
+            }
+            {
+                int kr = tid / 32, nq = (tid % 32) * 4;
+                int gk = k0 + kr;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    int gn = n0 + nq + t;
+                    Bs[kr][nq + t] = (gk < K && gn < N) ? B[(int64_t)gk * N + gn] : 0.0f;
+                }
+            }
+            __syncthreads();
+            const int kmax = min(TBK, K - k0);
+            for (int kk = 0; kk < kmax; ++kk) {
+                float a[8], b[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a[i] = As[kk][ty * 8 + i];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) b[j] = Bs[kk][tx * 8 + j];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {            // columns ascending within the thread
+            const int gn = n0 + tx * 8 + j;
+            if (gn >= N) break;
+            const float nb = norms[gn];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float sc = nb - 2.0f * acc[i][j];
+                if (sc < best[i]) { best[i] = sc; bidx[i] = gn; }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { red_v[ty * 8 + i][tx] = best[i]; red_i[ty * 8 + i][tx] = bidx[i]; }
+    __syncthreads();
+    if (tid < TBM) {
+        const int64_t gr = r0 + tid;
+        float bv = red_v[tid][0];
+        int bi = red_i[tid][0];
+        for (int t = 1; t < 16; ++t) {
+            const float v = red_v[tid][t];
+            const int ix = red_i[tid][t];
+            if (v < bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+        }
+        if (gr < R) out[gr] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
 // Skinny path: CTA = SK_ROWS rows x SK_BN columns, 256 threads; thread
 // (column c, row group r) owns rows r*SK_TR .. r*SK_TR+SK_TR-1 of column c:
 // SK_TR independent chains. Chunks of SK_KC rows of B (and the matching
@@ -223,6 +311,14 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
 }
 
 }  // namespace
+
+void gemm_argmin(const float* A, const float* B, const float* norms, int64_t R, int K, int N,
+                 int32_t* out, cudaStream_t s) {
+    if (R <= 0 || N <= 0) return;
+    gemm_argmin_kernel<<<(unsigned)ceil_div(R, TBM), 256, 0, s>>>(A, B, norms, R, K, N, out);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
 
 void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N,
                GemmEpi epi, const float* norms, cudaStream_t s) {

@@ -19,7 +19,6 @@
 namespace jhq {
 
 namespace {
-constexpr int64_t SCORE_BYTES = 256ll << 20;     // bound of one coarse-score block
 constexpr int MAX_CK_PAD = 256;
 
 template <class T>
@@ -101,15 +100,11 @@ void Index::assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaSt
         JHQ_CUDA(cudaMemsetAsync(d_assign, 0, n * sizeof(int32_t), s));
         return;
     }
-    int64_t rows = std::max<int64_t>(1, std::min<int64_t>(n, SCORE_BYTES / 4 / p_.nlist));
-    DevBuf<float> scores((size_t)rows * p_.nlist);
-    for (int64_t r0 = 0; r0 < n; r0 += rows) {
-        int64_t nr = std::min(rows, n - r0);
-        gemm_rows(d_y + r0 * d_, dcentsT_.get(), scores.get(), nr, d_, p_.nlist, EPI_COARSE,
-                  dnorms_.get(), s);
-        argmin_rows(scores.get(), nr, p_.nlist, d_assign + r0, s);
-    }
-    JHQ_CUDA(cudaStreamSynchronize(s));   // scores is freed on return
+    // fused GEMM + running argmin, in row blocks within the grid limit
+    const int64_t rows = 65535ll * 128;
+    for (int64_t r0 = 0; r0 < n; r0 += rows)
+        gemm_argmin(d_y + r0 * d_, dcentsT_.get(), dnorms_.get(), std::min(rows, n - r0), d_,
+                    p_.nlist, d_assign + r0, s);
 }
 
 void Index::upload_trained() {
@@ -373,11 +368,27 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
     const double avg_pages = (double)npages_ / p_.nlist;
     const double visits = std::max(1.0, (double)Bq * p_.nprobe * avg_pages / qg);
     sh.chunk_pages = (int)std::min(256.0, std::max(16.0, visits / (4.0 * sh.grid)));
-    // slots: per query, one per chunk of each probed list; bounded by nprobe
-    // plus the chunks of the nprobe largest lists
     int64_t top_pages = 0;
     for (int i = 0; i < p_.nprobe && i < (int)h_list_pages_sorted_.size(); ++i)
         top_pages += h_list_pages_sorted_[i];
+    // small IVF lists: query-major warp items instead of list-major units
+    sh.qmajor = 0;
+    if (p_.nlist > 1 && sh.mode == 1 && Mp_ <= 64 && avg_pages < 16.0 &&
+        scan_qmajor_smem_bytes(Mp_, sh.ck_pad) <= 227 * 1024)
+        sh.qmajor = 1;
+    if (const char* e = std::getenv("JHQ_SCAN_ORDER")) {     // tuning / test override
+        if (!std::strcmp(e, "list")) sh.qmajor = 0;
+        if (!std::strcmp(e, "query") && sh.mode == 1 && Mp_ <= 64) sh.qmajor = 1;
+    }
+    if (sh.qmajor) {
+        sh.grid = scan_qmajor_grid_for(Mp_, sh.ck_pad);
+        const double pages = std::max(1.0, (double)Bq * p_.nprobe * avg_pages);
+        sh.chunk_pages = (int)std::min(256.0, std::max(16.0, pages / (8.0 * sh.grid * 8)));
+        sh.max_slots = (int64_t)Bq * (1 + ceil_div(top_pages, sh.chunk_pages));
+        return sh;
+    }
+    // slots: per query, one per chunk of each probed list; bounded by nprobe
+    // plus the chunks of the nprobe largest lists
     sh.max_slots = (int64_t)Bq * (p_.nprobe + ceil_div(top_pages, sh.chunk_pages));
     return sh;
 }
@@ -418,6 +429,7 @@ void Index::prepare_workspace(int k) {
     ws_.mode = sh.mode;
     ws_.chunk_pages = sh.chunk_pages;
     ws_.max_slots = sh.max_slots;
+    ws_.qmajor = sh.qmajor;
     // capture the per-batch pipeline once (capture_graph, search.cu:315-386)
     const int64_t before = g_kernel_launches.load();
     JHQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
@@ -451,8 +463,12 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     }
     mark(2);
     const int qg = sh.mode == 0 ? 1 : sh.mode;
-    plan_build(b.probes, nq, p_.nprobe, p_.nlist, dlist_page_off_.get(), d_nvalid, sh.chunk_pages,
-               qg, b.plan, s);
+    if (sh.qmajor)
+        plan_build_qmajor(b.probes, nq, p_.nprobe, dlist_page_off_.get(), d_nvalid,
+                          sh.chunk_pages, b.plan, s);
+    else
+        plan_build(b.probes, nq, p_.nprobe, p_.nlist, dlist_page_off_.get(), d_nvalid,
+                   sh.chunk_pages, qg, b.plan, s);
     ScanArgs sa;
     sa.q_rot = b.q_rot; sa.c1d = dc1d_.get(); sa.list_page_off = dlist_page_off_.get();
     sa.pages = dpages_.get(); sa.slot_ids = dslot_ids_.get();
@@ -460,7 +476,8 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     sa.cpo = b.plan.cpo; sa.qslot_off = b.plan.qslot_off; sa.gthr = b.plan.gthr; sa.cand = b.cand;
     sa.nq = nq; sa.nlist = p_.nlist; sa.d = d_; sa.M = M_; sa.Mp = Mp_; sa.B = B_;
     sa.nprobe = p_.nprobe; sa.ck = sh.ck; sa.ck_pad = sh.ck_pad; sa.grid = sh.grid;
-    sa.chunk_pages = sh.chunk_pages; sa.mode = sh.mode;
+    sa.chunk_pages = sh.chunk_pages; sa.mode = sh.mode; sa.qmajor = sh.qmajor;
+    sa.probes = b.probes;
     mark(3);
     scan_topck(sa, s);
     mark(4);
@@ -479,6 +496,7 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.ck = ws_.ck; sh.ck_pad = ws_.ck_pad;
     sh.grid = ws_.grid; sh.mode = ws_.mode; sh.chunk_pages = ws_.chunk_pages;
     sh.max_slots = ws_.max_slots;
+    sh.qmajor = ws_.qmajor;
     BatchBufs b;
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),

@@ -77,7 +77,7 @@ public:
 private:
     struct Workspace {                 // SearchWorkspace (search.cuh:24-46)
         int batch_cap = 0, k = 0, ck = 0, ck_pad = 0, grid = 0;
-        int mode = 0, chunk_pages = 64;
+        int mode = 0, chunk_pages = 64, qmajor = 0;
         int64_t max_slots = 0;         // candidate slots a batch can need
         PinnedBuf<float> h_q;          // [batch][d] staged queries
         PinnedBuf<float> h_d;          // [batch][k]
@@ -103,7 +103,7 @@ private:
     void destroy_graph();
     // Shapes of one search batch: ck, scan mode / grid / chunking, slot bound.
     struct BatchShape {
-        int Bq, k, ck, ck_pad, grid, mode, chunk_pages;
+        int Bq, k, ck, ck_pad, grid, mode, chunk_pages, qmajor;
         int64_t max_slots;
     };
     // Device temporaries of one batch (workspace or fixed scratch array).

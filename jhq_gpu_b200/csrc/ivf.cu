@@ -211,6 +211,50 @@ void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probe
     count_launch();
 }
 
+namespace {
+
+// Per query: page prefix over its probes, item count, fresh bound.
+__global__ void plan_qmajor_kernel(const int32_t* __restrict__ probes, int nq, int nprobe,
+                                   const int32_t* __restrict__ lpo, const int* __restrict__ d_nvalid,
+                                   int item_pages, PlanBufs b) {
+    const int nvalid = d_nvalid ? *d_nvalid : nq;
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    int32_t* po = b.cpo + (int64_t)q * (nprobe + 1);
+    int acc = 0;
+    po[0] = 0;
+    for (int p = 0; p < nprobe; ++p) {
+        if (q < nvalid) {
+            const int l = probes[(int64_t)q * nprobe + p];
+            acc += lpo[l + 1] - lpo[l];
+        }
+        po[p + 1] = acc;
+    }
+    b.qslot_off[q + 1] = (acc + item_pages - 1) / item_pages;
+    b.gthr[q] = KEY_EMPTY;
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS)
+plan_qmajor_scan_kernel(int nq, PlanBufs b) {
+    const int64_t ns = block_exclusive_scan<int64_t>(nq, [&](int q) { return b.qslot_off[q + 1]; },
+                                                     b.qslot_off);
+    if (threadIdx.x == 0) b.qslot_off[nq] = ns;
+}
+
+}  // namespace
+
+void plan_build_qmajor(const int32_t* probes, int nq, int nprobe, const int32_t* list_page_off,
+                       const int* d_nvalid, int item_pages, const PlanBufs& b, cudaStream_t st) {
+    if (nq <= 0) return;
+    plan_qmajor_kernel<<<(unsigned)ceil_div(nq, 256), 256, 0, st>>>(probes, nq, nprobe,
+                                                                   list_page_off, d_nvalid,
+                                                                   item_pages, b);
+    JHQ_LAUNCH_CHECK();
+    plan_qmajor_scan_kernel<<<1, PLAN_THREADS, 0, st>>>(nq, b);
+    JHQ_LAUNCH_CHECK();
+    count_launch(2);
+}
+
 void plan_build(const int32_t* probes, int nq, int nprobe, int nlist,
                 const int32_t* list_page_off, const int* d_nvalid, int chunk_pages, int qg,
                 const PlanBufs& b, cudaStream_t st) {

@@ -19,6 +19,11 @@ enum GemmEpi { EPI_STORE = 0, EPI_COARSE = 1 };
 void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N,
                GemmEpi epi, const float* norms, cudaStream_t s);
 
+// out[r] = argmin_n (norms[n] - 2 * sum_k A[r*K+k] B[k*N+n]), first minimum,
+// each dot an in-order fma chain; the scores are never stored.
+void gemm_argmin(const float* A, const float* B, const float* norms, int64_t R, int K, int N,
+                 int32_t* out, cudaStream_t s);
+
 // ---- encode / IVF build (encode.cu) --------------------------------------
 // Primary + residual codes and corr of rotated rows y [n][d]
 // (encode.cu:20-86 of the reference). res rows are bpv_pad bytes apart.
@@ -27,8 +32,6 @@ void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
                  uint8_t* rcodes, int bpv_pad, float* corr, cudaStream_t s);
 // dst[0] = value (stream-ordered scalar upload, no host buffer involved).
 void set_int(int* dst, int value, cudaStream_t s);
-// argmin over each row of s [n][nlist] (first minimum) -> assign [n].
-void argmin_rows(const float* s, int64_t n, int nlist, int32_t* assign, cudaStream_t st);
 // Scatter codes into the page layout: slot_ids [npages*32] (-1 = empty slot),
 // pcodes [N][M] id-ordered -> pages [npages][Mp/16][32][16].
 void scatter_pages(const int32_t* slot_ids, int64_t nslots, const uint8_t* pcodes,
@@ -56,6 +59,11 @@ struct PlanBufs {
     uint64_t* gthr;        // [nq]  global pruning bound per query
 };
 // Queries >= *d_nvalid (when given) take part in nothing.
+// Query-major variant (small lists): a work item = (query, up to item_pages
+// consecutive pages of its probe sequence); cpo[q][p] = pages before probe p,
+// qslot_off = item offsets (one slot per item). cnt/bucket/unit/fill unused.
+void plan_build_qmajor(const int32_t* probes, int nq, int nprobe, const int32_t* list_page_off,
+                       const int* d_nvalid, int item_pages, const PlanBufs& b, cudaStream_t st);
 void plan_build(const int32_t* probes, int nq, int nprobe, int nlist,
                 const int32_t* list_page_off, const int* d_nvalid, int chunk_pages, int qg,
                 const PlanBufs& b, cudaStream_t st);
@@ -74,12 +82,16 @@ struct ScanArgs {
     const int64_t* qslot_off;
     uint64_t* gthr;                // [nq] lowered by the scan
     uint64_t* cand;                // [slots][ck] output candidate keys
+    const int32_t* probes;         // [nq][nprobe] (query-major order)
     int nq, nlist, d, M, Mp, B, nprobe, ck, ck_pad, grid, chunk_pages, mode;
+    int qmajor;                    // 1: query-major warp items (chunk_pages = item pages)
 };
 // mode 0: byte LUT, one query per unit; 1/2/4: nibble tables, 1/2/4 queries.
 int scan_mode_for(int d, int M, int B, double queries_per_list);
 size_t scan_smem_bytes(int Mp, int d, int ck_pad, int mode);  // dynamic shared memory per CTA
 int scan_grid_for(int Mp, int d, int ck_pad, int mode);       // persistent CTAs: SMs x resident
+int scan_qmajor_grid_for(int Mp, int ck_pad);
+size_t scan_qmajor_smem_bytes(int Mp, int ck_pad);
 void scan_topck(const ScanArgs& a, cudaStream_t st);
 void scan_configure();                               // opt-in shared memory, current device
 

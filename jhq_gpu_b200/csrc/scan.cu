@@ -420,6 +420,118 @@ scan_kernel(ScanArgs a) {
     if (run_open) close_run();
 }
 
+// ---------------------------------------------------------------------------
+// Query-major warp items, for IVF with small lists (a few pages per list),
+// where list-major units would be dominated by their per-unit block-wide work.
+// A warp owns one item = (query, up to item_pages consecutive pages of the
+// query's probe sequence): it builds the query's nibble tables in its own
+// shared region (kept while consecutive items share the query), scans the
+// pages, keeps an exact top-ck (pruned by the query's global bound) and
+// writes it to the item's slot — no block-wide synchronisation. The per-warp
+// table base is folded into the byte-permute that extracts each nibble offset
+// (the bases are multiples of 256 bytes), so a lookup needs no extra add.
+constexpr int QM_WARPS = 8;
+constexpr int QM_THREADS = QM_WARPS * 32;
+
+__host__ __device__ inline size_t qm_table_bytes(int Mp) { return ((size_t)Mp * 128 + 255) & ~size_t(255); }
+__host__ __device__ inline size_t qm_smem_bytes(int Mp, int ck_pad) {
+    return QM_WARPS * qm_table_bytes(Mp) + (size_t)QM_WARPS * merge_n_of(ck_pad) * 8 + 256 * 4;
+}
+
+template <int G_T>
+__global__ void __launch_bounds__(QM_THREADS, 2)
+scan_qmajor_kernel(ScanArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int G = G_T > 0 ? G_T : a.Mp / 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t tb = qm_table_bytes(a.Mp);
+    const int merge_n = merge_n_of(a.ck_pad);
+    float* tab = reinterpret_cast<float*>(smem + warp * tb);
+    uint64_t* wl = reinterpret_cast<uint64_t*>(smem + QM_WARPS * tb) + (size_t)warp * merge_n;
+    float* c1d = reinterpret_cast<float*>(smem + QM_WARPS * tb + (size_t)QM_WARPS * merge_n * 8);
+    const uint32_t base = (uint32_t)(warp * tb);            // byte offset of this warp's table
+
+    const int K1D = 1 << (a.B / (a.d / a.M));
+    for (int i = threadIdx.x; i < K1D; i += QM_THREADS) c1d[i] = a.c1d[i];
+    __syncthreads();
+
+    const int Ds = a.d / a.M, bpd = a.B / Ds, kmask = (1 << bpd) - 1, kpn = 4 / bpd;
+    const int64_t total = a.qslot_off[a.nq];
+    const int64_t nw = (int64_t)gridDim.x * QM_WARPS;
+    int cur_q = -1;
+    WarpTop top;
+    top.s = wl;
+    for (int64_t it = (int64_t)blockIdx.x * QM_WARPS + warp; it < total; it += nw) {
+        int lo = 0, hi = a.nq;                                // last q with qslot_off[q] <= it
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (a.qslot_off[mid] <= it) lo = mid; else hi = mid;
+        }
+        const int q = lo;
+        const int32_t* po = a.cpo + (int64_t)q * (a.nprobe + 1);
+        const int32_t* pr = a.probes + (int64_t)q * a.nprobe;
+        const int first = (int)(it - a.qslot_off[q]) * a.chunk_pages;
+        const int last = min(first + a.chunk_pages, po[a.nprobe]);
+        if (q != cur_q) {                                     // this query's tables
+            __syncwarp();
+            const float* qv = a.q_rot + (int64_t)q * a.d;
+            for (int i = lane; i < a.Mp * 32; i += 32) {
+                const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
+                float acc = 0.0f;
+                if (m < a.M) {
+                    const int k0 = half ? kpn : 0;
+                    const int k1 = half ? Ds : min(kpn, Ds);
+                    for (int k = k0; k < k1; ++k) {
+                        const float diff = __ldg(qv + m * Ds + k) - c1d[(n >> ((k - k0) * bpd)) & kmask];
+                        acc = __fmaf_rn(diff, diff, acc);
+                    }
+                }
+                tab[i] = acc;
+            }
+            __syncwarp();
+            cur_q = q;
+        }
+        top.reset(lane, merge_n, a.gthr[q]);
+        int p = 0;
+        for (int lp = first; lp < last; ++lp) {
+            while (lp >= po[p + 1]) ++p;
+            const int64_t pg = a.list_page_off[pr[p]] + (lp - po[p]);
+            const int32_t id = __ldg(a.slot_ids + pg * 32 + lane);
+            const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
+            float dist = 0.0f;
+            uint4 cur = __ldg(pp);
+#pragma unroll (G_T > 0 ? G_T : 1)
+            for (int g = 0; g < G; ++g) {
+                uint4 nxt = cur;
+                if (g + 1 < G) nxt = __ldg(pp + (g + 1) * 32);
+#pragma unroll
+                for (int wi = 0; wi < 4; ++wi) {
+                    const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
+                    const uint32_t Lo = (w << 2) & 0x3C3C3C3Cu;
+                    const uint32_t Hi = (w >> 2) & 0x3C3C3C3Cu;
+#pragma unroll
+                    for (int bb = 0; bb < 4; ++bb) {
+                        const int b = g * 16 + wi * 4 + bb;           // subspace
+                        // low byte from the nibble offset, upper bytes from the warp base
+                        const uint32_t olo = __byte_perm(Lo, base, 0x7650u | bb);
+                        const uint32_t ohi = __byte_perm(Hi, base, 0x7650u | bb);
+                        const float lo_v = *reinterpret_cast<const float*>(smem + olo + b * 128);
+                        const float hi_v = *reinterpret_cast<const float*>(smem + ohi + b * 128 + 64);
+                        dist = __fadd_rn(dist, __fadd_rn(lo_v, hi_v));
+                    }
+                }
+                cur = nxt;
+            }
+            top.push(id >= 0 ? make_key(dist, id) : KEY_EMPTY, lane, a.ck, a.ck_pad, merge_n,
+                     reinterpret_cast<uint64_t*>(&a.gthr[q]));
+        }
+        top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
+        uint64_t* out = a.cand + it * a.ck;
+        for (int i = lane; i < a.ck; i += 32) out[i] = top.s[i];
+        __syncwarp();
+    }
+}
+
 template <int G_T, int MODE>
 void launch_scan(const ScanArgs& a, size_t smem, cudaStream_t st) {
     scan_kernel<G_T, MODE><<<a.grid, SCAN_THREADS, smem, st>>>(a);
@@ -499,7 +611,46 @@ int scan_grid_for(int Mp, int d, int ck_pad, int mode) {
     return sms * per_sm;
 }
 
+template <int G_T>
+void qm_configure_one() {
+    JHQ_CUDA(cudaFuncSetAttribute(scan_qmajor_kernel<G_T>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+}
+
+size_t scan_qmajor_smem_bytes(int Mp, int ck_pad) { return qm_smem_bytes(Mp, ck_pad); }
+
+int scan_qmajor_grid_for(int Mp, int ck_pad) {
+    int dev = 0, sms = 0, per_sm = 0;
+    JHQ_CUDA(cudaGetDevice(&dev));
+    JHQ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const size_t smem = qm_smem_bytes(Mp, ck_pad);
+    switch (Mp / 16) {
+        case 1: qm_configure_one<1>();
+                JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<1>, QM_THREADS, smem)); break;
+        case 2: qm_configure_one<2>();
+                JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<2>, QM_THREADS, smem)); break;
+        case 4: qm_configure_one<4>();
+                JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<4>, QM_THREADS, smem)); break;
+        default: qm_configure_one<0>();
+                JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<0>, QM_THREADS, smem)); break;
+    }
+    if (per_sm < 1) fail(JHQ_EINVAL, "scan: query-major kernel does not fit on an SM");
+    return sms * per_sm;
+}
+
 void scan_topck(const ScanArgs& a, cudaStream_t st) {
+    if (a.qmajor) {
+        const size_t smem = qm_smem_bytes(a.Mp, a.ck_pad);
+        switch (a.Mp / 16) {
+            case 1: scan_qmajor_kernel<1><<<a.grid, QM_THREADS, smem, st>>>(a); break;
+            case 2: scan_qmajor_kernel<2><<<a.grid, QM_THREADS, smem, st>>>(a); break;
+            case 4: scan_qmajor_kernel<4><<<a.grid, QM_THREADS, smem, st>>>(a); break;
+            default: scan_qmajor_kernel<0><<<a.grid, QM_THREADS, smem, st>>>(a); break;
+        }
+        JHQ_LAUNCH_CHECK();
+        count_launch();
+        return;
+    }
     const size_t smem = scan_smem_layout(a.Mp, a.d, a.ck_pad, a.mode).total;
     if (smem > SCAN_SMEM_LIMIT) fail(JHQ_EINVAL, "scan: shared-memory tables too large (reduce M)");
     dispatch(a.Mp, a.mode, [&](auto G, auto Md) { launch_scan<G.value, Md.value>(a, smem, st); return 0; });

@@ -15,8 +15,9 @@ data of the stated shapes and value distributions:
             Student-t(4) mixture of 16,384 components, centres N(0, 20^2), scale 12
 
 Base and query sets are drawn from the same generator with different
-sub-seeds derived from the config seed. `chunked` generators yield base rows
-in blocks so 100M-row configs never materialise in host memory at once.
+sub-seeds derived from the config seed. The 100M-row generators (rows_c3,
+rows_c4) seed every 500,000-row block separately, so a rank generates only its
+own row range and host memory never holds the whole set.
 """
 from __future__ import annotations
 
@@ -56,34 +57,53 @@ def normalized_mixture(n: int, d: int, ncomp: int, seed: int, sub: int, sigma: f
     return out
 
 
-def uint8_mixture_chunks(n: int, seed: int, sub: int, d: int = 128, ncomp: int = 16384,
-                         block: int = 1 << 20) -> Iterator[np.ndarray]:
-    """C3 rows (as float32 of exact integer values) in blocks."""
+BLOCK = 500_000          # rows per independently seeded block of the 100M-row generators
+
+
+def _uint8_block(seed: int, sub: int, b: int, rows: int, d: int, centres, zero_dims):
+    rng = np.random.default_rng(np.random.SeedSequence([seed, sub, b]))
+    comp = rng.integers(0, len(centres), rows)
+    x = rng.standard_normal((rows, d), dtype=np.float32)
+    x *= 18.0
+    x += centres[comp]
+    zd = np.flatnonzero(zero_dims)                  # zero-heavy dims: 70% of values set to 0
+    sub_x = x[:, zd]
+    sub_x[rng.random((rows, len(zd)), dtype=np.float32) < 0.7] = 0.0
+    x[:, zd] = sub_x
+    np.clip(x, 0, 255, out=x)
+    return np.round(x, out=x)
+
+
+def _int8_block(seed: int, sub: int, b: int, rows: int, d: int, d_pad: int, centres):
+    rng = np.random.default_rng(np.random.SeedSequence([seed, sub, b]))
+    comp = rng.integers(0, len(centres), rows)
+    x = centres[comp] + 12.0 * rng.standard_t(4, (rows, d)).astype(np.float32)
+    out = np.zeros((rows, d_pad), np.float32)
+    out[:, :d] = np.round(np.clip(x, -128, 127))
+    return out
+
+
+def rows_c3(lo: int, hi: int, seed: int = 0, sub: int = 1, d: int = 128,
+            ncomp: int = 16384) -> Iterator[np.ndarray]:
+    """C3 rows [lo, hi) (float32 of exact uint8 values), one block-slice at a time;
+    block b of BLOCK rows has its own seed, so any row range is generated alone."""
     cr = _rng(seed, 2000)
     centres = cr.uniform(0, 120, (ncomp, d)).astype(np.float32)
     zero_dims = cr.random(d) < 0.25
-    rng = _rng(seed, sub)
-    for s in range(0, n, block):
-        m = min(block, n - s)
-        comp = rng.integers(0, ncomp, m)
-        x = centres[comp] + 18.0 * rng.standard_normal((m, d), dtype=np.float32)
-        zmask = (rng.random((m, d)) < 0.7) & zero_dims[None, :]
-        x[zmask] = 0.0
-        yield np.round(np.clip(x, 0, 255)).astype(np.float32)
+    for b in range(lo // BLOCK, (hi + BLOCK - 1) // BLOCK):
+        blk = _uint8_block(seed, sub, b, BLOCK, d, centres, zero_dims)
+        s, e = max(lo, b * BLOCK) - b * BLOCK, min(hi, (b + 1) * BLOCK) - b * BLOCK
+        yield blk[s:e]
 
 
-def int8_t_mixture_chunks(n: int, seed: int, sub: int, d: int = 100, d_pad: int = 104,
-                          ncomp: int = 16384, block: int = 1 << 20) -> Iterator[np.ndarray]:
-    """C4 rows, zero-padded from 100 to 104 dims, as float32 of exact integers."""
+def rows_c4(lo: int, hi: int, seed: int = 0, sub: int = 1, d: int = 100, d_pad: int = 104,
+            ncomp: int = 16384) -> Iterator[np.ndarray]:
+    """C4 rows [lo, hi), zero-padded from 100 to 104 dims (float32 of exact integers)."""
     centres = (20.0 * _rng(seed, 3000).standard_normal((ncomp, d))).astype(np.float32)
-    rng = _rng(seed, sub)
-    for s in range(0, n, block):
-        m = min(block, n - s)
-        comp = rng.integers(0, ncomp, m)
-        x = centres[comp] + 12.0 * rng.standard_t(4, (m, d)).astype(np.float32)
-        out = np.zeros((m, d_pad), np.float32)
-        out[:, :d] = np.round(np.clip(x, -128, 127))
-        yield out
+    for b in range(lo // BLOCK, (hi + BLOCK - 1) // BLOCK):
+        blk = _int8_block(seed, sub, b, BLOCK, d, d_pad, centres)
+        s, e = max(lo, b * BLOCK) - b * BLOCK, min(hi, (b + 1) * BLOCK) - b * BLOCK
+        yield blk[s:e]
 
 
 def make(config: str, seed: int = 0, n: int | None = None, nq: int | None = None
@@ -99,11 +119,11 @@ def make(config: str, seed: int = 0, n: int | None = None, nq: int | None = None
         return (normalized_mixture(n, c["d"], ncomp, seed, 1),
                 normalized_mixture(nq, c["d"], ncomp, seed, 2))
     if config == "c3":
-        return (np.concatenate(list(uint8_mixture_chunks(n, seed, 1))),
-                np.concatenate(list(uint8_mixture_chunks(nq, seed, 2))))
+        return (np.concatenate(list(rows_c3(0, n, seed, 1))),
+                np.concatenate(list(rows_c3(0, nq, seed, 2))))
     if config == "c4":
-        return (np.concatenate(list(int8_t_mixture_chunks(n, seed, 1))),
-                np.concatenate(list(int8_t_mixture_chunks(nq, seed, 2))))
+        return (np.concatenate(list(rows_c4(0, n, seed, 1))),
+                np.concatenate(list(rows_c4(0, nq, seed, 2))))
     raise KeyError(config)
 
 
@@ -148,3 +168,47 @@ def recall_at_k(labels: np.ndarray, gt: np.ndarray, k: int) -> float:
         gs = set(int(v) for v in g)
         hits += sum(1 for v in row if int(v) in gs)
     return hits / float(labels.shape[0] * k)
+
+
+def _torch_gen(device, seed: int, sub: int, b: int):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed((seed * 1_000_003 + sub) * 1_000_003 + b)
+    return g
+
+
+def rows_torch(config: str, lo: int, hi: int, device, seed: int = 0, sub: int = 1):
+    """C3 / C4 rows [lo, hi) generated on a CUDA device (float32 tensor of exact
+    integer values), for the 100M-row sharded runs. Every BLOCK-row block has
+    its own generator seed, so a rank can make exactly its own row range and
+    the rows do not depend on the number of ranks. Same distributions as
+    rows_c3 / rows_c4 (which use numpy and are used for small sets)."""
+    import torch
+    if config == "c3":
+        d, ncomp = 128, 16384
+        g0 = _torch_gen(device, seed, 2000, 0)
+        centres = torch.rand((ncomp, d), generator=g0, device=device) * 120.0
+        zero_dims = torch.rand(d, generator=g0, device=device) < 0.25
+    else:
+        d, d_pad, ncomp = 100, 104, 16384
+        g0 = _torch_gen(device, seed, 3000, 0)
+        centres = 20.0 * torch.randn((ncomp, d), generator=g0, device=device)
+    out = []
+    for b in range(lo // BLOCK, (hi + BLOCK - 1) // BLOCK):
+        g = _torch_gen(device, seed, sub, b)
+        comp = torch.randint(0, ncomp, (BLOCK,), generator=g, device=device)
+        if config == "c3":
+            x = centres[comp] + 18.0 * torch.randn((BLOCK, d), generator=g, device=device)
+            zmask = (torch.rand((BLOCK, d), generator=g, device=device) < 0.7) & zero_dims[None, :]
+            x = torch.where(zmask, torch.zeros_like(x), x)
+            x = torch.round(torch.clamp(x, 0, 255))
+        else:
+            z = torch.randn((BLOCK, d), generator=g, device=device)
+            chi = torch.randn((BLOCK, d, 4), generator=g, device=device).pow(2).sum(-1) / 4.0
+            t = z / torch.sqrt(chi)                         # Student-t, 4 degrees of freedom
+            x = torch.zeros((BLOCK, d_pad), device=device)
+            x[:, :d] = torch.round(torch.clamp(centres[comp] + 12.0 * t, -128, 127))
+        s, e = max(lo, b * BLOCK) - b * BLOCK, min(hi, (b + 1) * BLOCK) - b * BLOCK
+        out.append(x[s:e])
+    return torch.cat(out) if out else torch.zeros((0, 128 if config == "c3" else 104),
+                                                   device=device)

@@ -121,6 +121,26 @@ def test_search_bit_exact_vs_oracle(jhq, oracle, cfg):
         _assert_same(D, I, D2, I2)
 
 
+@pytest.mark.parametrize("order", ["list", "query"])
+@pytest.mark.parametrize("cfg", [
+    dict(d=128, M=32, nlist=64, nprobe=8, n=20000, nq=300, batch=100),        # C3 shape, small lists
+    dict(d=104, M=26, nlist=128, nprobe=16, n=9000, nq=50, batch=64),         # C4 shape
+    dict(d=64, M=16, nlist=300, nprobe=40, n=2000, nq=40, batch=13),          # many empty lists
+])
+def test_ivf_scan_orders_bit_exact(jhq, oracle, monkeypatch, cfg, order):
+    """Both scan work orders (list-major units / query-major warp items) give the
+    oracle's results bit for bit."""
+    monkeypatch.setenv("JHQ_SCAN_ORDER", order)
+    d, n = cfg["d"], cfg["n"]
+    x = _data(n, d, 21)
+    q = _data(cfg["nq"], d, 22)
+    p = jhq.Params(M=cfg["M"], nlist=cfg["nlist"], nprobe=cfg["nprobe"], batch_size=cfg["batch"])
+    idx = _build(jhq, d, p, x[:min(n, 4000)], x)
+    ox = _oracle_index(oracle, idx, x)
+    for k in (10, 3):
+        _assert_same(*idx.search(q, k), *_oracle_search(oracle, idx, ox, q, k))
+
+
 def test_edge_cases(jhq, oracle):
     d, M = 32, 8
     x = _data(300, d, 7)
