@@ -505,7 +505,7 @@ def run_sharded(args):
     import torch
     import jhq_gpu_b200 as J
     from jhq_gpu_b200 import datasets
-    from jhq_gpu_b200.sharded import ShardedSearch, contiguous_shard, index_local_search
+    from jhq_gpu_b200.sharded import PartitionedCoarseSearch, contiguous_shard
     cfg = SHARDED[args.config]
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -554,7 +554,7 @@ def run_sharded(args):
     D = torch.empty((nq, k), dtype=torch.float32, device=dev)
     I = torch.empty((nq, k), dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)          # a real stream: handle 0 means "index's own"
-    ss = ShardedSearch(index_local_search(idx), lo) if ws > 1 else None
+    ss = PartitionedCoarseSearch(idx, lo) if ws > 1 else None
 
     def search():
         with torch.cuda.stream(stream):

@@ -97,6 +97,16 @@ int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int 
  * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
 int jhq_synchronize(jhq_index* idx, double timeout_s);
 
+/* Split search for query-partitioned sharding: jhq_probe_device writes the
+ * nprobe list ids of each query (rotation + coarse scores + exact top-nprobe,
+ * search.cu:338-346 + select_probes_kernel) to d_probes [nq][nprobe];
+ * jhq_search_device_probes then searches with those lists (so ranks can share
+ * one rank's coarse work). No reference counterpart (single-GPU only). */
+int jhq_probe_device(jhq_index* idx, const float* d_q, int64_t nq, int32_t* d_probes,
+                     void* stream);
+int jhq_search_device_probes(jhq_index* idx, const float* d_q, const int32_t* d_probes,
+                             int64_t nq, int k, float* d_dists, int32_t* d_ids, void* stream);
+
 /* Changes the number of probed lists of later searches (clamped to nlist,
  * like the constructor, jhq_gpu_index.cu:128). The reference fixes nprobe at
  * construction; this allows an nprobe sweep on one trained index. */

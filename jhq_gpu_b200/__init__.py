@@ -35,7 +35,8 @@ EXPORTED = [
     "jhq_encode", "jhq_save", "jhq_load", "jhq_merge_shards", "jhq_kernel_launches",
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
-    "jhq_search_device_noalloc", "jhq_set_nprobe",
+    "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_probe_device",
+    "jhq_search_device_probes",
 ]
 STAGES = ["rotate", "coarse+probes", "plan", "scan", "refine"]
 
@@ -98,6 +99,8 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_search_device_noalloc.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_synchronize.argtypes = [vp, C.c_double]
     L.jhq_set_nprobe.argtypes = [vp, C.c_int]
+    L.jhq_probe_device.argtypes = [vp, vp, i64, vp, vp]
+    L.jhq_search_device_probes.argtypes = [vp, vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_ntotal.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_dim.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_is_trained.argtypes = [vp, C.POINTER(C.c_int)]
@@ -245,6 +248,16 @@ class JHQGpuIndex:
         in a fixed 16 MiB array inside the library (for callers that must not
         allocate while serving). Calls that overlap on the GPU race; serialise them."""
         _check(self._L.jhq_search_device_noalloc(self._h, q_ptr, nq, k, d_ptr, i_ptr, stream))
+
+    def probe_device(self, q_ptr: int, nq: int, probes_ptr: int, stream: int = 0) -> None:
+        """nprobe list ids per query ([nq][nprobe] int32, device) without searching."""
+        _check(self._L.jhq_probe_device(self._h, q_ptr, nq, probes_ptr, stream))
+
+    def search_device_probes(self, q_ptr: int, probes_ptr: int, nq: int, k: int, d_ptr: int,
+                             i_ptr: int, stream: int = 0) -> None:
+        """Device search with given probe lists (from probe_device, any rank)."""
+        _check(self._L.jhq_search_device_probes(self._h, q_ptr, probes_ptr, nq, k, d_ptr, i_ptr,
+                                                stream))
 
     def set_nprobe(self, nprobe: int) -> None:
         """Probe count of later searches (clamped to nlist)."""

@@ -119,6 +119,21 @@ int jhq_synchronize(jhq_index* idx, double timeout_s) {
     return guarded([&] { need(idx)->synchronize(timeout_s); });
 }
 
+int jhq_probe_device(jhq_index* idx, const float* d_q, int64_t nq, int32_t* d_probes,
+                     void* stream) {
+    return guarded([&] {
+        need(idx)->probe_device(d_q, nq, d_probes, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int jhq_search_device_probes(jhq_index* idx, const float* d_q, const int32_t* d_probes,
+                             int64_t nq, int k, float* d_dists, int32_t* d_ids, void* stream) {
+    return guarded([&] {
+        need(idx)->search_device_probes(d_q, d_probes, nq, k, d_dists, d_ids,
+                                        static_cast<cudaStream_t>(stream));
+    });
+}
+
 int jhq_set_nprobe(jhq_index* idx, int nprobe) {
     return guarded([&] { need(idx)->set_nprobe(nprobe); });
 }

@@ -452,22 +452,24 @@ void Index::prepare_workspace(int k) {
 // plan -> scan -> refine, with optional events between the stages.
 void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
                              const BatchShape& sh, const BatchBufs& b, float* out_d,
-                             int32_t* out_i, cudaStream_t s, cudaEvent_t* ev) {
+                             int32_t* out_i, cudaStream_t s, cudaEvent_t* ev,
+                             const int32_t* probes_in) {
     auto mark = [&](int i) { if (ev) JHQ_CUDA(cudaEventRecord(ev[i], s)); };
     mark(0);
     rotate_device(q_in, nq, b.q_rot, s);
     mark(1);
-    if (p_.nlist > 1) {
+    const int32_t* probes = probes_in ? probes_in : b.probes;
+    if (p_.nlist > 1 && !probes_in) {
         gemm_rows(b.q_rot, dcentsT_.get(), b.scores, nq, d_, p_.nlist, EPI_COARSE, dnorms_.get(), s);
         select_probes(b.scores, nq, p_.nlist, p_.nprobe, b.probes, s);
     }
     mark(2);
     const int qg = sh.mode == 0 ? 1 : sh.mode;
     if (sh.qmajor)
-        plan_build_qmajor(b.probes, nq, p_.nprobe, dlist_page_off_.get(), d_nvalid,
+        plan_build_qmajor(probes, nq, p_.nprobe, dlist_page_off_.get(), d_nvalid,
                           sh.chunk_pages, b.plan, s);
     else
-        plan_build(b.probes, nq, p_.nprobe, p_.nlist, dlist_page_off_.get(), d_nvalid,
+        plan_build(probes, nq, p_.nprobe, p_.nlist, dlist_page_off_.get(), d_nvalid,
                    sh.chunk_pages, qg, b.plan, s);
     ScanArgs sa;
     sa.q_rot = b.q_rot; sa.c1d = dc1d_.get(); sa.list_page_off = dlist_page_off_.get();
@@ -477,7 +479,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     sa.nq = nq; sa.nlist = p_.nlist; sa.d = d_; sa.M = M_; sa.Mp = Mp_; sa.B = B_;
     sa.nprobe = p_.nprobe; sa.ck = sh.ck; sa.ck_pad = sh.ck_pad; sa.grid = sh.grid;
     sa.chunk_pages = sh.chunk_pages; sa.mode = sh.mode; sa.qmajor = sh.qmajor;
-    sa.probes = b.probes;
+    sa.probes = probes;
     mark(3);
     scan_topck(sa, s);
     mark(4);
@@ -605,6 +607,52 @@ void Index::search_device(const float* d_q, int64_t nq, int k, float* d_dists, i
                                  cudaMemcpyDeviceToDevice, s));
         JHQ_CUDA(cudaMemcpyAsync(d_ids + q0 * k, ws_.out_i.get(), (size_t)nv * k * 4,
                                  cudaMemcpyDeviceToDevice, s));
+    }
+}
+
+void Index::probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaStream_t stream) {
+    DeviceGuard g(dev_);
+    check_search_args(nq, ws_.k ? ws_.k : 10);
+    if (nq == 0) return;
+    if (!d_q || !d_probes) fail(JHQ_EINVAL, "probe_device: null buffer");
+    prepare_workspace(ws_.k ? ws_.k : 10);
+    cudaStream_t s = stream ? stream : stream_;
+    const int Bq = ws_.batch_cap, np = p_.nprobe;
+    for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
+        const int nv = (int)std::min<int64_t>(Bq, nq - q0);
+        rotate_device(d_q + q0 * d_, nv, ws_.q_rot.get(), s);
+        if (p_.nlist > 1) {
+            gemm_rows(ws_.q_rot.get(), dcentsT_.get(), ws_.scores.get(), nv, d_, p_.nlist,
+                      EPI_COARSE, dnorms_.get(), s);
+            select_probes(ws_.scores.get(), nv, p_.nlist, np, d_probes + q0 * np, s);
+        } else {
+            JHQ_CUDA(cudaMemsetAsync(d_probes + q0 * np, 0, (size_t)nv * np * 4, s));
+        }
+    }
+}
+
+void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int64_t nq, int k,
+                                 float* d_dists, int32_t* d_ids, cudaStream_t stream) {
+    DeviceGuard g(dev_);
+    check_search_args(nq, k);
+    if (nq == 0) return;
+    if (!d_q || !d_probes || !d_dists || !d_ids) fail(JHQ_EINVAL, "search_device_probes: null buffer");
+    prepare_workspace(k);
+    cudaStream_t s = stream ? stream : stream_;
+    BatchShape sh;
+    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.ck = ws_.ck; sh.ck_pad = ws_.ck_pad;
+    sh.grid = ws_.grid; sh.mode = ws_.mode; sh.chunk_pages = ws_.chunk_pages;
+    sh.max_slots = ws_.max_slots; sh.qmajor = ws_.qmajor;
+    BatchBufs b;
+    b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
+    b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
+                      ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
+    b.cand = ws_.cand.get();
+    const int Bq = ws_.batch_cap;
+    for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
+        const int nv = (int)std::min<int64_t>(Bq, nq - q0);
+        enqueue_pipeline(d_q + q0 * d_, nv, nullptr, sh, b, d_dists + q0 * k, d_ids + q0 * k, s,
+                         nullptr, d_probes + q0 * p_.nprobe);
     }
 }
 

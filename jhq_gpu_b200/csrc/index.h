@@ -51,6 +51,9 @@ public:
                                int32_t* d_ids, cudaStream_t stream);
     void synchronize(double timeout_s);
     void set_nprobe(int nprobe);
+    void probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaStream_t stream);
+    void search_device_probes(const float* d_q, const int32_t* d_probes, int64_t nq, int k,
+                              float* d_dists, int32_t* d_ids, cudaStream_t stream);
 
     int64_t ntotal() const { return ntotal_; }
     int dim() const { return d_; }
@@ -117,7 +120,7 @@ private:
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
                           const BatchBufs& b, float* out_d, int32_t* out_i, cudaStream_t s,
-                          cudaEvent_t* ev);
+                          cudaEvent_t* ev, const int32_t* probes_in = nullptr);
     void enqueue_batch(cudaStream_t s, cudaEvent_t* ev = nullptr);
     void run_batch(cudaStream_t s, int nvalid);
     void check_search_args(int64_t nq, int k) const;

@@ -1,13 +1,6 @@
 // ivf.cu — IVF probe selection and the page partition of the ADC scan.
 //
-// select_probes_kernel replaces select_probes_kernel of the reference
-// (jhq_v14_streaming_add/search.cu:13-62), which runs nprobe rounds of
-// block-wide argmin with the whole score row in shared memory and cannot
-// launch above ~11.7k lists (48 KB default). Here one CTA per query finds the
-// nprobe-th smallest score by a 4-pass 8-bit radix select over
-// order-preserving keys read from global memory (no size limit), gathers the
-// winners — ties at the threshold resolved by ascending list id — and sorts
-// them by (score, list id), the exact order of jhq_v3_ivf/search.cu:46-85.
+// select_probes_kernel: exact top-nprobe lists per query (see the kernel).
 //
 // The plan kernels invert the (query, probe) pairs into per-list buckets and
 // number the scan's work units and candidate slots (see kernels.cuh).
@@ -20,17 +13,78 @@
 namespace jhq {
 namespace {
 
-constexpr int SP_THREADS = 256;
+constexpr int SP_THREADS = 512;
+constexpr int SP_CAP = 4096;                 // keys held in shared memory per query
+
+// Exact top-nprobe of one score row by (score, list id) — composite uint64
+// keys (order-preserving score << 32 | id) make the order a plain integer one.
+//  - nlist <= SP_CAP: the whole row is sorted in shared memory;
+//  - otherwise the first SP_CAP scores are sorted and their nprobe-th key T is
+//    an upper bound of the row's nprobe-th key, so every winner has key <= T;
+//    one pass collects those keys (about nprobe * nlist / SP_CAP of them) and
+//    a final sort picks the winners. If more than SP_CAP keys tie below T the
+//    row falls back to a 4-pass 8-bit radix select (select_probes_radix).
+// The reference's select_probes_kernel (jhq_v14_streaming_add/search.cu:13-62)
+// runs nprobe block-argmin rounds over the row in shared memory and cannot
+// launch above ~11.7k lists; the order here is jhq_v3_ivf/search.cu:46-85's.
+__device__ void select_probes_radix(const float* row, int nlist, int nprobe, int np_pad,
+                                    uint64_t* sp_buf, int32_t* out);
 
 __global__ void __launch_bounds__(SP_THREADS)
-select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int np_pad,
-                     int32_t* __restrict__ probes) {
-    extern __shared__ uint64_t sp_buf[];           // np_pad entries
-    __shared__ uint32_t hist[256];
-    __shared__ uint32_t sh_prefix, sh_rank, sh_nbuf, sh_eq_taken;
+select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t* __restrict__ probes) {
+    __shared__ uint64_t buf[SP_CAP];
+    __shared__ unsigned int cnt;
     const int q = blockIdx.x, tid = threadIdx.x;
     const float* row = s + (int64_t)q * nlist;
+    int32_t* out = probes + (int64_t)q * nprobe;
+    const int n0 = min(nlist, SP_CAP);
+    int P = 1;
+    while (P < n0) P <<= 1;
+    for (int i = tid; i < P; i += SP_THREADS)
+        buf[i] = i < n0 ? (((uint64_t)float_order(row[i]) << 32) | (uint32_t)i) : KEY_EMPTY;
+    __syncthreads();
+    block_bitonic_sort(buf, P);
+    if (nlist > SP_CAP) {
+        const uint64_t T = buf[nprobe - 1];
+        __syncthreads();
+        if (tid == 0) cnt = 0;
+        __syncthreads();
+        for (int c = tid; c < nlist; c += SP_THREADS) {
+            const uint64_t key = ((uint64_t)float_order(row[c]) << 32) | (uint32_t)c;
+            if (key <= T) {
+                const unsigned int pos = atomicAdd(&cnt, 1u);
+                if (pos < SP_CAP) buf[pos] = key;
+            }
+        }
+        __syncthreads();
+        const unsigned int n = cnt;
+        if (n > SP_CAP) {                      // pathological ties: radix select
+            int np_pad = 1;
+            while (np_pad < nprobe) np_pad <<= 1;
+            select_probes_radix(row, nlist, nprobe, np_pad, buf, out);
+            return;
+        }
+        P = 1;
+        while (P < (int)n) P <<= 1;
+        for (int i = n + tid; i < P; i += SP_THREADS) buf[i] = KEY_EMPTY;
+        __syncthreads();
+        block_bitonic_sort(buf, P);
+    }
+    for (int p = tid; p < nprobe; p += SP_THREADS) {
+        const uint64_t e = buf[p];
+        out[p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
+    }
+}
 
+// 4-pass 8-bit radix select of the nprobe-th key, then the winners (ties at
+// the threshold taken in ascending list id), sorted. Uses sp_buf[np_pad].
+__device__ void select_probes_radix(const float* row, int nlist, int nprobe, int np_pad,
+                                    uint64_t* sp_buf, int32_t* out) {
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t sh_prefix, sh_rank, sh_nbuf, sh_eq_taken;
+    __shared__ uint32_t warp_eq[SP_THREADS / 32];
+    const int tid = threadIdx.x;
+    __syncthreads();
     uint32_t prefix = 0, pmask = 0;
     uint32_t rank = (uint32_t)nprobe;               // 1-based rank of the threshold
     for (int shift = 24; shift >= 0; shift -= 8) {
@@ -64,7 +118,6 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int np_
     __syncthreads();
     const uint32_t need_eq = rank;
     const int lane = tid & 31, warp = tid / 32;
-    __shared__ uint32_t warp_eq[SP_THREADS / 32];
     for (int base = 0; base < nlist; base += SP_THREADS) {
         int c = base + tid;
         uint32_t k = (c < nlist) ? float_order(row[c]) : 0xffffffffu;
@@ -96,7 +149,7 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int np_
     block_bitonic_sort(sp_buf, np_pad);
     for (int p = tid; p < nprobe; p += SP_THREADS) {
         uint64_t e = sp_buf[p];
-        probes[(int64_t)q * nprobe + p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
+        out[p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
     }
 }
 
@@ -204,9 +257,8 @@ __global__ void plan_fill_kernel(const int32_t* __restrict__ probes, int nq, int
 void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probes,
                    cudaStream_t st) {
     if (nq <= 0) return;
-    int np_pad = next_pow2(nprobe);
-    size_t smem = (size_t)np_pad * sizeof(uint64_t);
-    select_probes_kernel<<<nq, SP_THREADS, smem, st>>>(s, nlist, nprobe, np_pad, probes);
+    if (nprobe > SP_CAP) fail(JHQ_EINVAL, "select_probes: nprobe too large");
+    select_probes_kernel<<<nq, SP_THREADS, 0, st>>>(s, nlist, nprobe, probes);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -94,6 +94,42 @@ def device_merge(Dall, Iall, world, nq, k, D, I, stream):
                  stream.cuda_stream if stream is not None else 0)
 
 
+class PartitionedCoarseSearch(ShardedSearch):
+    """ShardedSearch whose coarse step (rotation + scores against all nlist
+    centroids + top-nprobe) is split by queries: rank r computes the probe lists
+    of its 1/world of the queries, the lists are all-gathered, and every rank
+    then scans its shard with the full set. The coarse GEMM is the same on all
+    ranks (replicated centroids), so the gathered lists equal the ones each rank
+    would compute alone."""
+
+    def __init__(self, index, id_base: int, group=None):
+        super().__init__(None, id_base, group)
+        self.index = index
+
+    def search(self, q, k: int, stream=None):
+        import torch
+        nq = q.shape[0]
+        dev = q.device
+        st = stream if stream is not None else torch.cuda.current_stream(dev)
+        rank = self.dist.get_rank(self.group)
+        np_ = self.index.params.nprobe
+        per = -(-nq // self.world)
+        lo, hi = min(nq, rank * per), min(nq, (rank + 1) * per)
+        mine = torch.zeros((per, np_), dtype=torch.int32, device=dev)
+        if hi > lo:
+            self.index.probe_device(q[lo:hi].data_ptr(), hi - lo, mine.data_ptr(), st.cuda_stream)
+        parts = [torch.empty_like(mine) for _ in range(self.world)]
+        self.dist.all_gather(parts, mine, group=self.group)
+        probes = torch.cat(parts)[:nq].contiguous()
+        idx = self.index
+
+        def local(qq, n, kk, D, I, s):
+            idx.search_device_probes(qq.data_ptr(), probes.data_ptr(), n, kk, D.data_ptr(),
+                                     I.data_ptr(), s.cuda_stream)
+        self.local_search = local
+        return super().search(q, k, st)
+
+
 def index_local_search(index):
     """local_search callable for ShardedSearch backed by a JHQGpuIndex."""
     def run(q, nq, k, D, I, stream):

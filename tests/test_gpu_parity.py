@@ -126,6 +126,7 @@ def test_search_bit_exact_vs_oracle(jhq, oracle, cfg):
     dict(d=128, M=32, nlist=64, nprobe=8, n=20000, nq=300, batch=100),        # C3 shape, small lists
     dict(d=104, M=26, nlist=128, nprobe=16, n=9000, nq=50, batch=64),         # C4 shape
     dict(d=64, M=16, nlist=300, nprobe=40, n=2000, nq=40, batch=13),          # many empty lists
+    dict(d=32, M=8, nlist=5000, nprobe=64, n=12000, nq=30, batch=16),         # nlist > 4096 probe path
 ])
 def test_ivf_scan_orders_bit_exact(jhq, oracle, monkeypatch, cfg, order):
     """Both scan work orders (list-major units / query-major warp items) give the
@@ -135,7 +136,7 @@ def test_ivf_scan_orders_bit_exact(jhq, oracle, monkeypatch, cfg, order):
     x = _data(n, d, 21)
     q = _data(cfg["nq"], d, 22)
     p = jhq.Params(M=cfg["M"], nlist=cfg["nlist"], nprobe=cfg["nprobe"], batch_size=cfg["batch"])
-    idx = _build(jhq, d, p, x[:min(n, 4000)], x)
+    idx = _build(jhq, d, p, x[:min(n, max(4000, cfg["nlist"]))], x)
     ox = _oracle_index(oracle, idx, x)
     for k in (10, 3):
         _assert_same(*idx.search(q, k), *_oracle_search(oracle, idx, ox, q, k))
@@ -206,6 +207,30 @@ def test_device_search_equals_host_search(jhq):
                       torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     _assert_same(D, I, tD.cpu().numpy(), tI.cpu().numpy())
+
+
+@pytest.mark.parametrize("nlist,nprobe", [(1, 1), (40, 6)])
+def test_probe_then_search_equals_search(jhq, nlist, nprobe):
+    """jhq_probe_device + jhq_search_device_probes (query-partitioned coarse step
+    of the sharded search) == jhq_search_device."""
+    import torch
+    d, M = 64, 16
+    x = _data(6000, d, 31)
+    q = _data(333, d, 32)
+    idx = _build(jhq, d, jhq.Params(M=M, nlist=nlist, nprobe=nprobe, batch_size=100), x[:3000], x)
+    tq = torch.from_numpy(q).cuda()
+    s = torch.cuda.current_stream().cuda_stream
+    D1 = torch.empty((333, 10), dtype=torch.float32, device="cuda")
+    I1 = torch.empty((333, 10), dtype=torch.int32, device="cuda")
+    idx.search_device(tq.data_ptr(), 333, 10, D1.data_ptr(), I1.data_ptr(), s)
+    pr = torch.empty((333, nprobe), dtype=torch.int32, device="cuda")
+    idx.probe_device(tq[:200].data_ptr(), 200, pr.data_ptr(), s)          # two partial calls
+    idx.probe_device(tq[200:].data_ptr(), 133, pr[200:].data_ptr(), s)
+    D2 = torch.empty_like(D1)
+    I2 = torch.empty_like(I1)
+    idx.search_device_probes(tq.data_ptr(), pr.data_ptr(), 333, 10, D2.data_ptr(), I2.data_ptr(), s)
+    torch.cuda.synchronize()
+    assert torch.equal(I1, I2) and torch.equal(D1, D2)
 
 
 def test_save_load_roundtrip(jhq, tmp_path):
