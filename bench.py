@@ -513,7 +513,7 @@ def run_sharded(args):
     if ws > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    n = args.n or cfg["n"]
+    n = args.db_size or cfg["n"]
     nq, k = cfg["nq"], 10
     lo, hi = contiguous_shard(n, ws, rank)
     p = J.Params(M=cfg["M"], B=8, Br=4, alpha=4.0, nlist=cfg["nlist"], nprobe=cfg["nprobe"],
@@ -641,7 +641,7 @@ def main(argv=None):
     ap.add_argument("--config", choices=["c1", "c2", "c3", "c4"], default="c1",
                     help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep; "
                          "c3 / c4 = 100M-vector sharded IVF (one process per GPU)")
-    ap.add_argument("--n", type=int, default=0, help="c3/c4: database size (default 100M)")
+    ap.add_argument("--db-size", type=int, default=0, help="c3/c4: database size (default 100M)")
     ap.add_argument("--profile-run", action="store_true",
                     help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)

@@ -431,6 +431,8 @@ scan_kernel(ScanArgs a) {
 // table base is folded into the byte-permute that extracts each nibble offset
 // (the bases are multiples of 256 bytes), so a lookup needs no extra add.
 constexpr int QM_WARPS = 8;
+constexpr int QM_U = 1;                     // pages per warp step (measured: 1 beats 4)
+constexpr int QM_GMAX = 4;                  // code groups per page (Mp <= 64)
 constexpr int QM_THREADS = QM_WARPS * 32;
 
 __host__ __device__ inline size_t qm_table_bytes(int Mp) { return ((size_t)Mp * 128 + 255) & ~size_t(255); }
@@ -492,38 +494,55 @@ scan_qmajor_kernel(ScanArgs a) {
             cur_q = q;
         }
         top.reset(lane, merge_n, a.gthr[q]);
+        // QM_U pages per step: every page's ids and code groups are loaded
+        // before the first lookup, so QM_U page fetches are in flight per warp
         int p = 0;
-        for (int lp = first; lp < last; ++lp) {
-            while (lp >= po[p + 1]) ++p;
-            const int64_t pg = a.list_page_off[pr[p]] + (lp - po[p]);
-            const int32_t id = __ldg(a.slot_ids + pg * 32 + lane);
-            const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
-            float dist = 0.0f;
-            uint4 cur = __ldg(pp);
-#pragma unroll (G_T > 0 ? G_T : 1)
-            for (int g = 0; g < G; ++g) {
-                uint4 nxt = cur;
-                if (g + 1 < G) nxt = __ldg(pp + (g + 1) * 32);
+        for (int lp0 = first; lp0 < last; lp0 += QM_U) {
+            int32_t id[QM_U];
+            uint4 code[QM_U][QM_GMAX];
 #pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {
-                    const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
-                    const uint32_t Lo = (w << 2) & 0x3C3C3C3Cu;
-                    const uint32_t Hi = (w >> 2) & 0x3C3C3C3Cu;
+            for (int u = 0; u < QM_U; ++u) {
+                const int lp = lp0 + u;
+                id[u] = -1;
 #pragma unroll
-                    for (int bb = 0; bb < 4; ++bb) {
-                        const int b = g * 16 + wi * 4 + bb;           // subspace
-                        // low byte from the nibble offset, upper bytes from the warp base
-                        const uint32_t olo = __byte_perm(Lo, base, 0x7650u | bb);
-                        const uint32_t ohi = __byte_perm(Hi, base, 0x7650u | bb);
-                        const float lo_v = *reinterpret_cast<const float*>(smem + olo + b * 128);
-                        const float hi_v = *reinterpret_cast<const float*>(smem + ohi + b * 128 + 64);
-                        dist = __fadd_rn(dist, __fadd_rn(lo_v, hi_v));
+                for (int g = 0; g < QM_GMAX; ++g) code[u][g] = make_uint4(0, 0, 0, 0);
+                if (lp < last) {
+                    while (lp >= po[p + 1]) ++p;
+                    const int64_t pg = a.list_page_off[pr[p]] + (lp - po[p]);
+                    id[u] = __ldg(a.slot_ids + pg * 32 + lane);
+                    const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
+#pragma unroll
+                    for (int g = 0; g < QM_GMAX; ++g)
+                        if (g < G) code[u][g] = __ldg(pp + g * 32);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < QM_U; ++u) {
+                float dist = 0.0f;
+#pragma unroll
+                for (int g = 0; g < QM_GMAX; ++g) {
+                    if (g >= G) break;
+                    const uint4 cur = code[u][g];
+#pragma unroll
+                    for (int wi = 0; wi < 4; ++wi) {
+                        const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
+                        const uint32_t Lo = (w << 2) & 0x3C3C3C3Cu;
+                        const uint32_t Hi = (w >> 2) & 0x3C3C3C3Cu;
+#pragma unroll
+                        for (int bb = 0; bb < 4; ++bb) {
+                            const int b = g * 16 + wi * 4 + bb;           // subspace
+                            // low byte from the nibble offset, upper bytes from the warp base
+                            const uint32_t olo = __byte_perm(Lo, base, 0x7650u | bb);
+                            const uint32_t ohi = __byte_perm(Hi, base, 0x7650u | bb);
+                            const float lo_v = *reinterpret_cast<const float*>(smem + olo + b * 128);
+                            const float hi_v = *reinterpret_cast<const float*>(smem + ohi + b * 128 + 64);
+                            dist = __fadd_rn(dist, __fadd_rn(lo_v, hi_v));
+                        }
                     }
                 }
-                cur = nxt;
+                top.push(id[u] >= 0 ? make_key(dist, id[u]) : KEY_EMPTY, lane, a.ck, a.ck_pad,
+                         merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
             }
-            top.push(id >= 0 ? make_key(dist, id) : KEY_EMPTY, lane, a.ck, a.ck_pad, merge_n,
-                     reinterpret_cast<uint64_t*>(&a.gthr[q]));
         }
         top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
         uint64_t* out = a.cand + it * a.ck;
