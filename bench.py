@@ -585,8 +585,9 @@ def run_sharded(args):
     torch.cuda.synchronize(dev)
     ms = sum(a.elapsed_time(e) for a, e in ev)
     barrier()
-    idx.set_profiling(True)
-    search()
+    idx.set_profiling(True)                    # stage times of this rank's local pipeline
+    with torch.cuda.stream(stream):
+        idx.search_device(q_dev.data_ptr(), nq, k, D.data_ptr(), I.data_ptr(), stream.cuda_stream)
     torch.cuda.synchronize(dev)
     st, _ = idx.stage_times()
     idx.set_profiling(False)
