@@ -515,46 +515,59 @@ def run_sharded(args):
         dist.init_process_group("nccl", device_id=dev)
     n = args.db_size or cfg["n"]
     nq, k = cfg["nq"], 10
-    lo, hi = contiguous_shard(n, ws, rank)
+    # C4: bulk part, then `rounds` of (add round_size new vectors, search); the
+    # rows of every block are split contiguously over the ranks
+    rounds = args.rounds if args.config == "c4" else 0
+    round_size = min(1_000_000, n // 10) if rounds else 0
+    n_bulk = n - rounds * round_size
+    lo, hi = contiguous_shard(n_bulk, ws, rank)
     p = J.Params(M=cfg["M"], B=8, Br=4, alpha=4.0, nlist=cfg["nlist"], nprobe=cfg["nprobe"],
                  batch_size=cfg["batch"], add_batch=1 << 20, device=local)
     idx = J.JHQGpuIndex(cfg["d"], p)
     t0 = time.perf_counter()
     idx.train(datasets.rows_torch(args.config, 0, min(n, 100_000), dev).cpu().numpy())
     t_train = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    step = 2_000_000
-    for s in range(lo, hi, step):
-        idx.add(datasets.rows_torch(args.config, s, min(hi, s + step), dev).cpu().numpy())
-    t_add = time.perf_counter() - t0
     q_dev = datasets.rows_torch(args.config, 0, nq, dev, sub=2)
-    # exact ground truth of this shard (fp64 distances of exact integers), then merged
     qd = q_dev.double()
     qn = (qd * qd).sum(1, keepdim=True)
-    bd = torch.full((nq, k), float("inf"), dtype=torch.float64, device=dev)
-    bi = torch.full((nq, k), -1, dtype=torch.int64, device=dev)
-    for s in range(lo, hi, 50_000):
-        x = datasets.rows_torch(args.config, s, min(hi, s + 50_000), dev).double()
-        dd = qn - 2.0 * qd @ x.T + (x * x).sum(1)[None, :]
-        ids = torch.arange(s, s + x.shape[0], device=dev).expand(nq, -1)
-        cd, pos = torch.cat([bd, dd], 1).topk(k, dim=1, largest=False)
-        bi = torch.cat([bi, ids], 1).gather(1, pos)
-        bd = cd
-    if ws > 1:
-        import torch.distributed as dist
-        gd = [torch.empty_like(bd) for _ in range(ws)]
-        gi = [torch.empty_like(bi) for _ in range(ws)]
-        dist.all_gather(gd, bd)
-        dist.all_gather(gi, bi)
-        cd, pos = torch.cat(gd, 1).topk(k, dim=1, largest=False)
-        bi = torch.cat(gi, 1).gather(1, pos)
-    gt = bi.cpu().numpy().astype(np.int32)
-    del qd, bd
+    gt_d = torch.full((nq, k), float("inf"), dtype=torch.float64, device=dev)
+    gt_i = torch.full((nq, k), -1, dtype=torch.int64, device=dev)
 
+    def add_rows(a, b_):
+        """add global rows [a, b_) to this rank's index; fold them into the
+        rank's exact top-k (fp64 distances of exact integers)."""
+        nonlocal gt_d, gt_i
+        for s in range(a, b_, 2_000_000):
+            e = min(b_, s + 2_000_000)
+            x = datasets.rows_torch(args.config, s, e, dev)
+            idx.add(x.cpu().numpy())
+            for c in range(0, e - s, 50_000):
+                xd = x[c:c + 50_000].double()
+                dd = qn - 2.0 * qd @ xd.T + (xd * xd).sum(1)[None, :]
+                ids = torch.arange(s + c, s + c + xd.shape[0], device=dev).expand(nq, -1)
+                gt_d, pos = torch.cat([gt_d, dd], 1).topk(k, dim=1, largest=False)
+                gt_i = torch.cat([gt_i, ids], 1).gather(1, pos)
+
+    def global_gt():
+        if ws == 1:
+            return gt_i.cpu().numpy().astype(np.int32)
+        import torch.distributed as dist
+        gd = [torch.empty_like(gt_d) for _ in range(ws)]
+        gi = [torch.empty_like(gt_i) for _ in range(ws)]
+        dist.all_gather(gd, gt_d)
+        dist.all_gather(gi, gt_i)
+        _, pos = torch.cat(gd, 1).topk(k, dim=1, largest=False)
+        return torch.cat(gi, 1).gather(1, pos).cpu().numpy().astype(np.int32)
+
+    t0 = time.perf_counter()
+    add_rows(lo, hi)
+    t_add = time.perf_counter() - t0
+    id_map = torch.arange(lo, hi, dtype=torch.int32, device=dev)   # local id -> global id
+    gt = global_gt()
     D = torch.empty((nq, k), dtype=torch.float32, device=dev)
     I = torch.empty((nq, k), dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)          # a real stream: handle 0 means "index's own"
-    ss = PartitionedCoarseSearch(idx, lo) if ws > 1 else None
+    ss = PartitionedCoarseSearch(idx, id_map if rounds else lo) if ws > 1 else None
 
     def search():
         with torch.cuda.stream(stream):
@@ -596,6 +609,39 @@ def run_sharded(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    # ---- C4: interleaved streaming add rounds
+    round_log = []
+    for r in range(rounds):
+        a0 = n_bulk + r * round_size
+        rlo, rhi = contiguous_shard(round_size, ws, rank)
+        barrier()
+        t0 = time.perf_counter()
+        add_rows(a0 + rlo, a0 + rhi)
+        torch.cuda.synchronize(dev)
+        barrier()
+        t_r = time.perf_counter() - t0
+        id_map = torch.cat([id_map, torch.arange(a0 + rlo, a0 + rhi, dtype=torch.int32, device=dev)])
+        if ss is not None:
+            ss.id_base = id_map
+        gt_r = global_gt()
+        search()
+        torch.cuda.synchronize(dev)
+        barrier()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        Dr, Ir = search()
+        e.record(stream)
+        torch.cuda.synchronize(dev)
+        ms_r = a.elapsed_time(e)
+        if ws > 1:
+            import torch.distributed as dist
+            t = torch.tensor([ms_r], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_r = float(t.item())
+        round_log.append({"round": r + 1, "ntotal": a0 + round_size,
+                          "add_s": round(t_r, 2), "add_vectors_per_s": round(round_size / t_r, 1),
+                          "qps": round(nq / (ms_r / 1000.0), 1),
+                          "recall_at_10": round(datasets.recall_at_k(Ir.cpu().numpy(), gt_r, k), 4)})
     if rank == 0:
         out = {"metric": f"QPS (C{args.config[1]} sharded IVF-JHQ, {n // 1_000_000}M vectors)",
                "value": round(args.steps * nq / (ms / 1000.0), 1), "unit": "QPS", "n_gpus": ws,
@@ -608,6 +654,11 @@ def run_sharded(args):
                "recall_at_10": round(recall, 4), "stage_ms_rank0": {kk: round(v, 3) for kk, v in st.items()},
                "train_s": round(t_train, 1), "add_s_rank0": round(t_add, 1),
                "shard_vectors_rank0": hi - lo}
+        if rounds:
+            out["metric"] = (f"QPS (C4 sharded IVF-JHQ, {n_bulk // 1_000_000}M bulk + {rounds} "
+                             f"streaming rounds of {round_size} adds)")
+            out["n_base_bulk"] = n_bulk
+            out["rounds"] = round_log
         print(json.dumps(out), flush=True)
     if ws > 1:
         import torch.distributed as dist
@@ -643,6 +694,8 @@ def main(argv=None):
                     help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep; "
                          "c3 / c4 = 100M-vector sharded IVF (one process per GPU)")
     ap.add_argument("--db-size", type=int, default=0, help="c3/c4: database size (default 100M)")
+    ap.add_argument("--rounds", type=int, default=10,
+                    help="c4: interleaved (add 1M, search) rounds after the bulk add")
     ap.add_argument("--profile-run", action="store_true",
                     help="short C1 run for ncu (2 searches after a 20k-row training)")
     args = ap.parse_args(argv)

@@ -53,12 +53,14 @@ class ShardedSearch:
     device merge (jhq_gpu_b200.merge_shards) — both injectable so the
     gather/offset logic can be exercised on CPU ranks in tests."""
 
-    def __init__(self, local_search: Callable, id_base: int, group=None,
+    def __init__(self, local_search: Callable, id_base, group=None,
                  merge: Optional[Callable] = None):
+        """id_base: int (shard = global ids [id_base, ...)) or an int32 tensor on
+        the device mapping local ids to global ids (streaming adds)."""
         import torch.distributed as dist
         self.dist = dist
         self.local_search = local_search
-        self.id_base = int(id_base)
+        self.id_base = id_base
         self.group = group
         self.world = dist.get_world_size(group)
         self.merge = merge if merge is not None else device_merge
@@ -74,7 +76,10 @@ class ShardedSearch:
         st = stream if stream is not None else (torch.cuda.current_stream(dev)
                                                 if dev.type == "cuda" else None)
         self.local_search(q, nq, k, Dl, Il, st)
-        Il = torch.where(Il >= 0, Il + self.id_base, Il)
+        if isinstance(self.id_base, int):
+            Il = torch.where(Il >= 0, Il + self.id_base, Il)
+        else:
+            Il = torch.where(Il >= 0, self.id_base[Il.clamp(min=0).long()], Il)
         Dparts = [torch.empty_like(Dl) for _ in range(self.world)]
         Iparts = [torch.empty_like(Il) for _ in range(self.world)]
         self.dist.all_gather(Dparts, Dl.contiguous(), group=self.group)
