@@ -381,7 +381,9 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
         sh.qmajor = 1;
     if (const char* e = std::getenv("JHQ_SCAN_ORDER")) {     // tuning / test override
         if (!std::strcmp(e, "list")) sh.qmajor = 0;
-        if (!std::strcmp(e, "query") && sh.mode == 1 && Mp_ <= 64) sh.qmajor = 1;
+        if (!std::strcmp(e, "query") && sh.mode == 1 && Mp_ <= 128 &&
+            scan_qmajor_smem_bytes(Mp_, sh.ck_pad) <= 227 * 1024)
+            sh.qmajor = 1;
     }
     if (sh.qmajor) {
         sh.grid = scan_qmajor_grid_for(Mp_, sh.ck_pad);

@@ -38,7 +38,10 @@
 //      + ck serial block-argmin rounds (search.cu:153-194), which can drop
 //      true top-ck. Candidates are pruned against min(warp ck-th, CTA ck-th,
 //      the query's global ck-th): a key above any of them has ck better keys
-//      already kept somewhere, so it cannot reach the query's top-ck;
+//      already kept somewhere, so it cannot reach the query's top-ck. Every
+//      warp flush publishes its ck-th key to both bounds (a CTA's merged list
+//      keeps ck keys at or below any of its warps' ck-th keys), so CTAs that
+//      scan the same query tighten each other's bounds while they run;
 //   4. at the end of a run (consecutive units of one list and query group on
 //      this CTA) merges its warps' lists per query, writes the top-ck to the
 //      run's first slot (the run's other slots hold empty lists) and lowers
@@ -210,28 +213,35 @@ struct WarpTop {
     }
     // Merge the buffer into the list; publish the warp's ck-th key to the CTA
     // bound and pick up the tightest bound.
-    __device__ __forceinline__ void flush(int lane, int ck, int ck_pad, int merge_n, uint64_t* tau) {
+    __device__ __forceinline__ void flush(int lane, int ck, int ck_pad, int merge_n, uint64_t* tau,
+                                          uint64_t* gbound = nullptr) {
         const int cap = merge_n - ck_pad;
         if (lane == 0) SCAN_STAT(2, 1);
         for (int i = count + lane; i < cap; i += 32) s[ck_pad + i] = KEY_EMPTY;
         __syncwarp();
         warp_bitonic_sort(s, merge_n, lane);
         const uint64_t kth = s[ck - 1];
-        if (lane == 0 && kth != KEY_EMPTY)
+        if (lane == 0 && kth != KEY_EMPTY) {
             atomicMin(reinterpret_cast<unsigned long long*>(tau), (unsigned long long)kth);
+            if (gbound) atomicMin(reinterpret_cast<unsigned long long*>(gbound), (unsigned long long)kth);
+        }
         __syncwarp();
-        const uint64_t t = *reinterpret_cast<volatile uint64_t*>(tau);
+        uint64_t t = *reinterpret_cast<volatile uint64_t*>(tau);
+        if (gbound) {
+            const uint64_t g = *reinterpret_cast<volatile uint64_t*>(gbound);
+            t = g < t ? g : t;
+        }
         thr = kth < t ? kth : t;
         count = 0;
     }
     __device__ __forceinline__ void push(uint64_t key, int lane, int ck, int ck_pad, int merge_n,
-                                         uint64_t* tau) {
+                                         uint64_t* tau, uint64_t* gbound = nullptr) {
         bool take = key < thr;
         unsigned mask = __ballot_sync(0xffffffffu, take);
         if (lane == 0) { SCAN_STAT(0, 32); SCAN_STAT(1, __popc(mask)); }
         if (mask == 0) return;
         if (count + __popc(mask) > merge_n - ck_pad) {
-            flush(lane, ck, ck_pad, merge_n, tau);
+            flush(lane, ck, ck_pad, merge_n, tau, gbound);
             take = key < thr;
             mask = __ballot_sync(0xffffffffu, take);
             if (mask == 0) return;
@@ -302,7 +312,9 @@ scan_kernel(ScanArgs a) {
     bool run_open = false;
     auto close_run = [&]() {
 #pragma unroll
-        for (int j = 0; j < QG; ++j) top[j].flush(lane, a.ck, a.ck_pad, merge_n, tau + j);
+        for (int j = 0; j < QG; ++j)
+            top[j].flush(lane, a.ck, a.ck_pad, merge_n, tau + j,
+                         cur_q[j] >= 0 ? a.gthr + cur_q[j] : nullptr);
         for (int j = 0; j < QG; ++j) {
             if (cur_q[j] < 0) continue;        // uniform across the block
             __syncthreads();
@@ -413,7 +425,7 @@ scan_kernel(ScanArgs a) {
 #pragma unroll
                 for (int u = 0; u < PPW; ++u)
                     top[j].push(id[u] >= 0 ? make_key(dd[u][j], id[u]) : KEY_EMPTY, lane, a.ck,
-                                a.ck_pad, merge_n, tau + j);
+                                a.ck_pad, merge_n, tau + j, a.gthr + unit.q[j]);
             }
         }
     }
@@ -432,7 +444,7 @@ scan_kernel(ScanArgs a) {
 // (the bases are multiples of 256 bytes), so a lookup needs no extra add.
 constexpr int QM_WARPS = 8;
 constexpr int QM_U = 1;                     // pages per warp step (measured: 1 beats 4)
-constexpr int QM_GMAX = 4;                  // code groups per page (Mp <= 64)
+constexpr int QM_GMAX = 8;                  // code groups per page (Mp <= 128)
 constexpr int QM_THREADS = QM_WARPS * 32;
 
 __host__ __device__ inline size_t qm_table_bytes(int Mp) { return ((size_t)Mp * 128 + 255) & ~size_t(255); }
@@ -650,6 +662,8 @@ int scan_qmajor_grid_for(int Mp, int ck_pad) {
                 JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<2>, QM_THREADS, smem)); break;
         case 4: qm_configure_one<4>();
                 JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<4>, QM_THREADS, smem)); break;
+        case 8: qm_configure_one<8>();
+                JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<8>, QM_THREADS, smem)); break;
         default: qm_configure_one<0>();
                 JHQ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_qmajor_kernel<0>, QM_THREADS, smem)); break;
     }
@@ -664,6 +678,7 @@ void scan_topck(const ScanArgs& a, cudaStream_t st) {
             case 1: scan_qmajor_kernel<1><<<a.grid, QM_THREADS, smem, st>>>(a); break;
             case 2: scan_qmajor_kernel<2><<<a.grid, QM_THREADS, smem, st>>>(a); break;
             case 4: scan_qmajor_kernel<4><<<a.grid, QM_THREADS, smem, st>>>(a); break;
+            case 8: scan_qmajor_kernel<8><<<a.grid, QM_THREADS, smem, st>>>(a); break;
             default: scan_qmajor_kernel<0><<<a.grid, QM_THREADS, smem, st>>>(a); break;
         }
         JHQ_LAUNCH_CHECK();
