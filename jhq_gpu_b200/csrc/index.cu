@@ -71,7 +71,7 @@ Index::~Index() {
         if (e) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
     // DevBuf / PinnedBuf members free themselves (device still current).
-    dPi_.release(); dc1d_.release(); dres_.release(); dcentsT_.release(); dnorms_.release();
+    dPi_.release(); dc1d_.release(); dres_.release(); dcentsT_.release(); dcents_.release(); dcents3_.release(); dassign_scratch_.release(); dnorms_.release();
     dpcodes_.release(); drcodes_.release(); dpages_.release(); dcorr_.release();
     dassign_.release(); dslot_ids_.release(); dlist_page_off_.release();
     ws_.q.release(); ws_.q_rot.release(); ws_.scores.release(); ws_.out_d.release();
@@ -98,6 +98,17 @@ void Index::rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t 
 void Index::assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaStream_t s) {
     if (p_.nlist == 1) {
         JHQ_CUDA(cudaMemsetAsync(d_assign, 0, n * sizeof(int32_t), s));
+        return;
+    }
+    if (coarse_tc_) {
+        // tensor-core scores + margin selection of the single nearest list, in
+        // row blocks whose score rows stay within about 256 MB
+        const int64_t R = std::max<int64_t>(128, std::min<int64_t>(
+            n, ((256ll << 20) / ((int64_t)p_.nlist * 4)) / 128 * 128));
+        dassign_scratch_.ensure(coarse_scratch_floats((int)R));
+        for (int64_t r0 = 0; r0 < n; r0 += R)
+            coarse_probes(d_y + r0 * d_, (int)std::min(R, n - r0), (int)R, 1,
+                          dassign_scratch_.get(), d_assign + r0, s);
         return;
     }
     // fused GEMM + running argmin, in row blocks within the grid limit
@@ -131,6 +142,24 @@ void Index::upload_trained() {
     dnorms_.resize(nl);
     h2d(dcentsT_.get(), cT.data(), cT.size(), stream_);
     h2d(dnorms_.get(), norms.data(), norms.size(), stream_);
+    // Row-major copy for the tensor-core path (TMA operand and exact rescoring).
+    const char* cm = std::getenv("JHQ_COARSE");
+    coarse_tc_ = nl > 1 && coarse_tc_supported(d_, nl) && d_ <= 2048 &&
+                 !(cm && std::string(cm) == "simt");
+    if (coarse_tc_) {
+        dcents_.resize((size_t)nl * d_);
+        h2d(dcents_.get(), cents_.data(), (size_t)nl * d_, stream_);
+        std::vector<float> c3((size_t)nl * 3 * d_);
+        split3_rows_host(cents_.data(), nl, d_, 1, c3.data());
+        dcents3_.resize(c3.size());
+        h2d(dcents3_.get(), c3.data(), c3.size(), stream_);
+        double mx = 0.0;
+        for (int c = 0; c < nl; ++c) mx = std::max(mx, (double)norms[c]);
+        cmax_ = (float)(std::sqrt(mx) * 1.0001);
+    } else {
+        dcents_.release();
+        dcents3_.release();
+    }
     JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
@@ -400,7 +429,9 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
 
 void Index::prepare_workspace(int k) {
     const int Bq = p_.batch_size;
-    if (ws_.batch_cap == Bq && ws_.k == k && ws_.exec) return;
+    if (ws_.batch_cap == Bq && ws_.k == k && ws_.exec &&
+        ws_.coarse_floats == coarse_scratch_floats(Bq))
+        return;
     destroy_graph();
     scan_configure();
     refine_configure();
@@ -408,7 +439,8 @@ void Index::prepare_workspace(int k) {
     const int nl = p_.nlist, np = p_.nprobe;
     ws_.q.ensure((size_t)Bq * d_);
     ws_.q_rot.ensure((size_t)Bq * d_);
-    if (nl > 1) ws_.scores.ensure((size_t)Bq * nl);
+    ws_.coarse_floats = coarse_scratch_floats(Bq);
+    if (nl > 1) ws_.scores.ensure(ws_.coarse_floats);
     ws_.probes.ensure((size_t)Bq * np);
     ws_.cnt.ensure((size_t)nl + 1);
     ws_.bucket_off.ensure((size_t)nl + 1);
@@ -453,6 +485,28 @@ void Index::prepare_workspace(int k) {
     JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
+size_t Index::coarse_scratch_floats(int Bq) const {
+    if (p_.nlist <= 1) return 0;
+    const size_t sc = ((size_t)Bq * p_.nlist + 63) & ~(size_t)63;   // split rows 256-byte aligned
+    return sc + (coarse_tc_ ? (size_t)Bq * 3 * d_ + (size_t)Bq * coarse_tc_tiles(p_.nlist) : 0);
+}
+
+void Index::coarse_probes(const float* q_rot, int nq, int Bq, int nprobe, float* scores,
+                          int32_t* probes, cudaStream_t s) {
+    if (coarse_tc_) {
+        float* q3 = scores + (((size_t)Bq * p_.nlist + 63) & ~(size_t)63);
+        float* tmin = q3 + (size_t)Bq * 3 * d_;
+        const int nt = coarse_tc_tiles(p_.nlist);
+        split3_rows(q_rot, nq, d_, q3, s);
+        coarse_scores_tc(q3, nq, dcents3_.get(), dnorms_.get(), p_.nlist, d_, scores, tmin, s);
+        select_probes_margin(scores, q_rot, dcents_.get(), dnorms_.get(), tmin, nt, nq, p_.nlist,
+                             d_, nprobe, cmax_, probes, s);
+    } else {
+        gemm_rows(q_rot, dcentsT_.get(), scores, nq, d_, p_.nlist, EPI_COARSE, dnorms_.get(), s);
+        select_probes(scores, nq, p_.nlist, nprobe, probes, s);
+    }
+}
+
 // Kernel sequence of one query batch: rotate -> coarse scores + probes ->
 // plan -> scan -> refine, with optional events between the stages.
 void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
@@ -465,8 +519,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     mark(1);
     const int32_t* probes = probes_in ? probes_in : b.probes;
     if (p_.nlist > 1 && !probes_in) {
-        gemm_rows(b.q_rot, dcentsT_.get(), b.scores, nq, d_, p_.nlist, EPI_COARSE, dnorms_.get(), s);
-        select_probes(b.scores, nq, p_.nlist, p_.nprobe, b.probes, s);
+        coarse_probes(b.q_rot, nq, sh.Bq, p_.nprobe, b.scores, b.probes, s);
     }
     mark(2);
     const int qg = sh.mode == 0 ? 1 : sh.mode;
@@ -592,6 +645,8 @@ void Index::search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t*
     }
     cudaEventDestroy(ev[0]);
     cudaEventDestroy(ev[1]);
+    if (coarse_tc_ && coarse_tc_error(true))
+        fail(JHQ_ETIMEDOUT, "search: a tensor-core coarse wait gave up");
 }
 
 void Index::search_device(const float* d_q, int64_t nq, int k, float* d_dists, int32_t* d_ids,
@@ -627,9 +682,7 @@ void Index::probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaSt
         const int nv = (int)std::min<int64_t>(Bq, nq - q0);
         rotate_device(d_q + q0 * d_, nv, ws_.q_rot.get(), s);
         if (p_.nlist > 1) {
-            gemm_rows(ws_.q_rot.get(), dcentsT_.get(), ws_.scores.get(), nv, d_, p_.nlist,
-                      EPI_COARSE, dnorms_.get(), s);
-            select_probes(ws_.scores.get(), nv, p_.nlist, np, d_probes + q0 * np, s);
+            coarse_probes(ws_.q_rot.get(), nv, Bq, np, ws_.scores.get(), d_probes + q0 * np, s);
         } else {
             JHQ_CUDA(cudaMemsetAsync(d_probes + q0 * np, 0, (size_t)nv * np * 4, s));
         }
@@ -675,7 +728,11 @@ void Index::synchronize(double timeout_s) {
     auto t0 = std::chrono::steady_clock::now();
     for (;;) {
         cudaError_t e = cudaStreamQuery(stream_);
-        if (e == cudaSuccess) return;
+        if (e == cudaSuccess) {
+            if (coarse_tc_ && coarse_tc_error(true))
+                fail(JHQ_ETIMEDOUT, "synchronize: a tensor-core coarse wait gave up");
+            return;
+        }
         if (e != cudaErrorNotReady) JHQ_CUDA(e);
         double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (el > timeout_s) fail(JHQ_ETIMEDOUT, "synchronize: stream still busy at the deadline");

@@ -95,10 +95,18 @@ private:
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
         int64_t graph_kernels = 0;
+        size_t coarse_floats = 0;
     };
 
     void upload_trained();
     void rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const;
+    // q_rot [nq][d] -> probes [nq][nprobe] through scores [nq][nlist] (scratch):
+    // tensor-core scores + margin selection, or the fp32 SIMT GEMM + exact
+    // selection (JHQ_COARSE=simt); both give the same lists.
+    // `scores` holds coarse_scratch_floats(Bq) floats (scores, then the split queries).
+    void coarse_probes(const float* q_rot, int nq, int Bq, int nprobe, float* scores,
+                       int32_t* probes, cudaStream_t s);
+    size_t coarse_scratch_floats(int Bq) const;
     void assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaStream_t s);
     void grow_master(int64_t need);
     void rebuild_layout();
@@ -141,7 +149,10 @@ private:
     int64_t stage_batches_ = 0;
     cudaEvent_t prof_ev_[6] = {};
 
-    DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dnorms_;
+    DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dcents_, dcents3_, dnorms_;
+    DevBuf<float> dassign_scratch_;    // tensor-core assignment: scores of a row block
+    float cmax_ = 0.0f;                // >= max |centroid| (coarse margin)
+    bool coarse_tc_ = false;
     DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
     DevBuf<float> dcorr_;
     DevBuf<int32_t> dassign_, dslot_ids_, dlist_page_off_;

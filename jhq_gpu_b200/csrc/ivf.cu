@@ -15,6 +15,7 @@ namespace {
 
 constexpr int SP_THREADS = 512;
 constexpr int SP_CAP = 4096;                 // keys held in shared memory per query
+constexpr int SPM_DMAX = 2048;               // largest d of select_probes_margin
 
 // Exact top-nprobe of one score row by (score, list id) — composite uint64
 // keys (order-preserving score << 32 | id) make the order a plain integer one.
@@ -30,13 +31,11 @@ constexpr int SP_CAP = 4096;                 // keys held in shared memory per q
 __device__ void select_probes_radix(const float* row, int nlist, int nprobe, int np_pad,
                                     uint64_t* sp_buf, int32_t* out);
 
-__global__ void __launch_bounds__(SP_THREADS)
-select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t* __restrict__ probes) {
-    __shared__ uint64_t buf[SP_CAP];
+// Exact selection of one row into out[nprobe]; buf = SP_CAP keys of shared memory.
+__device__ void select_row_exact(const float* row, int nlist, int nprobe, int32_t* out,
+                                 uint64_t* buf) {
     __shared__ unsigned int cnt;
-    const int q = blockIdx.x, tid = threadIdx.x;
-    const float* row = s + (int64_t)q * nlist;
-    int32_t* out = probes + (int64_t)q * nprobe;
+    const int tid = threadIdx.x;
     const int n0 = min(nlist, SP_CAP);
     int P = 1;
     while (P < n0) P <<= 1;
@@ -70,6 +69,136 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t
         __syncthreads();
         block_bitonic_sort(buf, P);
     }
+    for (int p = tid; p < nprobe; p += SP_THREADS) {
+        const uint64_t e = buf[p];
+        out[p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
+    }
+}
+
+__global__ void __launch_bounds__(SP_THREADS)
+select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t* __restrict__ probes) {
+    __shared__ uint64_t buf[SP_CAP];
+    const int q = blockIdx.x;
+    select_row_exact(s + (int64_t)q * nlist, nlist, nprobe, probes + (int64_t)q * nprobe, buf);
+}
+
+// Exact top-nprobe from APPROXIMATE scores s~ (the tensor-core coarse GEMM,
+// coarse_tc.cu). With |s~_c - s_c| <= E for every list c (s = the fp32 chain
+// score norms[c] - 2 * fma-chain(q, cent_c)), and t~ the nprobe-th smallest s~:
+//   a winner w has s_w <= t (the nprobe-th smallest s), and t <= t~ + E (the
+//   nprobe lists with s~ <= t~ have s <= t~ + E), so s~_w <= s_w + E <= t~ + 2E.
+// Hence the lists with s~ <= t~ + 2E contain every winner; they are rescored
+// with the exact chain and the exact (s, list id) order picks the winners.
+// E bounds, for the 3-term tf32 split of coarse_tc.cu (x = hi + lo; hi exact
+// in tf32, lo rounded to tf32 within 2^-10 |lo| <= 2^-20 |x|; the dropped
+// q_lo.c_lo term below 2^-20 |q_i c_i|), fp32 accumulation of the 3d products
+// inside the tensor core (at most 3d * 2^-23 of the absolute sum, allowing
+// truncating adds), the fp32 chain (d * 2^-24) and the final subtractions:
+//   |q3.c3 - q.c| <= (3 * 2^-20 + 3d * 2^-23 + d * 2^-24) |q| |c|, doubled for
+//   safety: eps = 6 * 2^-20 + d * (3 * 2^-22 + 2^-23),
+//   E = (2 eps |q| cmax + 2^-21 (cmax^2 + 2 |q| cmax)) * 1.01,
+// with cmax >= max |c|. Step 1 bounds t~ by T >= t~: the nprobe-th smallest of
+// the per-tile minima of s~ (nprobe distinct lists lie at or below it) when the
+// GEMM supplied at least nprobe of them, else the nprobe-th smallest of the
+// first SP_CAP scores. One pass then collects every s~ <= T + 2E (>= t~ + 2E);
+// those are sorted to find t~. If more than SP_CAP lists fall in the window the
+// row is rescored in full (in place) and selected exactly.
+__global__ void __launch_bounds__(SP_THREADS)
+select_probes_margin_kernel(float* __restrict__ s, const float* __restrict__ q_rot,
+                            const float* __restrict__ cents, const float* __restrict__ norms,
+                            const float* __restrict__ tile_min, int ntiles,
+                            int nlist, int d, int nprobe, float cmax,
+                            int32_t* __restrict__ probes) {
+    __shared__ uint64_t buf[SP_CAP];
+    __shared__ float qs[SPM_DMAX];
+    __shared__ float red[SP_THREADS / 32];
+    __shared__ unsigned int cnt, m_sh;
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float* row = s + (int64_t)q * nlist;
+    int32_t* out = probes + (int64_t)q * nprobe;
+    const float* qr = q_rot + (int64_t)q * d;
+    float ss = 0.0f;
+    for (int j = tid; j < d; j += SP_THREADS) {
+        const float v = qr[j];
+        qs[j] = v;
+        ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    if (tid == 0) { cnt = 0; m_sh = 0; }
+    __syncthreads();
+    float qn2 = 0.0f;
+    for (int w = 0; w < SP_THREADS / 32; ++w) qn2 += red[w];
+    const float qn = sqrtf(qn2) * 1.001f;
+    const float eps = 5.7220459e-06f + (float)d * 8.3446503e-07f;   // 6*2^-20 + d (3*2^-22 + 2^-23)
+    const float E = (2.0f * eps * qn * cmax + 4.7683716e-07f * (cmax * cmax + 2.0f * qn * cmax)) *
+                    1.01f;
+    const float twoE = 2.0f * E;
+
+    auto exact = [&](int c) {
+        const float4* cr = reinterpret_cast<const float4*>(cents + (int64_t)c * d);
+        float acc = 0.0f;
+        for (int j4 = 0; j4 < d / 4; ++j4) {
+            const float4 v = cr[j4];
+            acc = __fmaf_rn(qs[4 * j4 + 0], v.x, acc);
+            acc = __fmaf_rn(qs[4 * j4 + 1], v.y, acc);
+            acc = __fmaf_rn(qs[4 * j4 + 2], v.z, acc);
+            acc = __fmaf_rn(qs[4 * j4 + 3], v.w, acc);
+        }
+        return norms[c] - 2.0f * acc;
+    };
+
+    const bool use_tiles = tile_min && nlist > SP_CAP && ntiles >= nprobe && ntiles <= SP_CAP;
+    const float* src = use_tiles ? tile_min + (int64_t)q * ntiles : row;
+    const int n0 = use_tiles ? ntiles : min(nlist, SP_CAP);
+    int P = 1;
+    while (P < n0) P <<= 1;
+    for (int i = tid; i < P; i += SP_THREADS)
+        buf[i] = i < n0 ? (((uint64_t)float_order(src[i]) << 32) | (uint32_t)i) : KEY_EMPTY;
+    __syncthreads();
+    block_bitonic_sort(buf, P);
+    int n = n0;
+    if (nlist > SP_CAP) {
+        const float T = key_dist(buf[nprobe - 1]);
+        const float thr = __fadd_ru(T, twoE);
+        __syncthreads();
+        for (int c = tid; c < nlist; c += SP_THREADS) {
+            const float v = row[c];
+            if (v <= thr) {
+                const unsigned int pos = atomicAdd(&cnt, 1u);
+                if (pos < SP_CAP) buf[pos] = ((uint64_t)float_order(v) << 32) | (uint32_t)c;
+            }
+        }
+        __syncthreads();
+        n = (int)cnt;
+        if (n > SP_CAP) {                      // window too wide: rescore the row exactly
+            for (int c = tid; c < nlist; c += SP_THREADS) row[c] = exact(c);
+            __syncthreads();
+            select_row_exact(row, nlist, nprobe, out, buf);
+            return;
+        }
+        P = 1;
+        while (P < n) P <<= 1;
+        for (int i = n + tid; i < P; i += SP_THREADS) buf[i] = KEY_EMPTY;
+        __syncthreads();
+        block_bitonic_sort(buf, P);
+    }
+    const float thr2 = __fadd_ru(key_dist(buf[nprobe - 1]), twoE);
+    for (int i = tid; i < n; i += SP_THREADS)
+        if (key_dist(buf[i]) <= thr2 && (i + 1 == n || !(key_dist(buf[i + 1]) <= thr2)))
+            m_sh = (unsigned)(i + 1);
+    __syncthreads();
+    const int m = (int)m_sh;
+    for (int i = tid; i < m; i += SP_THREADS) {
+        const int c = key_id(buf[i]);
+        buf[i] = ((uint64_t)float_order(exact(c)) << 32) | (uint32_t)c;
+    }
+    P = 1;
+    while (P < m) P <<= 1;
+    for (int i = m + tid; i < P; i += SP_THREADS) buf[i] = KEY_EMPTY;
+    __syncthreads();
+    block_bitonic_sort(buf, P);
     for (int p = tid; p < nprobe; p += SP_THREADS) {
         const uint64_t e = buf[p];
         out[p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
@@ -259,6 +388,18 @@ void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probe
     if (nq <= 0) return;
     if (nprobe > SP_CAP) fail(JHQ_EINVAL, "select_probes: nprobe too large");
     select_probes_kernel<<<nq, SP_THREADS, 0, st>>>(s, nlist, nprobe, probes);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
+void select_probes_margin(float* s, const float* q_rot, const float* cents, const float* norms,
+                          const float* tile_min, int ntiles, int nq, int nlist, int d, int nprobe,
+                          float cmax, int32_t* probes, cudaStream_t st) {
+    if (nq <= 0) return;
+    if (nprobe > SP_CAP || nprobe > nlist) fail(JHQ_EINVAL, "select_probes_margin: bad nprobe");
+    if (d > SPM_DMAX || d % 4) fail(JHQ_EINVAL, "select_probes_margin: unsupported d");
+    select_probes_margin_kernel<<<nq, SP_THREADS, 0, st>>>(s, q_rot, cents, norms, tile_min,
+                                                           ntiles, nlist, d, nprobe, cmax, probes);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

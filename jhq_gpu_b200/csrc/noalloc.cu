@@ -80,7 +80,7 @@ void Index::search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_
     auto take = [&](size_t bytes) { size_t o = off; off = up256(off + bytes); return base + o; };
     BatchBufs b;
     b.q_rot = reinterpret_cast<float*>(take((size_t)Bq * d_ * 4));
-    b.scores = nl > 1 ? reinterpret_cast<float*>(take((size_t)Bq * nl * 4)) : nullptr;
+    b.scores = nl > 1 ? reinterpret_cast<float*>(take(coarse_scratch_floats(Bq) * 4)) : nullptr;
     b.probes = reinterpret_cast<int32_t*>(take((size_t)Bq * np * 4));
     b.plan.cnt = reinterpret_cast<int32_t*>(take((size_t)(nl + 1) * 4));
     b.plan.bucket_off = reinterpret_cast<int32_t*>(take((size_t)(nl + 1) * 4));

@@ -284,3 +284,60 @@ def test_set_trained_uses_reference_artefacts(jhq, oracle):
         prim_ref = lut_ref[np.arange(M)[None, :], codes[got]].sum(1)
         prim = lut[np.arange(M)[None, :], codes[got]].sum(1)
         np.testing.assert_allclose(prim, prim_ref, rtol=1e-4)
+
+
+def _probe_lists(jhq, d, nlist, nprobe, cents, q):
+    """probe_device lists of an index whose centroids are `cents` (identity rotation)."""
+    import torch
+    idx = jhq.JHQGpuIndex(d, jhq.Params(M=d // 4, nlist=nlist, nprobe=nprobe, batch_size=512))
+    rng = np.random.default_rng(5)
+    c1d = np.sort(rng.standard_normal(idx.K1D)).astype(np.float32)
+    res = np.sort(rng.standard_normal(idx.Kr) * 0.1).astype(np.float32)
+    idx.set_trained(np.eye(d, dtype=np.float32), c1d, res, cents, 1.0)
+    idx.add(_data(500, d, 6))
+    tq = torch.from_numpy(q).cuda()
+    pr = torch.empty((len(q), nprobe), dtype=torch.int32, device="cuda")
+    idx.probe_device(tq.data_ptr(), len(q), pr.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    idx.synchronize()                      # raises if a tensor-core wait gave up
+    return pr.cpu().numpy()
+
+
+def _unit(n, d, seed):
+    c = _data(n, d, seed)
+    return (c / np.linalg.norm(c, axis=1, keepdims=True)).astype(np.float32)
+
+
+@pytest.mark.parametrize("case", ["gauss_dups", "sphere_zero_query", "sphere_tiny_query",
+                                  "wide_small_nlist", "c3_shape"])
+def test_coarse_tensor_core_probes_equal_fp32(jhq, monkeypatch, case):
+    """Tensor-core coarse scores + margin selection give the same probe lists as
+    the fp32 SIMT GEMM + exact selection (itself bit-exact against the oracle),
+    including exact ties (duplicate centroids, all-equal scores) that send rows
+    through the full-rescore path."""
+    if case == "gauss_dups":
+        d, nlist, nprobe = 104, 5000, 64
+        cents = _data(nlist, d, 40)
+        cents[100:300] = cents[:200]
+        q = _data(700, d, 41)
+    elif case == "sphere_zero_query":
+        d, nlist, nprobe = 64, 8192, 32
+        cents = _unit(nlist, d, 42)
+        q = np.zeros((130, d), np.float32)
+    elif case == "sphere_tiny_query":
+        d, nlist, nprobe = 64, 8192, 32
+        cents = _unit(nlist, d, 43)
+        q = _data(257, d, 44, scale=1e-4)
+    elif case == "wide_small_nlist":
+        d, nlist, nprobe = 1024, 300, 16
+        cents = _data(nlist, d, 45)
+        q = _data(129, d, 46)
+    else:
+        d, nlist, nprobe = 128, 65536, 64
+        cents = _data(nlist, d, 47)
+        q = cents[:1000] + _data(1000, d, 48, scale=0.3)
+    monkeypatch.delenv("JHQ_COARSE", raising=False)
+    tc = _probe_lists(jhq, d, nlist, nprobe, cents, q)
+    monkeypatch.setenv("JHQ_COARSE", "simt")
+    ref = _probe_lists(jhq, d, nlist, nprobe, cents, q)
+    assert np.array_equal(tc, ref), np.argwhere(tc != ref)[:5]
