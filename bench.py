@@ -514,7 +514,7 @@ def run_sharded(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     n = args.db_size or cfg["n"]
-    nq, k = cfg["nq"], 10
+    nq, k = (args.queries or cfg["nq"]), 10
     # C4: bulk part, then `rounds` of (add round_size new vectors, search); the
     # rows of every block are split contiguously over the ranks
     rounds = args.rounds if args.config == "c4" else 0
@@ -522,7 +522,7 @@ def run_sharded(args):
     n_bulk = n - rounds * round_size
     lo, hi = contiguous_shard(n_bulk, ws, rank)
     p = J.Params(M=cfg["M"], B=8, Br=4, alpha=4.0, nlist=cfg["nlist"], nprobe=cfg["nprobe"],
-                 batch_size=cfg["batch"], add_batch=1 << 20, device=local)
+                 batch_size=min(cfg["batch"], nq), add_batch=1 << 20, device=local)
     idx = J.JHQGpuIndex(cfg["d"], p)
     t0 = time.perf_counter()
     idx.train(datasets.rows_torch(args.config, 0, min(n, 100_000), dev).cpu().numpy())
@@ -694,6 +694,8 @@ def main(argv=None):
                     help="c1 = the headline flat workload (default); c2 = IVF nprobe sweep; "
                          "c3 / c4 = 100M-vector sharded IVF (one process per GPU)")
     ap.add_argument("--db-size", type=int, default=0, help="c3/c4: database size (default 100M)")
+    ap.add_argument("--queries", type=int, default=0,
+                    help="c3/c4: query count (default 10k; smaller for profiling captures)")
     ap.add_argument("--rounds", type=int, default=10,
                     help="c4: interleaved (add 1M, search) rounds after the bulk add")
     ap.add_argument("--profile-run", action="store_true",

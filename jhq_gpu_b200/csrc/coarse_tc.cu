@@ -1,41 +1,50 @@
 // coarse_tc.cu — approximate IVF coarse scores on the 5th-generation tensor
-// cores (tcgen05.mma kind::tf32, accumulator in TMEM, operands staged by TMA).
+// cores (tcgen05.mma kind::f16 with bf16 operands, fp32 accumulator in TMEM,
+// operands staged by TMA).
 //
-//   s~[q][c] = |c|^2 - 2 * (q3[q] . c3[c])      (tf32 inputs, fp32 sums)
+//   s~[q][c] = |c|^2 - 2 * (q3[q] . c3[c])      (bf16 inputs, fp32 sums)
 //
-// with the 3-term tf32 split of each fp32 value x = hi + lo (hi = x with its 13
-// low mantissa bits cleared, lo = x - hi, exact): the rows are laid out as
-//   q3 = [q_hi | q_hi | q_lo],  c3 = [c_hi | c_lo | c_hi]   (K = 3d),
-// so one GEMM over K = 3d sums q_hi.c_hi + q_hi.c_lo + q_lo.c_hi, which misses
-// only q_lo.c_lo (< 2^-20 |q_i c_i|). The scores are approximate within a
-// bound that select_probes_margin (ivf.cu) states and turns into the EXACT
-// top-nprobe lists of the
+// with a 2-piece bf16 split of each fp32 value, x = hi + lo + r (hi = bf16
+// round-to-nearest-even of x, lo = the same rounding of x - hi, which is exact
+// in fp32, |r| <= 2^-18 |x|); the rows are laid out as
+//   q3 = [q_hi | q_hi | q_lo],  c3 = [c_hi | c_lo | c_hi]   (K = 3d, zero-padded to K3)
+// so one GEMM over K3 sums q_hi.c_hi + q_hi.c_lo + q_lo.c_hi (bf16 products
+// are exact in fp32), within about 3 * 2^-18 |q_i c_i| of each product. The
+// scores are approximate within a bound that select_probes_margin (ivf.cu)
+// states and turns into the EXACT top-nprobe lists of the
 // fp32 fma-chain scores (the order the reference's coarse GEMM + selection
 // define, jhq_v14_streaming_add/search.cu:13-62), so the probe lists stay
 // bit-identical to the fp32 path while the contraction runs on tensor cores.
 //
-// Tiling: one CTA per 128-query x 256-centroid tile, 128 threads, K in chunks of 32.
-//   warp 0 lane 0   TMA producer: K chunks of 32 fp32 (one 128-byte swizzle
-//                   row) of the query tile [128][32] and centroid tile
-//                   [256][32], double-buffered in shared memory (2 x 48 KB);
-//   warp 1 lane 0   MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=8) per chunk
-//                   into a 256-column fp32 accumulator in TMEM; tcgen05.commit
-//                   frees the stage, a last commit signals the epilogue;
-//   warps 0-3       epilogue: tcgen05.ld 32x32b (warp w owns TMEM lanes
-//                   32w..32w+31 = tile rows), transposed through shared memory
-//                   so each warp stores 128-byte row segments of s~; each row's
-//                   minimum over the tile goes to tile_min [nq][ntiles] (the
-//                   selection's threshold bound).
-// Two CTAs fit per SM (2 x 97 KB shared, 2 x 256 TMEM columns), so one CTA's
-// epilogue overlaps the other's loads and MMAs.
+// Persistent kernel, one CTA per SM (192 threads), over 128-query x 256-list
+// output tiles (tile t = query tile t % mt, list tile t / mt, so the CTAs
+// resident together share one list tile and each is read from HBM about once):
+//   warp 0 lane 0   TMA producer: K chunks of 64 bf16 (one 128-byte swizzle
+//                   row) of the query tile [128][64] and list tile [256][64]
+//                   into a 4-stage ring (4 x 48 KB);
+//   warp 1 lane 0   MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per chunk
+//                   into one of two 256-column fp32 accumulators in TMEM
+//                   (512 columns), tcgen05.commit frees each stage and, after
+//                   a tile's last chunk, hands the accumulator to the epilogue;
+//   warps 2-9       epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
+//                   32 (w % 4) .. +31 = tile rows, warps w and w + 4 split the
+//                   256 columns into two 128-list groups), transposed through
+//                   shared memory so each warp stores 128-byte row segments of
+//                   s~; each row's minimum over its group goes to tile_min
+//                   [nq][ngroups] (the selection's threshold bound); then the
+//                   accumulator is released to the MMA warp.
+// The epilogue of tile i overlaps the loads and MMAs of tile i + 1.
 //
 // Every mbarrier wait is bounded (about a second of clock cycles); a wait that
-// gives up sets g_tc_error, the CTA stops issuing work, waits (bounded) for
-// the copies and MMAs it already issued, frees its TMEM and returns.
+// gives up sets g_tc_error and a shared abort flag that ends every role's
+// loop; the producer then waits (bounded) for the copies it issued, the MMA
+// warp for its MMAs (a final commit), and the CTA frees its TMEM and returns.
 // No TMA load here uses cluster multicast; the operands are this GPU's own memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <climits>
 #include <cstring>
 #include <mutex>
 
@@ -48,22 +57,30 @@ __device__ int g_tc_error;
 
 namespace {
 
-constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 32;
-constexpr int TC_STAGES = 2;
-constexpr int TC_THREADS = 128;
-constexpr int TC_A_BYTES = TC_BM * TC_BK * 4;              // 16 KB
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 4;              // 32 KB
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64;       // BK in bf16 elements
+constexpr int TC_STAGES = 4;
+constexpr int TC_EPI_WARPS = 8;                            // two per TMEM lane quarter
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
+constexpr int TC_EPI_THREADS = 32 * TC_EPI_WARPS;
+constexpr int TC_GROUP = COARSE_TILE_LISTS;                // lists per tile_min entry
+static_assert(TC_BN == 2 * TC_GROUP, "each epilogue warp of a quarter owns one group");
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;              // 16 KB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;              // 32 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024 + 128;
-constexpr uint32_t TC_TMEM_COLS = 256;
-// Instruction descriptor: fp32 accumulate (bit 4), A and B tf32 (bits 7-9,
-// 10-12 = 2), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t TC_IDESC = (1u << 4) | (2u << 7) | (2u << 10) |
+constexpr int TC_EPI_BYTES = TC_EPI_WARPS * 32 * 32 * 4;   // per-warp 32 x 32 transposition
+constexpr int TC_NBARS = 2 * TC_STAGES + 2 + 2 + 1;        // full, empty, tfull, tempty, drain
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + TC_EPI_BYTES + 1024 + 256;
+constexpr uint32_t TC_TMEM_COLS = 512;
+static_assert(TC_NBARS * 8 + 16 <= 256, "barrier area");
+// Instruction descriptor: fp32 accumulate (bit 4), A and B bf16 (bits 7-9,
+// 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
                               ((uint32_t)(TC_BN >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
 constexpr long long TC_WAIT_CYCLES = 1ll << 31;
 
-__device__ __forceinline__ float tf32_hi(float v) {
-    return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+// bf16 bits of x, rounded to nearest even (finite x).
+__host__ __device__ __forceinline__ uint16_t bf16_rne(uint32_t u) {
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -80,13 +97,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase of parity `parity` to complete.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase of parity `parity`; gives up (false) when the
+// CTA's abort flag is set or after TC_WAIT_CYCLES, which sets the flag.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity)) {
+        if (abort && *abort) return false;
         if (clock64() - t0 > TC_WAIT_CYCLES) {
             atomicExch(&g_tc_error, 1);
+            if (abort) *abort = 1;
             return false;
         }
     }
@@ -109,31 +129,36 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         :: "r"(dst), "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar) : "memory");
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 2)
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(bar) : "memory");
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
 coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
                  const float* __restrict__ norms, float* __restrict__ scores,
-                 float* __restrict__ tile_min, int nq, int nlist, int K) {
+                 float* __restrict__ tile_min, int nq, int nlist, int K, int mt, int ntiles) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ float nrm_s[TC_BN];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + TC_STAGES * TC_STAGE_BYTES);   // full[S] empty[S] done
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * TC_STAGES + 1);
-    int* flags = (int*)(tmem_slot + 1);                                 // abort, issued
+    float* epi = (float*)(smem + TC_STAGES * TC_STAGE_BYTES);
+    uint64_t* bars = (uint64_t*)(smem + TC_STAGES * TC_STAGE_BYTES + TC_EPI_BYTES);
+    uint32_t* tmem_slot = (uint32_t*)(bars + TC_NBARS);
+    volatile int* abort = (volatile int*)(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
     const int nk = (K + TC_BK - 1) / TC_BK;
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + TC_STAGES),
-                   done = smem_u32(bars + 2 * TC_STAGES);
+    const int ngr = (nlist + TC_GROUP - 1) / TC_GROUP;    // tile_min row length
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * TC_STAGES,
+                   tfull0 = empty0 + 8 * TC_STAGES, tempty0 = tfull0 + 16, drain = tempty0 + 16;
 
     if (tid == 0) {
-        for (int s = 0; s < 2 * TC_STAGES + 1; ++s)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(smem_u32(bars + s)));
+        for (int i = 0; i < TC_NBARS; ++i) {
+            const uint32_t a = full0 + 8 * i;
+            const uint32_t cnt = (a >= tempty0 && a < drain) ? TC_EPI_THREADS : 1;
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(a), "r"(cnt));
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        flags[0] = 0;
-        flags[1] = 0;
+        *abort = 0;
     }
-    for (int i = tid; i < TC_BN; i += TC_THREADS)
-        nrm_s[i] = n0 + i < nlist ? norms[n0 + i] : __int_as_float(0x7f800000);   // +inf
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(tmem_slot)), "r"(TC_TMEM_COLS));
@@ -144,96 +169,157 @@ coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {                       // TMA producer
-        for (int kc = 0; kc < nk; ++kc) {
-            const int s = kc % TC_STAGES;
-            if (kc >= TC_STAGES && !mbar_wait(empty0 + 8 * s, ((kc / TC_STAGES) - 1) & 1)) {
-                flags[0] = 1;
-                break;
+    if (warp == 0) {
+        if (lane == 0) {                                   // TMA producer
+            int it = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+                const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * TC_BN;
+                for (int kc = 0; kc < nk; ++kc, ++it) {
+                    const int s = it % TC_STAGES;
+                    if (it >= TC_STAGES &&
+                        !mbar_wait(empty0 + 8 * s, ((it / TC_STAGES) - 1) & 1, abort))
+                        break;
+                    const uint32_t fb = full0 + 8 * s;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                                 :: "r"(fb), "r"((uint32_t)TC_STAGE_BYTES) : "memory");
+                    const uint32_t a_s = smem_u32(smem + s * TC_STAGE_BYTES);
+                    tma_load_2d(a_s, &map_q, kc * TC_BK, m0, fb);
+                    tma_load_2d(a_s + TC_A_BYTES, &map_c, kc * TC_BK, n0, fb);
+                }
             }
-            if (*(volatile int*)&flags[0]) break;
-            const uint32_t fb = full0 + 8 * s;
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                         :: "r"(fb), "r"((uint32_t)TC_STAGE_BYTES) : "memory");
-            const uint32_t a_s = smem_u32(smem + s * TC_STAGE_BYTES);
-            tma_load_2d(a_s, &map_q, kc * TC_BK, m0, fb);
-            tma_load_2d(a_s + TC_A_BYTES, &map_c, kc * TC_BK, n0, fb);
-            flags[1] = kc + 1;
+            if (*abort)   // copies still in flight land before the shared memory is released
+                for (int j = it > TC_STAGES ? it - TC_STAGES : 0; j < it; ++j)
+                    mbar_wait(full0 + 8 * (j % TC_STAGES), (j / TC_STAGES) & 1, nullptr);
         }
-    } else if (warp == 1 && lane == 0) {                // MMA issuer
-        for (int kc = 0; kc < nk; ++kc) {
-            const int s = kc % TC_STAGES;
-            if (!mbar_wait(full0 + 8 * s, (kc / TC_STAGES) & 1)) {
-                *(volatile int*)&flags[0] = 1;
-                break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a_s = smem_u32(smem + s * TC_STAGE_BYTES);
-            const uint64_t da = sw128_desc(a_s), db = sw128_desc(a_s + TC_A_BYTES);
+    } else if (warp == 1) {
+        if (lane == 0) {                                   // MMA issuer
+            int it = 0, i = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * TC_BN);
+                bool ok = true;
+                for (int kc = 0; kc < nk; ++kc, ++it) {
+                    const int s = it % TC_STAGES;
+                    if (!mbar_wait(full0 + 8 * s, (it / TC_STAGES) & 1, abort)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a_s = smem_u32(smem + s * TC_STAGE_BYTES);
+                    const uint64_t da = sw128_desc(a_s), db = sw128_desc(a_s + TC_A_BYTES);
 #pragma unroll
-            for (int k = 0; k < TC_BK / 8; ++k) {
-                // +32 bytes per K=8 step inside the swizzle row (start address in 16-byte units)
-                const uint32_t acc = (kc | k) != 0;
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-                    :: "r"(tmem), "l"(da + 2 * k), "l"(db + 2 * k), "r"(TC_IDESC), "r"(acc));
+                    for (int k = 0; k < TC_BK / 16; ++k) {
+                        // +32 bytes per K=16 step inside the swizzle row (16-byte units)
+                        const uint32_t accum = (kc | k) != 0;
+                        asm volatile(
+                            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(db + 2 * k), "r"(TC_IDESC),
+                               "r"(accum));
+                    }
+                    mma_commit(empty0 + 8 * s);
+                }
+                if (!ok) break;
+                mma_commit(tfull0 + 8 * acc);
             }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         :: "r"(empty0 + 8 * s) : "memory");
+            mma_commit(drain);                             // every MMA issued has completed
+            mbar_wait(drain, 0, nullptr);
         }
-        // Always signal: the epilogue's wait then covers every MMA issued.
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                     :: "r"(done) : "memory");
+    } else {                                               // epilogue, warps 2..9
+        const int q4 = warp & 3;                           // TMEM lane quarter
+        const int half = (warp - 2) >> 2;                  // column half = list group
+        float* tile = epi + (warp - 2) * (32 * 32);
+        const bool vec = (nlist & 3) == 0;                 // 16-byte row segments
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            const bool ok = mbar_wait(tfull0 + 8 * acc, (i >> 1) & 1, abort);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * TC_BN;
+            const int row0 = m0 + q4 * 32;
+            // store layout: lane = (row sub-index rsub, 4-column group cg); a
+            // warp instruction covers 4 rows x 32 columns (four 128-byte segments)
+            const int cg = lane & 7, rsub = lane >> 3;
+            float rmin[8];
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) rmin[rr] = __int_as_float(0x7f800000);
+            for (int cb = half * TC_GROUP; cb < (half + 1) * TC_GROUP && n0 + cb < nlist; cb += 32) {
+                uint32_t r[32];
+                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) +
+                                       (uint32_t)(acc * TC_BN + cb);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                      "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+                      "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
+                      "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+                      "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                      "=r"(r[30]), "=r"(r[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                // row layout (thread = row) -> shared memory; 16-byte chunk k of
+                // row l sits at chunk k ^ (l & 7), conflict-free both ways
+                float4* trow = reinterpret_cast<float4*>(tile + lane * 32);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    trow[k ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                                          __uint_as_float(r[4 * k + 2]), __uint_as_float(r[4 * k + 3]));
+                __syncwarp();
+                const int col = n0 + cb + 4 * cg;
+                const float inf = __int_as_float(0x7f800000);
+                float4 nv;
+                if (vec && col + 3 < nlist) {
+                    nv = *reinterpret_cast<const float4*>(norms + col);
+                } else {
+                    nv.x = col < nlist ? norms[col] : inf;
+                    nv.y = col + 1 < nlist ? norms[col + 1] : inf;
+                    nv.z = col + 2 < nlist ? norms[col + 2] : inf;
+                    nv.w = col + 3 < nlist ? norms[col + 3] : inf;
+                }
+#pragma unroll
+                for (int rr = 0; rr < 8; ++rr) {
+                    const int rl = rr * 4 + rsub;
+                    const float4 a4 =
+                        *reinterpret_cast<const float4*>(tile + rl * 32 + 4 * (cg ^ (rl & 7)));
+                    float4 sv;
+                    sv.x = nv.x - 2.0f * a4.x;
+                    sv.y = nv.y - 2.0f * a4.y;
+                    sv.z = nv.z - 2.0f * a4.z;
+                    sv.w = nv.w - 2.0f * a4.w;
+                    rmin[rr] = fminf(rmin[rr], fminf(fminf(sv.x, sv.y), fminf(sv.z, sv.w)));
+                    const int row = row0 + rl;
+                    if (row < nq) {
+                        float* dst = scores + (int64_t)row * nlist + col;
+                        if (vec && col + 3 < nlist) {
+                            *reinterpret_cast<float4*>(dst) = sv;
+                        } else {
+                            if (col < nlist) dst[0] = sv.x;
+                            if (col + 1 < nlist) dst[1] = sv.y;
+                            if (col + 2 < nlist) dst[2] = sv.z;
+                            if (col + 3 < nlist) dst[3] = sv.w;
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            const int g = (t / mt) * 2 + half;
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) {
+                float m = rmin[rr];
+                m = fminf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                m = fminf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                m = fminf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+                const int row = row0 + rr * 4 + rsub;
+                if (cg == 0 && row < nq && g < ngr) tile_min[(int64_t)row * ngr + g] = m;
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(tempty0 + 8 * acc)
+                         : "memory");
+        }
     }
     __syncwarp();
-
-    // ---- epilogue ----
-    const bool ok = mbar_wait(done, 0);
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    __syncthreads();
-    const bool run = ok && !*(volatile int*)&flags[0];
-    if (run) {
-        float* tile = (float*)smem + warp * (32 * 33);
-        const int row0 = m0 + warp * 32;
-        float rmin = __int_as_float(0x7f800000);       // this thread's row over the tile
-        for (int cb = 0; cb < TC_BN && n0 + cb < nlist; cb += 32) {
-            uint32_t r[32];
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
-                  "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
-                  "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]),
-                  "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-                  "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-                  "=r"(r[30]), "=r"(r[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float sv = nrm_s[cb + j] - 2.0f * __uint_as_float(r[j]);   // +inf past nlist
-                tile[lane * 33 + j] = sv;
-                rmin = fminf(rmin, sv);
-            }
-            __syncwarp();
-            const int col = n0 + cb + lane;
-            for (int rr = 0; rr < 32; ++rr) {
-                const int row = row0 + rr;
-                if (row < nq && col < nlist) scores[(int64_t)row * nlist + col] = tile[rr * 33 + lane];
-            }
-            __syncwarp();
-        }
-        if (row0 + lane < nq) tile_min[(int64_t)(row0 + lane) * gridDim.x + blockIdx.x] = rmin;
-    }
-    if (tid == 0 && !run) {
-        // Copies still in flight land before the shared memory is released.
-        const int issued = flags[1];
-        for (int kc = (issued > TC_STAGES ? issued - TC_STAGES : 0); kc < issued; ++kc)
-            mbar_wait(full0 + 8 * (kc % TC_STAGES), (kc / TC_STAGES) & 1);
-    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
@@ -255,29 +341,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// Rows of x -> [hi | hi | lo] rows of out (n x 3d).
-__global__ void split3_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ out) {
+// Rows of x -> [hi | hi | lo | 0...] bf16 rows of out (n x K3).
+__global__ void split3_kernel(const float* __restrict__ x, int64_t n, int d, int K3,
+                              uint16_t* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n * d) return;
-    const int64_t r = i / d;
-    const int j = (int)(i - r * d);
-    const float v = x[i];
-    const float hi = tf32_hi(v);
-    float* o = out + r * 3 * d;
-    o[j] = hi;
-    o[d + j] = hi;
-    o[2 * d + j] = v - hi;
+    if (i >= n * K3) return;
+    const int64_t r = i / K3;
+    const int j = (int)(i - r * K3);
+    const int part = j / d, jj = j - part * d;
+    uint16_t v = 0;
+    if (part < 3) {
+        const float xv = x[r * d + jj];
+        const uint16_t hi = bf16_rne(__float_as_uint(xv));
+        v = part < 2 ? hi : bf16_rne(__float_as_uint(xv - __uint_as_float((uint32_t)hi << 16)));
+    }
+    out[i] = v;
 }
 
-// [rows][d] fp32 row-major, boxes of box_rows x 32 floats, 128-byte swizzle,
-// zero fill outside the array (rows >= rows, columns >= d).
-CUtensorMap make_map(const float* base, int64_t rows, int d, int box_rows) {
+// [rows][K] bf16 row-major, boxes of box_rows x 64 elements, 128-byte swizzle,
+// zero fill outside the array.
+CUtensorMap make_map(const uint16_t* base, int64_t rows, int K, int box_rows) {
     CUtensorMap m;
-    const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)d * 4};
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims,
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims,
                                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -287,30 +376,35 @@ CUtensorMap make_map(const float* base, int64_t rows, int d, int box_rows) {
 
 }  // namespace
 
-bool coarse_tc_supported(int d, int nlist) {
-    // TMA: row stride 3d*4 a multiple of 16 bytes; 16-byte aligned bases.
-    return d % 4 == 0 && d >= 4 && nlist >= 1;
-}
+bool coarse_tc_supported(int d, int nlist) { return d >= 1 && nlist >= 1; }
 
-void split3_rows(const float* x, int64_t n, int d, float* out, cudaStream_t s) {
+int coarse_tc_k3(int d) { return (3 * d + 7) / 8 * 8; }   // 16-byte row stride for TMA
+
+void split3_rows(const float* x, int64_t n, int d, uint16_t* out, cudaStream_t s) {
     if (n <= 0) return;
-    const int64_t tot = n * d;
-    split3_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(x, n, d, out);
+    const int K3 = coarse_tc_k3(d);
+    const int64_t tot = n * K3;
+    split3_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(x, n, d, K3, out);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }
 
-void split3_rows_host(const float* x, int64_t n, int d, int order, float* out) {
+void split3_rows_host(const float* x, int64_t n, int d, int order, uint16_t* out) {
+    const int K3 = coarse_tc_k3(d);
     for (int64_t r = 0; r < n; ++r) {
-        float* o = out + r * 3 * d;
+        uint16_t* o = out + r * K3;
+        for (int j = 0; j < K3; ++j) o[j] = 0;
         for (int j = 0; j < d; ++j) {
             const float v = x[r * d + j];
             uint32_t u;
             std::memcpy(&u, &v, 4);
-            u &= 0xFFFFE000u;
-            float hi;
-            std::memcpy(&hi, &u, 4);
-            const float lo = v - hi;
+            const uint16_t hi = bf16_rne(u);
+            const uint32_t hu = (uint32_t)hi << 16;
+            float hf;
+            std::memcpy(&hf, &hu, 4);
+            const float rest = v - hf;
+            std::memcpy(&u, &rest, 4);
+            const uint16_t lo = bf16_rne(u);
             o[j] = hi;
             o[d + j] = order == 0 ? hi : lo;
             o[2 * d + j] = order == 0 ? lo : hi;
@@ -318,25 +412,30 @@ void split3_rows_host(const float* x, int64_t n, int d, int order, float* out) {
     }
 }
 
-int coarse_tc_tiles(int nlist) { return (nlist + TC_BN - 1) / TC_BN; }
+int coarse_tc_tiles(int nlist) { return (nlist + TC_GROUP - 1) / TC_GROUP; }
 
-void coarse_scores_tc(const float* q3, int nq, const float* c3, const float* norms, int nlist,
-                      int d, float* scores, float* tile_min, cudaStream_t s) {
+void coarse_scores_tc(const uint16_t* q3, int nq, const uint16_t* c3, const float* norms,
+                      int nlist, int d, float* scores, float* tile_min, cudaStream_t s) {
     if (nq <= 0) return;
     if (!coarse_tc_supported(d, nlist) || ((uintptr_t)q3 | (uintptr_t)c3) % 16)
         fail(JHQ_EINVAL, "coarse_scores_tc: unsupported shape or alignment");
-    const int gy = (nq + TC_BM - 1) / TC_BM;
-    if (gy > 65535) fail(JHQ_EINVAL, "coarse_scores_tc: too many queries in one call");
+    const int mt = (nq + TC_BM - 1) / TC_BM, nlt = (nlist + TC_BN - 1) / TC_BN;   // MMA tiles
+    const int64_t ntiles = (int64_t)mt * nlt;
+    if (ntiles > INT32_MAX) fail(JHQ_EINVAL, "coarse_scores_tc: too many tiles");
     static std::once_flag attr;
     std::call_once(attr, [] {
         JHQ_CUDA(cudaFuncSetAttribute(coarse_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       TC_SMEM));
     });
-    const CUtensorMap mq = make_map(q3, nq, 3 * d, TC_BM);
-    const CUtensorMap mc = make_map(c3, nlist, 3 * d, TC_BN);
-    dim3 grid((unsigned)((nlist + TC_BN - 1) / TC_BN), (unsigned)gy);
+    int dev = 0, nsm = 0;
+    JHQ_CUDA(cudaGetDevice(&dev));
+    JHQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    const int K3 = coarse_tc_k3(d);
+    const CUtensorMap mq = make_map(q3, nq, K3, TC_BM);
+    const CUtensorMap mc = make_map(c3, nlist, K3, TC_BN);
+    const int grid = (int)std::min<int64_t>(ntiles, nsm);
     coarse_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(mq, mc, norms, scores, tile_min, nq, nlist,
-                                                       3 * d);
+                                                       K3, mt, (int)ntiles);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

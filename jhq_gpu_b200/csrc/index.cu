@@ -149,7 +149,7 @@ void Index::upload_trained() {
     if (coarse_tc_) {
         dcents_.resize((size_t)nl * d_);
         h2d(dcents_.get(), cents_.data(), (size_t)nl * d_, stream_);
-        std::vector<float> c3((size_t)nl * 3 * d_);
+        std::vector<uint16_t> c3((size_t)nl * coarse_tc_k3(d_));
         split3_rows_host(cents_.data(), nl, d_, 1, c3.data());
         dcents3_.resize(c3.size());
         h2d(dcents3_.get(), c3.data(), c3.size(), stream_);
@@ -488,14 +488,17 @@ void Index::prepare_workspace(int k) {
 size_t Index::coarse_scratch_floats(int Bq) const {
     if (p_.nlist <= 1) return 0;
     const size_t sc = ((size_t)Bq * p_.nlist + 63) & ~(size_t)63;   // split rows 256-byte aligned
-    return sc + (coarse_tc_ ? (size_t)Bq * 3 * d_ + (size_t)Bq * coarse_tc_tiles(p_.nlist) : 0);
+    // then the bf16 split queries (Bq x K3, rounded to 64 floats), then tile minima
+    const size_t q3f = (((size_t)Bq * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63;
+    return sc + (coarse_tc_ ? q3f + (size_t)Bq * coarse_tc_tiles(p_.nlist) : 0);
 }
 
 void Index::coarse_probes(const float* q_rot, int nq, int Bq, int nprobe, float* scores,
                           int32_t* probes, cudaStream_t s) {
     if (coarse_tc_) {
-        float* q3 = scores + (((size_t)Bq * p_.nlist + 63) & ~(size_t)63);
-        float* tmin = q3 + (size_t)Bq * 3 * d_;
+        float* q3f = scores + (((size_t)Bq * p_.nlist + 63) & ~(size_t)63);
+        uint16_t* q3 = reinterpret_cast<uint16_t*>(q3f);
+        float* tmin = q3f + ((((size_t)Bq * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63);
         const int nt = coarse_tc_tiles(p_.nlist);
         split3_rows(q_rot, nq, d_, q3, s);
         coarse_scores_tc(q3, nq, dcents3_.get(), dnorms_.get(), p_.nlist, d_, scores, tmin, s);

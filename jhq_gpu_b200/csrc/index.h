@@ -149,7 +149,8 @@ private:
     int64_t stage_batches_ = 0;
     cudaEvent_t prof_ev_[6] = {};
 
-    DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dcents_, dcents3_, dnorms_;
+    DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dcents_, dnorms_;
+    DevBuf<uint16_t> dcents3_;         // bf16 split centroids [nlist][K3]
     DevBuf<float> dassign_scratch_;    // tensor-core assignment: scores of a row block
     float cmax_ = 0.0f;                // >= max |centroid| (coarse margin)
     bool coarse_tc_ = false;

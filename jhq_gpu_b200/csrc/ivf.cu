@@ -9,6 +9,7 @@
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace jhq {
 namespace {
@@ -16,6 +17,7 @@ namespace {
 constexpr int SP_THREADS = 512;
 constexpr int SP_CAP = 4096;                 // keys held in shared memory per query
 constexpr int SPM_DMAX = 2048;               // largest d of select_probes_margin
+constexpr int TL_CAP = 1024;                 // candidate tiles read selectively
 
 // Exact top-nprobe of one score row by (score, list id) — composite uint64
 // keys (order-preserving score << 32 | id) make the order a plain integer one.
@@ -82,6 +84,47 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t
     select_row_exact(s + (int64_t)q * nlist, nlist, nprobe, probes + (int64_t)q * nprobe, buf);
 }
 
+// 2E of select_probes_margin for |q|^2 = qn2 (the bound is derived there).
+__device__ __forceinline__ float coarse_margin2(float qn2, int d, float cmax) {
+    const float qn = sqrtf(qn2) * 1.001f;
+    const float eps = 2.2888184e-05f + (float)d * 8.3446503e-07f;   // 6*2^-18 + d (3*2^-22 + 2^-23)
+    const float E = (2.0f * eps * qn * cmax + 4.7683716e-07f * (cmax * cmax + 2.0f * qn * cmax)) *
+                    1.01f;
+    return 2.0f * E;
+}
+
+// The fp32 chain score norms[c] - 2 * fma-chain_j(q[j] * cent_c[j]), j ascending
+// (the order of gemm_rows' EPI_COARSE and of the oracle).
+__device__ __forceinline__ float exact_coarse(const float* q, const float* __restrict__ cents,
+                                              const float* __restrict__ norms, int c, int d) {
+    float acc = 0.0f;
+    if (d % 4) {
+        const float* cr = cents + (int64_t)c * d;
+        for (int j = 0; j < d; ++j) acc = __fmaf_rn(q[j], cr[j], acc);
+        return norms[c] - 2.0f * acc;
+    }
+    // eight 16-byte loads in flight per round; the fma chain stays in order
+    const float4* cr = reinterpret_cast<const float4*>(cents + (int64_t)c * d);
+    const int d4 = d / 4;
+    for (int j0 = 0; j0 < d4; j0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (j0 + u < d4) v[u] = __ldg(cr + j0 + u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            if (j0 + u < d4) {
+                const float* qq = q + 4 * (j0 + u);
+                acc = __fmaf_rn(qq[0], v[u].x, acc);
+                acc = __fmaf_rn(qq[1], v[u].y, acc);
+                acc = __fmaf_rn(qq[2], v[u].z, acc);
+                acc = __fmaf_rn(qq[3], v[u].w, acc);
+            }
+        }
+    }
+    return norms[c] - 2.0f * acc;
+}
+
 // Exact top-nprobe from APPROXIMATE scores s~ (the tensor-core coarse GEMM,
 // coarse_tc.cu). With |s~_c - s_c| <= E for every list c (s = the fp32 chain
 // score norms[c] - 2 * fma-chain(q, cent_c)), and t~ the nprobe-th smallest s~:
@@ -89,18 +132,19 @@ select_probes_kernel(const float* __restrict__ s, int nlist, int nprobe, int32_t
 //   nprobe lists with s~ <= t~ have s <= t~ + E), so s~_w <= s_w + E <= t~ + 2E.
 // Hence the lists with s~ <= t~ + 2E contain every winner; they are rescored
 // with the exact chain and the exact (s, list id) order picks the winners.
-// E bounds, for the 3-term tf32 split of coarse_tc.cu (x = hi + lo; hi exact
-// in tf32, lo rounded to tf32 within 2^-10 |lo| <= 2^-20 |x|; the dropped
-// q_lo.c_lo term below 2^-20 |q_i c_i|), fp32 accumulation of the 3d products
-// inside the tensor core (at most 3d * 2^-23 of the absolute sum, allowing
-// truncating adds), the fp32 chain (d * 2^-24) and the final subtractions:
-//   |q3.c3 - q.c| <= (3 * 2^-20 + 3d * 2^-23 + d * 2^-24) |q| |c|, doubled for
-//   safety: eps = 6 * 2^-20 + d * (3 * 2^-22 + 2^-23),
+// E bounds, for the bf16 split of coarse_tc.cu (x = hi + lo + r with
+// |r| <= 2^-18 |x|; the three bf16 products are exact in fp32 and come within
+// 3 * 2^-18 |q_i c_i| of q_i c_i), fp32 accumulation of the 3d products inside
+// the tensor core (at most 3d * 2^-23 of the absolute sum, allowing truncating
+// adds), the fp32 chain (d * 2^-24) and the final subtractions:
+//   |q3.c3 - q.c| <= (3 * 2^-18 + 3d * 2^-23 + d * 2^-24) |q| |c|, doubled for
+//   safety: eps = 6 * 2^-18 + d * (3 * 2^-22 + 2^-23),
 //   E = (2 eps |q| cmax + 2^-21 (cmax^2 + 2 |q| cmax)) * 1.01,
 // with cmax >= max |c|. Step 1 bounds t~ by T >= t~: the nprobe-th smallest of
 // the per-tile minima of s~ (nprobe distinct lists lie at or below it) when the
 // GEMM supplied at least nprobe of them, else the nprobe-th smallest of the
-// first SP_CAP scores. One pass then collects every s~ <= T + 2E (>= t~ + 2E);
+// first SP_CAP scores. One pass then collects every s~ <= T + 2E (>= t~ + 2E),
+// reading only the tiles whose minimum is within that bound when tile minima exist;
 // those are sorted to find t~. If more than SP_CAP lists fall in the window the
 // row is rescored in full (in place) and selected exactly.
 __global__ void __launch_bounds__(SP_THREADS)
@@ -108,11 +152,13 @@ select_probes_margin_kernel(float* __restrict__ s, const float* __restrict__ q_r
                             const float* __restrict__ cents, const float* __restrict__ norms,
                             const float* __restrict__ tile_min, int ntiles,
                             int nlist, int d, int nprobe, float cmax,
-                            int32_t* __restrict__ probes) {
+                            int32_t* __restrict__ probes, int only_flagged) {
+    if (only_flagged && probes[(int64_t)blockIdx.x * nprobe] != -1) return;
     __shared__ uint64_t buf[SP_CAP];
     __shared__ float qs[SPM_DMAX];
     __shared__ float red[SP_THREADS / 32];
     __shared__ unsigned int cnt, m_sh;
+    __shared__ int tl[TL_CAP];
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* row = s + (int64_t)q * nlist;
     int32_t* out = probes + (int64_t)q * nprobe;
@@ -130,24 +176,8 @@ select_probes_margin_kernel(float* __restrict__ s, const float* __restrict__ q_r
     __syncthreads();
     float qn2 = 0.0f;
     for (int w = 0; w < SP_THREADS / 32; ++w) qn2 += red[w];
-    const float qn = sqrtf(qn2) * 1.001f;
-    const float eps = 5.7220459e-06f + (float)d * 8.3446503e-07f;   // 6*2^-20 + d (3*2^-22 + 2^-23)
-    const float E = (2.0f * eps * qn * cmax + 4.7683716e-07f * (cmax * cmax + 2.0f * qn * cmax)) *
-                    1.01f;
-    const float twoE = 2.0f * E;
-
-    auto exact = [&](int c) {
-        const float4* cr = reinterpret_cast<const float4*>(cents + (int64_t)c * d);
-        float acc = 0.0f;
-        for (int j4 = 0; j4 < d / 4; ++j4) {
-            const float4 v = cr[j4];
-            acc = __fmaf_rn(qs[4 * j4 + 0], v.x, acc);
-            acc = __fmaf_rn(qs[4 * j4 + 1], v.y, acc);
-            acc = __fmaf_rn(qs[4 * j4 + 2], v.z, acc);
-            acc = __fmaf_rn(qs[4 * j4 + 3], v.w, acc);
-        }
-        return norms[c] - 2.0f * acc;
-    };
+    const float twoE = coarse_margin2(qn2, d, cmax);
+    auto exact = [&](int c) { return exact_coarse(qs, cents, norms, c, d); };
 
     const bool use_tiles = tile_min && nlist > SP_CAP && ntiles >= nprobe && ntiles <= SP_CAP;
     const float* src = use_tiles ? tile_min + (int64_t)q * ntiles : row;
@@ -162,15 +192,35 @@ select_probes_margin_kernel(float* __restrict__ s, const float* __restrict__ q_r
     if (nlist > SP_CAP) {
         const float T = key_dist(buf[nprobe - 1]);
         const float thr = __fadd_ru(T, twoE);
+        // Only tiles whose minimum is <= thr can hold a list with s~ <= thr.
+        int ntc = TL_CAP + 1;
+        if (use_tiles) {
+            for (int i = tid; i < n0; i += SP_THREADS)
+                if (key_dist(buf[i]) <= thr && (i + 1 == n0 || !(key_dist(buf[i + 1]) <= thr)))
+                    m_sh = (unsigned)(i + 1);
+            __syncthreads();
+            ntc = (int)m_sh;
+            if (ntc <= TL_CAP)
+                for (int i = tid; i < ntc; i += SP_THREADS) tl[i] = key_id(buf[i]);
+        }
         __syncthreads();
-        for (int c = tid; c < nlist; c += SP_THREADS) {
+        auto take = [&](int c) {
             const float v = row[c];
             if (v <= thr) {
                 const unsigned int pos = atomicAdd(&cnt, 1u);
                 if (pos < SP_CAP) buf[pos] = ((uint64_t)float_order(v) << 32) | (uint32_t)c;
             }
+        };
+        if (ntc <= TL_CAP) {
+            for (int e = tid; e < ntc * COARSE_TILE_LISTS; e += SP_THREADS) {
+                const int c = tl[e / COARSE_TILE_LISTS] * COARSE_TILE_LISTS + e % COARSE_TILE_LISTS;
+                if (c < nlist) take(c);
+            }
+        } else {
+            for (int c = tid; c < nlist; c += SP_THREADS) take(c);
         }
         __syncthreads();
+        if (tid == 0) m_sh = 0;
         n = (int)cnt;
         if (n > SP_CAP) {                      // window too wide: rescore the row exactly
             for (int c = tid; c < nlist; c += SP_THREADS) row[c] = exact(c);
@@ -203,6 +253,128 @@ select_probes_margin_kernel(float* __restrict__ s, const float* __restrict__ q_r
         const uint64_t e = buf[p];
         out[p] = (e == KEY_EMPTY) ? 0 : (int32_t)(e & 0xffffffffu);
     }
+}
+
+// One warp per query for the common case of select_probes_margin_kernel
+// (group minima present, at most SW_CAP groups and SW_CAP collected lists):
+// the same steps with warp-synchronous sorts in shared memory and ballot-based
+// appends. A query whose window holds more than SW_CAP lists is flagged
+// (probes[q][0] = -1) and finished by the block kernel.
+constexpr int SW_WARPS = 8;
+constexpr int SW_CAP = 512;
+
+__global__ void __launch_bounds__(SW_WARPS * 32)
+select_probes_margin_warp_kernel(const float* __restrict__ s, const float* __restrict__ q_rot,
+                                 const float* __restrict__ cents, const float* __restrict__ norms,
+                                 const float* __restrict__ tile_min, int ngr, int nq, int nlist,
+                                 int d, int nprobe, float cmax, int32_t* __restrict__ probes) {
+    extern __shared__ uint64_t sw_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * SW_WARPS + warp;
+    if (q >= nq) return;                                   // warp-uniform; no block barriers below
+    uint64_t* gb = sw_smem + (size_t)warp * 2 * SW_CAP;    // group minima, sorted
+    uint64_t* cb = gb + SW_CAP;                            // collected lists
+    const float* qr = q_rot + (int64_t)q * d;
+    const float* row = s + (int64_t)q * nlist;
+    int32_t* out = probes + (int64_t)q * nprobe;
+    const unsigned lt = (1u << lane) - 1u;
+    float ss = 0.0f;
+    for (int j = lane; j < d; j += 32) {
+        const float v = qr[j];
+        ss += v * v;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float twoE = coarse_margin2(ss, d, cmax);
+
+    int P = 32;
+    while (P < ngr) P <<= 1;
+    const float* tm = tile_min + (int64_t)q * ngr;
+    for (int i0 = 0; i0 < P; i0 += 128) {                 // four loads in flight per lane
+        float x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 32 * u + lane;
+            x[u] = i < ngr ? tm[i] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = i0 + 32 * u + lane;
+            if (i < P) gb[i] = i < ngr ? (((uint64_t)float_order(x[u]) << 32) | (uint32_t)i) : KEY_EMPTY;
+        }
+    }
+    __syncwarp();
+    warp_bitonic_sort(gb, P, lane);
+    const float thr = __fadd_ru(key_dist(gb[nprobe - 1]), twoE);
+    int ntc = 0;                                           // sorted: groups with min <= thr lead
+    for (int base = 0; base < ngr; base += 32) {
+        const int i = base + lane;
+        const unsigned b = __ballot_sync(0xffffffffu, i < ngr && key_dist(gb[i]) <= thr);
+        ntc += __popc(b);
+        if (b != 0xffffffffu) break;
+    }
+    // groups 8 at a time, lane l holding lists 4l..4l+3 of each (loads in flight together)
+    static_assert(COARSE_TILE_LISTS == 128, "one 16-byte load per lane per group");
+    const bool vec = (nlist & 3) == 0;
+    const float inf = __int_as_float(0x7f800000);
+    int cnt = 0;
+    for (int t0 = 0; t0 < ntc; t0 += 8) {
+        float4 v[8];
+        int cc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            cc[u] = t0 + u < ntc ? key_id(gb[t0 + u]) * COARSE_TILE_LISTS + 4 * lane : nlist;
+            const int c = cc[u];
+            if (vec && c + 3 < nlist) {
+                v[u] = __ldcs(reinterpret_cast<const float4*>(row + c));
+            } else {
+                v[u].x = c < nlist ? row[c] : inf;
+                v[u].y = c + 1 < nlist ? row[c + 1] : inf;
+                v[u].z = c + 2 < nlist ? row[c + 2] : inf;
+                v[u].w = c + 3 < nlist ? row[c + 3] : inf;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float x = e == 0 ? v[u].x : e == 1 ? v[u].y : e == 2 ? v[u].z : v[u].w;
+                const bool in = cc[u] + e < nlist && x <= thr;
+                const unsigned b = __ballot_sync(0xffffffffu, in);
+                const int pos = cnt + __popc(b & lt);
+                if (in && pos < SW_CAP)
+                    cb[pos] = ((uint64_t)float_order(x) << 32) | (uint32_t)(cc[u] + e);
+                cnt += __popc(b);
+            }
+        }
+    }
+    if (cnt > SW_CAP) {
+        if (lane == 0) out[0] = -1;                        // left to the block kernel
+        return;
+    }
+    P = 32;
+    while (P < cnt) P <<= 1;
+    for (int i = cnt + lane; i < P; i += 32) cb[i] = KEY_EMPTY;
+    __syncwarp();
+    warp_bitonic_sort(cb, P, lane);
+    const float thr2 = __fadd_ru(key_dist(cb[nprobe - 1]), twoE);
+    int m = 0;
+    for (int base = 0; base < cnt; base += 32) {
+        const int i = base + lane;
+        const unsigned b = __ballot_sync(0xffffffffu, i < cnt && key_dist(cb[i]) <= thr2);
+        m += __popc(b);
+        if (b != 0xffffffffu) break;
+    }
+    for (int i = lane; i < m; i += 32) {
+        const int c = key_id(cb[i]);
+        cb[i] = ((uint64_t)float_order(exact_coarse(qr, cents, norms, c, d)) << 32) | (uint32_t)c;
+    }
+    int P3 = 32;
+    while (P3 < m) P3 <<= 1;
+    for (int i = m + lane; i < P3; i += 32) cb[i] = KEY_EMPTY;
+    __syncwarp();
+    warp_bitonic_sort(cb, P3, lane);
+    for (int p = lane; p < nprobe; p += 32) out[p] = key_id(cb[p]);
 }
 
 // 4-pass 8-bit radix select of the nprobe-th key, then the winners (ties at
@@ -397,9 +569,26 @@ void select_probes_margin(float* s, const float* q_rot, const float* cents, cons
                           float cmax, int32_t* probes, cudaStream_t st) {
     if (nq <= 0) return;
     if (nprobe > SP_CAP || nprobe > nlist) fail(JHQ_EINVAL, "select_probes_margin: bad nprobe");
-    if (d > SPM_DMAX || d % 4) fail(JHQ_EINVAL, "select_probes_margin: unsupported d");
-    select_probes_margin_kernel<<<nq, SP_THREADS, 0, st>>>(s, q_rot, cents, norms, tile_min,
-                                                           ntiles, nlist, d, nprobe, cmax, probes);
+    if (d > SPM_DMAX) fail(JHQ_EINVAL, "select_probes_margin: unsupported d");
+    if (tile_min && ntiles >= nprobe && ntiles <= SW_CAP && nprobe <= SW_CAP && nlist > SP_CAP) {
+        const size_t smem = (size_t)SW_WARPS * 2 * SW_CAP * sizeof(uint64_t);
+        static std::once_flag attr;
+        std::call_once(attr, [smem] {
+            JHQ_CUDA(cudaFuncSetAttribute(select_probes_margin_warp_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        });
+        select_probes_margin_warp_kernel<<<(nq + SW_WARPS - 1) / SW_WARPS, SW_WARPS * 32, smem, st>>>(
+            s, q_rot, cents, norms, tile_min, ntiles, nq, nlist, d, nprobe, cmax, probes);
+        JHQ_LAUNCH_CHECK();
+        count_launch();
+        select_probes_margin_kernel<<<nq, SP_THREADS, 0, st>>>(s, q_rot, cents, norms, tile_min,
+                                                               ntiles, nlist, d, nprobe, cmax,
+                                                               probes, 1);
+    } else {
+        select_probes_margin_kernel<<<nq, SP_THREADS, 0, st>>>(s, q_rot, cents, norms, tile_min,
+                                                               ntiles, nlist, d, nprobe, cmax,
+                                                               probes, 0);
+    }
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -45,24 +45,27 @@ void select_probes(const float* s, int nq, int nlist, int nprobe, int32_t* probe
 // Same lists from APPROXIMATE scores s~ (coarse_scores_tc): the lists within
 // a proven error margin of the nprobe-th s~ are rescored with the exact fp32
 // chain (cents [nlist][d] row-major, q_rot [nq][d]); cmax >= max |c|. The row
-// of s may be overwritten. d % 4 == 0, d <= 2048.
+// of s may be overwritten. d <= 2048.
 // tile_min (optional, [nq][ntiles]): minima of s~ over disjoint groups of lists.
 void select_probes_margin(float* s, const float* q_rot, const float* cents, const float* norms,
                           const float* tile_min, int ntiles, int nq, int nlist, int d, int nprobe,
                           float cmax, int32_t* probes, cudaStream_t st);
 
 // ---- tensor-core coarse scores (coarse_tc.cu) ------------------------------
-// s~[q][c] = norms[c] - 2 * (q3[q] . c3[c]) with tcgen05 kind::tf32 over K = 3d,
-// where q3 = [q_hi | q_hi | q_lo] (split3_rows order 0) and c3 = [c_hi | c_lo |
-// c_hi] (order 1), hi = x with the low 13 mantissa bits cleared, lo = x - hi.
+// s~[q][c] = norms[c] - 2 * (q3[q] . c3[c]) with tcgen05 kind::f16 (bf16
+// operands, fp32 accumulation) over K3 = coarse_tc_k3(d) >= 3d, where
+// q3 = [q_hi | q_hi | q_lo] (split3_rows, order 0) and c3 = [c_hi | c_lo | c_hi]
+// (order 1); hi = bf16(x), lo = bf16(x - hi), round to nearest even, zero pad.
 // Approximate: see select_probes_margin.
 bool coarse_tc_supported(int d, int nlist);
-void split3_rows(const float* x, int64_t n, int d, float* out, cudaStream_t s);   // order 0
-void split3_rows_host(const float* x, int64_t n, int d, int order, float* out);
-// Also tile_min[q][t] = min over lists [256t, 256t+256) of s~[q][.], t < coarse_tc_tiles.
+int coarse_tc_k3(int d);
+void split3_rows(const float* x, int64_t n, int d, uint16_t* out, cudaStream_t s);   // order 0
+void split3_rows_host(const float* x, int64_t n, int d, int order, uint16_t* out);
+// Also tile_min[q][t] = min over lists [128t, 128t+128) of s~[q][.], t < coarse_tc_tiles.
+constexpr int COARSE_TILE_LISTS = 128;
 int coarse_tc_tiles(int nlist);
-void coarse_scores_tc(const float* q3, int nq, const float* c3, const float* norms, int nlist,
-                      int d, float* scores, float* tile_min, cudaStream_t s);
+void coarse_scores_tc(const uint16_t* q3, int nq, const uint16_t* c3, const float* norms,
+                      int nlist, int d, float* scores, float* tile_min, cudaStream_t s);
 // Nonzero once a bounded wait inside the kernel gave up (cleared if `clear`).
 int coarse_tc_error(bool clear);
 
