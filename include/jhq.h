@@ -157,6 +157,27 @@ int jhq_merge_shards(const float* d_in_dists, const int32_t* d_in_ids,
                      int nshards, int64_t nq, int k,
                      float* d_out_dists, int32_t* d_out_ids, void* stream);
 
+/* ---- single-process sharded index ------------------------------------
+ * The JHQGpuIndex call shape (jhq_gpu_index.cuh:38-47) over nshards shards
+ * driven by one process: devices[s] is the GPU of shard s (NULL = 0..nshards-1;
+ * ordinals may repeat to put several shards on one GPU). Global id g lives on
+ * shard g % nshards. train() trains shard 0 and copies its artefacts to the
+ * others; add() may be called repeatedly; search() splits the coarse step by
+ * queries, scans every shard with the shared probe lists, and merges the
+ * shards' top-k on the first shard's GPU (order (distance, id), missing
+ * (+inf, -1)). Results equal searching each shard and merging with
+ * jhq_merge_shards. No reference counterpart (the reference is single-GPU). */
+typedef struct jhq_sharded jhq_sharded;
+int jhq_sharded_create(int d, const jhq_params* p, int nshards, const int* devices,
+                       jhq_sharded** out);
+int jhq_sharded_destroy(jhq_sharded* idx);
+int jhq_sharded_train(jhq_sharded* idx, const float* x, int64_t n_train);
+int jhq_sharded_add(jhq_sharded* idx, const float* x, int64_t n);
+int jhq_sharded_search(jhq_sharded* idx, const float* q, int64_t nq, int k, float* dists,
+                       int32_t* ids);
+int jhq_sharded_set_nprobe(jhq_sharded* idx, int nprobe);
+int64_t jhq_sharded_ntotal(const jhq_sharded* idx);
+
 /* ---- per-stage timing (the reference's jhq_v9_step_timing / v13 step
  * events, jhq_v13_step_timing/search.cu:456-491) -------------------------
  * With profiling on, search runs each batch as direct launches (no CUDA

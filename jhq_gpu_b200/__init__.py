@@ -36,7 +36,9 @@ EXPORTED = [
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_probe_device",
-    "jhq_search_device_probes",
+    "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
+    "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
+    "jhq_sharded_ntotal",
 ]
 STAGES = ["rotate", "coarse+probes", "plan", "scan", "refine"]
 
@@ -118,6 +120,14 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_kmeans_1d.argtypes = [f32p, i64, C.c_int, C.c_int, f32p, C.POINTER(C.c_int)]
     L.jhq_set_profiling.argtypes = [vp, C.c_int]
     L.jhq_stage_times.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.c_int]
+    L.jhq_sharded_create.argtypes = [C.c_int, C.POINTER(CParams), C.c_int, i32p, C.POINTER(vp)]
+    L.jhq_sharded_destroy.argtypes = [vp]
+    L.jhq_sharded_train.argtypes = [vp, f32p, i64]
+    L.jhq_sharded_add.argtypes = [vp, f32p, i64]
+    L.jhq_sharded_search.argtypes = [vp, f32p, i64, C.c_int, f32p, i32p]
+    L.jhq_sharded_set_nprobe.argtypes = [vp, C.c_int]
+    L.jhq_sharded_ntotal.argtypes = [vp]
+    L.jhq_sharded_ntotal.restype = C.c_int64
     L.jhq_kernel_launches.restype = C.c_int64
     L.jhq_last_error.restype = C.c_char_p
     L.jhq_version.restype = C.c_char_p
@@ -358,3 +368,57 @@ def _read_params(path: str) -> Params:
     return Params(M=int(hdr[1]), B=int(hdr[2]), Br=int(hdr[3]), alpha=alpha, nlist=int(hdr[4]),
                   nprobe=int(hdr[5]), ivf_iters=int(hdr[6]), batch_size=int(hdr[7]),
                   seed=int(hdr[8]), add_batch=int(hdr[9]))
+
+
+class JHQShardedIndex:
+    """Single-process sharded index (jhq_sharded_*): the JHQGpuIndex call shape
+    over shards on `devices` (one GPU each, or repeated ordinals for several
+    shards on one GPU). Global id g lives on shard g % nshards."""
+
+    def __init__(self, d: int, params: Optional[Params] = None, devices=(0,)):
+        self._L = load_library()
+        self.params = params or Params()
+        self.devices = [int(x) for x in devices]
+        devs = np.asarray(self.devices, np.int32)
+        h = C.c_void_p()
+        cp = self.params.to_c()
+        _check(self._L.jhq_sharded_create(d, C.byref(cp), len(self.devices),
+                                          _ptr(devs, C.c_int32), C.byref(h)))
+        self._h = h
+        self.d = d
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                self._L.jhq_sharded_destroy(h)
+            except Exception:
+                pass
+            self._h = C.c_void_p()
+
+    def close(self):
+        self.__del__()
+
+    @property
+    def ntotal(self) -> int:
+        return int(self._L.jhq_sharded_ntotal(self._h))
+
+    def train(self, x) -> None:
+        x = _f32(x)
+        _check(self._L.jhq_sharded_train(self._h, _ptr(x, C.c_float), x.shape[0]))
+
+    def add(self, x) -> None:
+        x = _f32(x)
+        _check(self._L.jhq_sharded_add(self._h, _ptr(x, C.c_float), x.shape[0]))
+
+    def set_nprobe(self, nprobe: int) -> None:
+        _check(self._L.jhq_sharded_set_nprobe(self._h, nprobe))
+
+    def search(self, q, k: int) -> Tuple[np.ndarray, np.ndarray]:
+        q = _f32(q)
+        nq = q.shape[0]
+        D = np.empty((nq, k), np.float32)
+        I = np.empty((nq, k), np.int32)
+        _check(self._L.jhq_sharded_search(self._h, _ptr(q, C.c_float), nq, k, _ptr(D, C.c_float),
+                                          _ptr(I, C.c_int32)))
+        return D, I

@@ -12,11 +12,16 @@
 
 #include "../../include/jhq.h"
 #include "index.h"
+#include "sharded.h"
 #include "kernels.cuh"
 #include "train_cpu.h"
 
 struct jhq_index {
     jhq::Index* impl;
+};
+
+struct jhq_sharded {
+    jhq::ShardedIndex* impl;
 };
 
 namespace {
@@ -215,6 +220,62 @@ int jhq_merge_shards(const float* d_in_dists, const int32_t* d_in_ids, int nshar
         jhq::merge_shard_lists(d_in_dists, d_in_ids, nshards, nq, k, d_out_dists, d_out_ids,
                                static_cast<cudaStream_t>(stream));
     });
+}
+
+int jhq_sharded_create(int d, const jhq_params* p, int nshards, const int* devices,
+                       jhq_sharded** out) {
+    return guarded([&] {
+        if (!out) jhq::fail(JHQ_EINVAL, "null output pointer");
+        *out = nullptr;
+        if (nshards <= 0 || nshards > 64) jhq::fail(JHQ_EINVAL, "nshards must be in 1..64");
+        jhq_params def;
+        if (!p) { jhq_params_default(&def); p = &def; }
+        std::vector<int> devs(nshards);
+        for (int s = 0; s < nshards; ++s) devs[s] = devices ? devices[s] : s;
+        auto* h = new jhq_sharded{nullptr};
+        try { h->impl = new jhq::ShardedIndex(d, to_params(p), devs); } catch (...) { delete h; throw; }
+        *out = h;
+    });
+}
+
+int jhq_sharded_destroy(jhq_sharded* idx) {
+    return guarded([&] {
+        if (!idx) return;
+        delete idx->impl;
+        delete idx;
+    });
+}
+
+namespace {
+jhq::ShardedIndex* need_sharded(const jhq_sharded* idx) {
+    if (!idx || !idx->impl) jhq::fail(JHQ_EINVAL, "null sharded index");
+    return idx->impl;
+}
+}  // namespace
+
+int jhq_sharded_train(jhq_sharded* idx, const float* x, int64_t n_train) {
+    return guarded([&] {
+        if (!x || n_train <= 0) jhq::fail(JHQ_EINVAL, "train: need at least one vector");
+        need_sharded(idx)->train(x, n_train);
+    });
+}
+
+int jhq_sharded_add(jhq_sharded* idx, const float* x, int64_t n) {
+    return guarded([&] { need_sharded(idx)->add(x, n); });
+}
+
+int jhq_sharded_search(jhq_sharded* idx, const float* q, int64_t nq, int k, float* dists,
+                       int32_t* ids) {
+    return guarded([&] { need_sharded(idx)->search(q, nq, k, dists, ids); });
+}
+
+int jhq_sharded_set_nprobe(jhq_sharded* idx, int nprobe) {
+    return guarded([&] { need_sharded(idx)->set_nprobe(nprobe); });
+}
+
+int64_t jhq_sharded_ntotal(const jhq_sharded* idx) {
+    if (!idx || !idx->impl) return -1;
+    return idx->impl->ntotal();
 }
 
 int jhq_set_profiling(jhq_index* idx, int on) {

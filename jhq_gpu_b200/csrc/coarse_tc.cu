@@ -422,8 +422,8 @@ void coarse_scores_tc(const uint16_t* q3, int nq, const uint16_t* c3, const floa
     const int mt = (nq + TC_BM - 1) / TC_BM, nlt = (nlist + TC_BN - 1) / TC_BN;   // MMA tiles
     const int64_t ntiles = (int64_t)mt * nlt;
     if (ntiles > INT32_MAX) fail(JHQ_EINVAL, "coarse_scores_tc: too many tiles");
-    static std::once_flag attr;
-    std::call_once(attr, [] {
+    static std::atomic<uint64_t> attr{0};
+    once_per_device(attr, [] {
         JHQ_CUDA(cudaFuncSetAttribute(coarse_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       TC_SMEM));
     });

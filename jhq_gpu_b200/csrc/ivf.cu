@@ -572,8 +572,8 @@ void select_probes_margin(float* s, const float* q_rot, const float* cents, cons
     if (d > SPM_DMAX) fail(JHQ_EINVAL, "select_probes_margin: unsupported d");
     if (tile_min && ntiles >= nprobe && ntiles <= SW_CAP && nprobe <= SW_CAP && nlist > SP_CAP) {
         const size_t smem = (size_t)SW_WARPS * 2 * SW_CAP * sizeof(uint64_t);
-        static std::once_flag attr;
-        std::call_once(attr, [smem] {
+        static std::atomic<uint64_t> attr{0};
+        once_per_device(attr, [smem] {
             JHQ_CUDA(cudaFuncSetAttribute(select_probes_margin_warp_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         });

@@ -9,10 +9,12 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
+#include <mutex>
 #include <utility>
 
 #include "../../include/jhq.h"
@@ -106,5 +108,20 @@ private:
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int next_pow2(int x) { int p = 1; while (p < x) p <<= 1; return p; }
+
+// Runs f once per CUDA device of the process, with that device current
+// (function attributes such as the opt-in shared memory size are per device).
+template <class F>
+void once_per_device(std::atomic<uint64_t>& done, F&& f) {
+    int dev = 0;
+    JHQ_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load() & bit) return;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.load() & bit) return;
+    f();
+    done.fetch_or(bit);
+}
 
 }  // namespace jhq

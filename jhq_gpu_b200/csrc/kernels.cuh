@@ -138,6 +138,9 @@ struct RefineArgs {
 void refine_topk(const RefineArgs& a, cudaStream_t st);
 void refine_configure();
 
+// ids[i] >= 0 -> ids[i] * mul + add (local -> global ids of a round-robin shard).
+void remap_ids(int32_t* ids, int64_t n, int mul, int add, cudaStream_t st);
+
 // k-way merge of per-shard top-k lists (jhq_merge_shards).
 void merge_shard_lists(const float* in_d, const int32_t* in_i, int nshards, int64_t nq,
                        int k, float* out_d, int32_t* out_i, cudaStream_t st);

@@ -164,6 +164,23 @@ void refine_configure() {
                                   227 * 1024));
 }
 
+namespace {
+__global__ void remap_ids_kernel(int32_t* __restrict__ ids, int64_t n, int mul, int add) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) {
+        const int32_t v = ids[i];
+        if (v >= 0) ids[i] = v * mul + add;
+    }
+}
+}  // namespace
+
+void remap_ids(int32_t* ids, int64_t n, int mul, int add, cudaStream_t st) {
+    if (n <= 0) return;
+    remap_ids_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, n, mul, add);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
 void merge_shard_lists(const float* in_d, const int32_t* in_i, int nshards, int64_t nq,
                        int k, float* out_d, int32_t* out_i, cudaStream_t st) {
     if (nq <= 0 || k <= 0) return;

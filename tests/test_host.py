@@ -77,6 +77,14 @@ def test_null_and_error_paths(jhq):
     assert L.jhq_search(None, None, 0, 10, None, None) == jhq.JHQ_EINVAL
     assert b"null index" in L.jhq_last_error()
     assert L.jhq_load(b"/nonexistent/file.jhq", -1, None) == jhq.JHQ_EINVAL
+    # sharded index: argument errors before any device is touched
+    import ctypes as C
+    h = C.c_void_p()
+    assert L.jhq_sharded_create(64, None, 0, None, C.byref(h)) == jhq.JHQ_EINVAL
+    assert L.jhq_sharded_create(64, None, 65, None, C.byref(h)) == jhq.JHQ_EINVAL
+    assert L.jhq_sharded_destroy(None) == 0
+    assert L.jhq_sharded_search(None, None, 0, 10, None, None) == jhq.JHQ_EINVAL
+    assert L.jhq_sharded_ntotal(None) == -1
 
 
 @pytest.mark.parametrize("d,M,nlist", [(128, 32, 1), (1024, 128, 1), (1024, 128, 1024),

@@ -129,3 +129,81 @@ def test_device_merge_two_shards(jhq, oracle):
     eD, eI = merge_topk_numpy(np.stack(Ds), np.stack(Is), k)
     assert np.array_equal(I.cpu().numpy(), eI)
     assert np.array_equal(D.cpu().numpy(), eD)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nlist,nprobe", [(1, 1), (64, 8)])
+def test_single_process_sharded_index_equals_merged_shards(nlist, nprobe):
+    """jhq_sharded_*: round-robin placement over 3 shards (all on GPU 0 here),
+    two add() calls, query-split coarse step, device merge == searching one
+    index per shard (same artefacts, rows g % 3 == s) and merging on the host."""
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200.sharded import merge_topk_numpy
+    rng = np.random.default_rng(51)
+    d, M, S = 64, 16, 3
+    x = rng.standard_normal((9001, d)).astype(np.float32)
+    q = rng.standard_normal((300, d)).astype(np.float32)
+    p = J.Params(M=M, nlist=nlist, nprobe=nprobe, batch_size=128)
+    sh = J.JHQShardedIndex(d, p, devices=[0] * S)
+    sh.train(x[:4000])
+    sh.add(x[:5000])
+    sh.add(x[5000:])
+    assert sh.ntotal == 9001
+    D, I = sh.search(q, 10)
+    ref = J.JHQGpuIndex(d, p)
+    ref.train(x[:4000])
+    t = ref.get_trained()
+    Ds, Is = [], []
+    for s in range(S):
+        idx = J.JHQGpuIndex(d, p)
+        idx.set_trained(t["Pi"], t["c1d"], t["res_c1d"], t["cents"], t["sigma"])
+        idx.add(x[s::S])
+        ds, is_ = idx.search(q, 10)
+        Ds.append(ds)
+        Is.append(np.where(is_ >= 0, is_ * S + s, -1).astype(np.int32))
+    D2, I2 = merge_topk_numpy(np.stack(Ds), np.stack(Is), 10)
+    assert np.array_equal(I, I2), np.argwhere(I != I2)[:5]
+    assert np.array_equal(D, D2)
+    # fewer vectors than shards: empty shards take no part
+    sh2 = J.JHQShardedIndex(d, p, devices=[0] * S)
+    sh2.train(x[:4000])
+    sh2.add(x[:2])
+    D3, I3 = sh2.search(q[:5], 4)
+    assert set(I3.ravel()) <= {-1, 0, 1} and (I3[:, 2:] == -1).all()
+    if nlist == 1:                         # flat: both vectors are always found
+        assert (np.sort(I3[:, :2], axis=1) == [0, 1]).all()
+
+
+@pytest.mark.gpu
+def test_single_process_sharded_index_over_gpus():
+    """jhq_sharded_* over every visible GPU (peer copies between devices):
+    equals one index per shard merged on the host."""
+    import torch
+    import jhq_gpu_b200 as J
+    from jhq_gpu_b200.sharded import merge_topk_numpy
+    ng = torch.cuda.device_count()
+    if ng < 2:
+        pytest.skip("needs 2 or more GPUs")
+    S = min(ng, 8)
+    rng = np.random.default_rng(61)
+    d = 64
+    x = rng.standard_normal((12000, d)).astype(np.float32)
+    q = rng.standard_normal((500, d)).astype(np.float32)
+    p = J.Params(M=16, nlist=32, nprobe=6, batch_size=128)
+    sh = J.JHQShardedIndex(d, p, devices=list(range(S)))
+    sh.train(x[:5000])
+    sh.add(x)
+    D, I = sh.search(q, 10)
+    ref = J.JHQGpuIndex(d, p)
+    ref.train(x[:5000])
+    t = ref.get_trained()
+    Ds, Is = [], []
+    for s in range(S):
+        idx = J.JHQGpuIndex(d, p)
+        idx.set_trained(t["Pi"], t["c1d"], t["res_c1d"], t["cents"], t["sigma"])
+        idx.add(x[s::S])
+        ds, is_ = idx.search(q, 10)
+        Ds.append(ds)
+        Is.append(np.where(is_ >= 0, is_ * S + s, -1).astype(np.int32))
+    D2, I2 = merge_topk_numpy(np.stack(Ds), np.stack(Is), 10)
+    assert np.array_equal(I, I2) and np.array_equal(D, D2)
