@@ -71,7 +71,7 @@ Index::~Index() {
         if (e) cudaEventDestroy(e);
     if (stream_) cudaStreamDestroy(stream_);
     // DevBuf / PinnedBuf members free themselves (device still current).
-    dPi_.release(); dc1d_.release(); dres_.release(); dcentsT_.release(); dcents_.release(); dcents3_.release(); dassign_scratch_.release(); dnorms_.release();
+    dPi_.release(); dc1d_.release(); dres_.release(); dcentsT_.release(); dcents_.release(); dpilot_centsT_.release(); dpilot_cents_.release(); dpilot_norms_.release(); dpilot_off_.release(); dpilot_ids_.release(); dcents3_.release(); dassign_scratch_.release(); dnorms_.release();
     dpcodes_.release(); drcodes_.release(); dpages_.release(); dcorr_.release();
     dassign_.release(); dslot_ids_.release(); dlist_page_off_.release();
     ws_.q.release(); ws_.q_rot.release(); ws_.scores.release(); ws_.out_d.release();
@@ -163,6 +163,71 @@ void Index::upload_trained() {
     JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
+// Lloyd k-means of the rotated rows y [n][d] into nl centroids (host copy in
+// `cents`, row-major): init rows floor(c * n / nl), `iters` rounds of
+// assign (on the device, through `assign`, which returns the device
+// assignment) + mean update in double, an empty cluster reseeded from the
+// row LCG(c, iter) (jhq_gpu_index.cu:228-299).
+void Index::lloyd(const std::vector<float>& y, int64_t n, int nl, int iters,
+                  std::vector<float>& cents,
+                  const std::function<const int32_t*(const std::vector<float>&)>& assign) {
+    cents.assign((size_t)nl * d_, 0.0f);
+    for (int c = 0; c < nl; ++c) {
+        const int64_t src = (int64_t)c * n / nl;
+        std::memcpy(&cents[(size_t)c * d_], &y[(size_t)src * d_], sizeof(float) * d_);
+    }
+    std::vector<int32_t> as((size_t)n);
+    std::vector<double> sums((size_t)nl * d_);
+    std::vector<int> counts(nl);
+    for (int iter = 0; iter < iters; ++iter) {
+        const int32_t* da = assign(cents);
+        d2h(as.data(), da, as.size(), stream_);
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
+        std::fill(sums.begin(), sums.end(), 0.0);
+        std::fill(counts.begin(), counts.end(), 0);
+        for (int64_t i = 0; i < n; ++i) {
+            const int c = as[i];
+            counts[c]++;
+            double* sc = &sums[(size_t)c * d_];
+            const float* yi = &y[(size_t)i * d_];
+            for (int j = 0; j < d_; ++j) sc[j] += yi[j];
+        }
+        for (int c = 0; c < nl; ++c) {
+            float* cc = &cents[(size_t)c * d_];
+            if (counts[c] == 0) {
+                const int64_t src = ((int64_t)c * 1103515245 + (int64_t)(iter * 12345)) % n;
+                std::memcpy(cc, &y[(size_t)src * d_], sizeof(float) * d_);
+                continue;
+            }
+            const double inv = 1.0 / (double)counts[c];
+            const double* sc = &sums[(size_t)c * d_];
+            for (int j = 0; j < d_; ++j) cc[j] = (float)(sc[j] * inv);
+        }
+    }
+}
+
+// Pilot centroids to the device: transposed [d][P] (assignment GEMM),
+// row-major [P][d] (nearest pilot at search) and squared norms.
+void Index::upload_pilot(const std::vector<float>& c, int P) {
+    std::vector<float> cT((size_t)d_ * P), norms(P);
+    for (int k = 0; k < P; ++k) {
+        double s2 = 0.0;
+        for (int j = 0; j < d_; ++j) {
+            const float v = c[(size_t)k * d_ + j];
+            cT[(size_t)j * P + k] = v;
+            s2 += (double)v * v;
+        }
+        norms[k] = (float)s2;
+    }
+    dpilot_centsT_.resize(cT.size());
+    dpilot_cents_.resize(c.size());
+    h2d(dpilot_cents_.get(), c.data(), c.size(), stream_);
+    dpilot_norms_.resize(P);
+    h2d(dpilot_centsT_.get(), cT.data(), cT.size(), stream_);
+    h2d(dpilot_norms_.get(), norms.data(), norms.size(), stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+}
+
 // ---- train: JHQGpuIndex::train (jhq_gpu_index.cu:333-364) --------------------
 void Index::train(const float* h_x, int64_t n) {
     DeviceGuard g(dev_);
@@ -198,41 +263,30 @@ void Index::train(const float* h_x, int64_t n) {
 
     // IVF centroids: Lloyd k-means in the rotated space (jhq_gpu_index.cu:228-299)
     {
-        const int nl = p_.nlist;
-        for (int c = 0; c < nl; ++c) {
-            int64_t src = (int64_t)c * n / nl;
-            std::memcpy(&cents_[(size_t)c * d_], &y[(size_t)src * d_], sizeof(float) * d_);
-        }
         DevBuf<int32_t> dassign((size_t)n);
-        std::vector<int32_t> as((size_t)n);
-        std::vector<double> sums((size_t)nl * d_);
-        std::vector<int> counts(nl);
-        for (int iter = 0; iter < p_.ivf_iters; ++iter) {
+        lloyd(y, n, p_.nlist, p_.ivf_iters, cents_, [&](const std::vector<float>&) {
             upload_trained();
             assign_device(dy.get(), n, dassign.get(), stream_);
-            d2h(as.data(), dassign.get(), as.size(), stream_);
-            JHQ_CUDA(cudaStreamSynchronize(stream_));
-            std::fill(sums.begin(), sums.end(), 0.0);
-            std::fill(counts.begin(), counts.end(), 0);
-            for (int64_t i = 0; i < n; ++i) {
-                int c = as[i];
-                counts[c]++;
-                double* sc = &sums[(size_t)c * d_];
-                const float* yi = &y[(size_t)i * d_];
-                for (int j = 0; j < d_; ++j) sc[j] += yi[j];
-            }
-            for (int c = 0; c < nl; ++c) {
-                float* cc = &cents_[(size_t)c * d_];
-                if (counts[c] == 0) {
-                    int64_t src = ((int64_t)c * 1103515245 + (int64_t)(iter * 12345)) % n;
-                    std::memcpy(cc, &y[(size_t)src * d_], sizeof(float) * d_);
-                    continue;
-                }
-                const double inv = 1.0 / (double)counts[c];
-                const double* sc = &sums[(size_t)c * d_];
-                for (int j = 0; j < d_; ++j) cc[j] = (float)(sc[j] * inv);
-            }
-        }
+            return dassign.get();
+        });
+    }
+    // pilot clusters of a flat index (search-time bound, see pilot.cu)
+    pilot_cents_.clear();
+    pilotP_ = 0;
+    const char* pe = std::getenv("JHQ_PILOT");
+    if (p_.nlist == 1 && !(pe && std::string(pe) == "0") && n >= 64 * PILOT_MIN_MEMBERS) {
+        const char* pl = std::getenv("JHQ_PILOT_LISTS");
+        const int P = std::max(2, std::min<int>(pl ? std::atoi(pl) : PILOT_LISTS,
+                                                (int)(n / PILOT_MIN_MEMBERS)));
+        DevBuf<int32_t> dassign((size_t)n);
+        lloyd(y, n, P, 6, pilot_cents_, [&](const std::vector<float>& c) {
+            upload_pilot(c, P);
+            gemm_argmin(dy.get(), dpilot_centsT_.get(), dpilot_norms_.get(), n, d_, P,
+                        dassign.get(), stream_);
+            return dassign.get();
+        });
+        pilotP_ = P;
+        upload_pilot(pilot_cents_, P);
     }
     dy.release();
 
@@ -257,6 +311,8 @@ void Index::set_trained(const float* Pi, const float* c1d, const float* res_c1d,
     DeviceGuard g(dev_);
     if (ntotal_ > 0) fail(JHQ_ESTATE, "set_trained() on a non-empty index");
     if (!Pi || !c1d || !res_c1d || !cents) fail(JHQ_EINVAL, "set_trained: null artefact");
+    pilotP_ = 0;                       // pilot clusters come from train() (or a saved index)
+    pilot_cents_.clear();
     Pi_.assign(Pi, Pi + (size_t)d_ * d_);
     c1d_.assign(c1d, c1d + K1D_);
     res_c1d_.assign(res_c1d, res_c1d + Kr_);
@@ -308,12 +364,20 @@ void Index::add(const float* h_x, int64_t n) {
     grow_master(ntotal_ + n);
     const int64_t AB = std::min<int64_t>(p_.add_batch, n);
     DevBuf<float> dx((size_t)AB * d_), dy((size_t)AB * d_);
+    DevBuf<int32_t> dpa;
+    if (pilotP_ > 0) h_pilot_assign_.resize((size_t)(ntotal_ + n));
     for (int64_t r0 = 0; r0 < n; r0 += AB) {
         const int64_t nr = std::min(AB, n - r0);
         const int64_t at = ntotal_ + r0;
         h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
         rotate_device(dx.get(), nr, dy.get(), stream_);
         assign_device(dy.get(), nr, dassign_.get() + at, stream_);
+        if (pilotP_ > 0) {
+            dpa.ensure((size_t)AB);
+            gemm_argmin(dy.get(), dpilot_centsT_.get(), dpilot_norms_.get(), nr, d_, pilotP_,
+                        dpa.get(), stream_);
+            d2h(h_pilot_assign_.data() + at, dpa.get(), (size_t)nr, stream_);
+        }
         encode_rows(dy.get(), nr, d_, M_, B_, Br_, dc1d_.get(), dres_.get(),
                     dpcodes_.get() + at * M_, drcodes_.get() + at * bpv_pad_, bpv_pad_,
                     dcorr_.get() + at, stream_);
@@ -359,6 +423,17 @@ void Index::rebuild_layout() {
     h2d(dslot_ids_.get(), slots.data(), slots.size(), stream_);
     scatter_pages(dslot_ids_.get(), (int64_t)slots.size(), dpcodes_.get(), M_, Mp_, dpages_.get(),
                   stream_);
+    if (pilotP_ > 0) {                 // pilot members, grouped by cluster in id order
+        std::vector<int32_t> off(pilotP_ + 1, 0), ids((size_t)std::max<int64_t>(1, ntotal_));
+        for (int64_t i = 0; i < ntotal_; ++i) off[h_pilot_assign_[(size_t)i] + 1]++;
+        for (int c = 0; c < pilotP_; ++c) off[c + 1] += off[c];
+        std::vector<int32_t> pos(off.begin(), off.end() - 1);
+        for (int64_t i = 0; i < ntotal_; ++i) ids[(size_t)pos[h_pilot_assign_[(size_t)i]]++] = (int32_t)i;
+        dpilot_off_.resize(off.size());
+        dpilot_ids_.resize(ids.size());
+        h2d(dpilot_off_.get(), off.data(), off.size(), stream_);
+        h2d(dpilot_ids_.get(), ids.data(), ids.size(), stream_);
+    }
     JHQ_CUDA(cudaStreamSynchronize(stream_));
     layout_dirty_ = false;
     destroy_graph();          // captured pointers changed
@@ -451,6 +526,10 @@ void Index::prepare_workspace(int k) {
     ws_.qslot_off.ensure((size_t)Bq + 1);
     ws_.gthr.ensure((size_t)Bq);
     ws_.cand.ensure((size_t)sh.max_slots * sh.ck);
+    if (pilotP_ > 0) {
+        ws_.pkeys.ensure((size_t)Bq * PILOT_SPLIT * sh.ck);
+        ws_.pcluster.ensure((size_t)Bq);
+    }
     ws_.out_d.ensure((size_t)Bq * k);
     ws_.out_i.ensure((size_t)Bq * k);
     ws_.nvalid.ensure(1);
@@ -541,6 +620,17 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     sa.nprobe = p_.nprobe; sa.ck = sh.ck; sa.ck_pad = sh.ck_pad; sa.grid = sh.grid;
     sa.chunk_pages = sh.chunk_pages; sa.mode = sh.mode; sa.qmajor = sh.qmajor;
     sa.probes = probes;
+    if (pilotP_ > 0 && p_.nlist == 1 && sh.mode == 1 && !sh.qmajor && ntotal_ > 0 && b.pkeys) {
+        PilotArgs pa;
+        pa.q_rot = b.q_rot; pa.c1d = dc1d_.get(); pa.pcents = dpilot_cents_.get();
+        pa.pnorms = dpilot_norms_.get(); pa.pilot_off = dpilot_off_.get();
+        pa.pilot_ids = dpilot_ids_.get(); pa.pcodes = dpcodes_.get(); pa.gthr = b.plan.gthr;
+        pa.pkeys = b.pkeys; pa.pcluster = b.pcluster;
+        pa.d_nvalid = d_nvalid; pa.nq = nq; pa.d = d_; pa.M = M_; pa.B = B_; pa.P = pilotP_;
+        pa.ck = sh.ck;
+        pilot_bound(pa, s);
+        sa.prune = 1;
+    }
     mark(3);
     scan_topck(sa, s);
     mark(4);
@@ -565,6 +655,7 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
+    b.pkeys = ws_.pkeys.get(); b.pcluster = ws_.pcluster.get();
     enqueue_pipeline(ws_.q.get(), ws_.batch_cap, ws_.nvalid.get(), sh, b, ws_.out_d.get(),
                      ws_.out_i.get(), s, ev);
 }
@@ -709,6 +800,7 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
+    b.pkeys = ws_.pkeys.get(); b.pcluster = ws_.pcluster.get();
     const int Bq = ws_.batch_cap;
     for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
         const int nv = (int)std::min<int64_t>(Bq, nq - q0);
@@ -801,7 +893,7 @@ void Index::save(const std::string& path) const {
     put(MAGIC, 8);
     put(&FORMAT_VERSION, 4);
     int32_t hdr[12] = {d_, p_.M, p_.B, p_.Br, p_.nlist, p_.nprobe, p_.ivf_iters,
-                       p_.batch_size, p_.seed, p_.add_batch, 0, 0};
+                       p_.batch_size, p_.seed, p_.add_batch, pilotP_, 0};
     put(hdr, sizeof hdr);
     put(&p_.alpha, 4);
     put(&sigma_, 4);
@@ -810,6 +902,7 @@ void Index::save(const std::string& path) const {
     put(c1d_.data(), c1d_.size() * 4);
     put(res_c1d_.data(), res_c1d_.size() * 4);
     put(cents_.data(), cents_.size() * 4);
+    if (pilotP_ > 0) put(pilot_cents_.data(), pilot_cents_.size() * 4);
     if (ntotal_ > 0) {
         std::vector<uint8_t> pc((size_t)ntotal_ * M_), rc((size_t)ntotal_ * bpv_);
         std::vector<float> co((size_t)ntotal_);
@@ -819,6 +912,7 @@ void Index::save(const std::string& path) const {
         put(rc.data(), rc.size());
         put(co.data(), co.size() * 4);
         put(as.data(), as.size() * 4);
+        if (pilotP_ > 0) put(h_pilot_assign_.data(), (size_t)ntotal_ * 4);
     }
     if (!f) fail(JHQ_EIO, "save: write failed for " + path);
 }
@@ -856,6 +950,16 @@ Index* Index::load(const std::string& path, int device) {
         get(res.data(), res.size() * 4);
         get(cents.data(), cents.size() * 4);
         idx->set_trained(Pi.data(), c1d.data(), res.data(), cents.data(), sigma);
+        const int P = hdr[10];                       // pilot clusters (0 = none)
+        if (P < 0 || P > (1 << 20)) fail(JHQ_EIO, "load: bad pilot cluster count");
+        if (P > 0) {
+            std::vector<float> pc((size_t)P * d);
+            get(pc.data(), pc.size() * 4);
+            DeviceGuard g(idx->dev_);
+            idx->pilot_cents_ = pc;
+            idx->upload_pilot(pc, P);
+            idx->pilotP_ = P;
+        }
         if (n > 0) {
             DeviceGuard g(idx->dev_);
             std::vector<uint8_t> pc((size_t)n * idx->M_), rc((size_t)n * idx->bpv_);
@@ -867,6 +971,12 @@ Index* Index::load(const std::string& path, int device) {
             get(as.data(), as.size() * 4);
             for (int32_t a : as)
                 if (a < 0 || a >= p.nlist) fail(JHQ_EIO, "load: bad list id");
+            if (P > 0) {
+                idx->h_pilot_assign_.resize((size_t)n);
+                get(idx->h_pilot_assign_.data(), (size_t)n * 4);
+                for (int32_t a : idx->h_pilot_assign_)
+                    if (a < 0 || a >= P) fail(JHQ_EIO, "load: bad pilot cluster id");
+            }
             idx->grow_master(n);
             JHQ_CUDA(cudaMemcpy(idx->dpcodes_.get(), pc.data(), pc.size(), cudaMemcpyHostToDevice));
             JHQ_CUDA(cudaMemcpy2D(idx->drcodes_.get(), idx->bpv_pad_, rc.data(), idx->bpv_, idx->bpv_,

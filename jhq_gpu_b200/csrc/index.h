@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -74,6 +75,7 @@ public:
     void stage_times(double* ms, int64_t* batches, int n) const;
 
     int K1D() const { return K1D_; }
+    int pilot_lists() const { return pilotP_; }
     int Kr() const { return Kr_; }
     int bpv() const { return bpv_; }
 
@@ -90,7 +92,8 @@ private:
         DevBuf<int32_t> probes, out_i, cnt, bucket_off, unit_off, fill, cpo;
         DevBuf<int2> bucket;
         DevBuf<int64_t> qslot_off;
-        DevBuf<uint64_t> cand, gthr;
+        DevBuf<uint64_t> cand, gthr, pkeys;
+        DevBuf<int32_t> pcluster;
         DevBuf<int> nvalid;
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
@@ -99,6 +102,9 @@ private:
     };
 
     void upload_trained();
+    void lloyd(const std::vector<float>& y, int64_t n, int nl, int iters, std::vector<float>& cents,
+               const std::function<const int32_t*(const std::vector<float>&)>& assign);
+    void upload_pilot(const std::vector<float>& c, int P);
     void rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const;
     // q_rot [nq][d] -> probes [nq][nprobe] through scores [nq][nlist] (scratch):
     // tensor-core scores + margin selection, or the fp32 SIMT GEMM + exact
@@ -124,6 +130,8 @@ private:
         int32_t* probes;
         PlanBufs plan;
         uint64_t* cand;
+        uint64_t* pkeys = nullptr;     // pilot scratch (flat index with pilot clusters)
+        int32_t* pcluster = nullptr;
     };
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
@@ -151,6 +159,14 @@ private:
 
     DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dcents_, dnorms_;
     DevBuf<uint16_t> dcents3_;         // bf16 split centroids [nlist][K3]
+    // Pilot clusters of a flat index: per query, the ADC keys of the nearest
+    // cluster's members seed its pruning bound (pilot.cu).
+    static constexpr int PILOT_LISTS = 64, PILOT_MIN_MEMBERS = 16;
+    int pilotP_ = 0;
+    std::vector<float> pilot_cents_;   // [P][d]
+    std::vector<int32_t> h_pilot_assign_;
+    DevBuf<float> dpilot_centsT_, dpilot_cents_, dpilot_norms_;
+    DevBuf<int32_t> dpilot_off_, dpilot_ids_;
     DevBuf<float> dassign_scratch_;    // tensor-core assignment: scores of a row block
     float cmax_ = 0.0f;                // >= max |centroid| (coarse margin)
     bool coarse_tc_ = false;

@@ -95,6 +95,29 @@ void plan_build(const int32_t* probes, int nq, int nprobe, int nlist,
                 const int32_t* list_page_off, const int* d_nvalid, int chunk_pages, int qg,
                 const PlanBufs& b, cudaStream_t st);
 
+// ---- pilot bound of a flat index (pilot.cu) --------------------------------
+// Per query q < *d_nvalid: gthr[q] = min(gthr[q], ck-th smallest ADC key of
+// the members of the nearest pilot cluster + 1), keys computed exactly as the
+// scan computes them (nibble tables; bits_per_dim in {1, 2, 4}).
+constexpr int PILOT_SPLIT = 8;             // CTAs per query scoring members
+constexpr int PILOT_CHUNK = 512;           // members per CTA (the rest are left out)
+struct PilotArgs {
+    const float* q_rot;            // [nq][d]
+    const float* c1d;              // [K1D]
+    const float* pcents;           // [P][d]
+    const float* pnorms;           // [P]
+    const int32_t* pilot_off;      // [P+1]
+    const int32_t* pilot_ids;      // members grouped by cluster
+    const uint8_t* pcodes;         // [N][M] primary codes, id order
+    int32_t* pcluster;             // scratch [nq]
+    uint64_t* pkeys;               // scratch [nq][PILOT_SPLIT][ck]
+    uint64_t* gthr;                // [nq]
+    const int* d_nvalid;
+    int nq, d, M, B, P, ck;
+};
+size_t pilot_smem_bytes(int M, int d);
+void pilot_bound(const PilotArgs& a, cudaStream_t st);
+
 // ---- LUT + ADC scan + exact top-ck (scan.cu) -------------------------------
 struct ScanArgs {
     const float* q_rot;            // [nq][d]
@@ -112,6 +135,7 @@ struct ScanArgs {
     const int32_t* probes;         // [nq][nprobe] (query-major order)
     int nq, nlist, d, M, Mp, B, nprobe, ck, ck_pad, grid, chunk_pages, mode;
     int qmajor;                    // 1: query-major warp items (chunk_pages = item pages)
+    int prune = 0;                 // 1: exit a page early once every slot is above its bound
 };
 // mode 0: byte LUT, one query per unit; 1/2/4: nibble tables, 1/2/4 queries.
 int scan_mode_for(int d, int M, int B, double queries_per_list);

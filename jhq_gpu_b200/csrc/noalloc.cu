@@ -91,6 +91,10 @@ void Index::search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_
     b.plan.qslot_off = reinterpret_cast<int64_t*>(take((size_t)(Bq + 1) * 8));
     b.plan.gthr = reinterpret_cast<uint64_t*>(take((size_t)Bq * 8));
     b.cand = reinterpret_cast<uint64_t*>(take((size_t)sh.max_slots * sh.ck * 8));
+    if (pilot_lists() > 0) {
+        b.pkeys = reinterpret_cast<uint64_t*>(take((size_t)Bq * PILOT_SPLIT * sh.ck * 8));
+        b.pcluster = reinterpret_cast<int32_t*>(take((size_t)Bq * 4));
+    }
     if (off > NOALLOC_SCRATCH_BYTES)
         fail(JHQ_EINVAL, "search_device_noalloc: batch needs " + std::to_string(off) +
                          " bytes of scratch, the fixed array holds " +

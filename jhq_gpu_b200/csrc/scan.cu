@@ -404,6 +404,7 @@ scan_kernel(ScanArgs a) {
 #pragma unroll
                 for (int j = 0; j < QG; ++j) dd[u][j] = 0.0f;
             }
+            bool pruned = false;
             // group g+1 of every page is in flight while group g is looked up
 #pragma unroll (G_T > 0 ? G_T : 1)
             for (int g = 0; g < G; ++g) {
@@ -418,7 +419,21 @@ scan_kernel(ScanArgs a) {
                 for (int u = 0; u < PPW; ++u) add_group<MODE>(dd[u], tg, cur[u]);
 #pragma unroll
                 for (int u = 0; u < PPW; ++u) cur[u] = nxt[u];
+                // Early exit (bounds seeded by pilot.cu): table entries are sums of
+                // squares (>= 0), so a partial distance never exceeds the final one;
+                // once every slot's partial is above its query's bound, none can enter.
+                if (a.prune && g + 1 < G) {
+                    bool dead = true;
+#pragma unroll
+                    for (int u = 0; u < PPW; ++u)
+#pragma unroll
+                        for (int j = 0; j < QG; ++j)
+                            dead = dead && (id[u] < 0 || unit.q[j] < 0 ||
+                                            float_order(dd[u][j]) > (uint32_t)(top[j].thr >> 32));
+                    if (__all_sync(0xffffffffu, dead)) { pruned = true; break; }
+                }
             }
+            if (pruned) continue;
 #pragma unroll
             for (int j = 0; j < QG; ++j) {
                 if (unit.q[j] < 0) continue;
