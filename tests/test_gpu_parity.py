@@ -341,3 +341,25 @@ def test_coarse_tensor_core_probes_equal_fp32(jhq, monkeypatch, case):
     monkeypatch.setenv("JHQ_COARSE", "simt")
     ref = _probe_lists(jhq, d, nlist, nprobe, cents, q)
     assert np.array_equal(tc, ref), np.argwhere(tc != ref)[:5]
+
+
+def test_flat_pilot_pruning_is_exact(jhq, monkeypatch, tmp_path):
+    """Flat index: the pilot-cluster bound plus the scan's early page exit give
+    the same ids and distances as the unpruned scan (clustered data, where most
+    pages exit early), also after save/load (the pilot clusters are stored)."""
+    from jhq_gpu_b200 import datasets
+    d, M = 256, 64
+    x = datasets.normalized_mixture(20000, d, 64, seed=3, sub=1)
+    q = datasets.normalized_mixture(300, d, 64, seed=3, sub=2)
+    p = jhq.Params(M=M, nlist=1, nprobe=1, batch_size=64)
+    monkeypatch.delenv("JHQ_PILOT", raising=False)
+    a = _build(jhq, d, p, x[:6000], x)
+    monkeypatch.setenv("JHQ_PILOT", "0")
+    b = _build(jhq, d, p, x[:6000], x)
+    Da, Ia = a.search(q, 10)
+    Db, Ib = b.search(q, 10)
+    _assert_same(Da, Ia, Db, Ib)
+    path = str(tmp_path / "flat.jhq")
+    a.save(path)
+    c = jhq.JHQGpuIndex.load(path)
+    _assert_same(*c.search(q, 10), Da, Ia)
