@@ -200,11 +200,11 @@ gemm_argmin_kernel(const float* __restrict__ A, const float* __restrict__ B,
 
 // Skinny path: CTA = SK_ROWS rows x SK_BN columns, 256 threads; thread
 // (column c, row group r) owns rows r*SK_TR .. r*SK_TR+SK_TR-1 of column c:
-// SK_TR independent chains. Chunks of SK_KC rows of B (and the matching
+// SK_TR (1 or 4) independent chains. Chunks of SK_KC rows of B (and the matching
 // SK_ROWS x SK_KC slice of A) are staged in shared memory by cp.async,
 // double-buffered. 16 rows per CTA keep the L2 re-reads of B (the d x d
 // rotation) at a quarter of a 4-row tiling.
-constexpr int SK_TR = 4, SK_RG = 4, SK_ROWS = SK_TR * SK_RG, SK_BN = 64, SK_KC = 32;
+constexpr int SK_RG = 4, SK_BN = 64, SK_KC = 64;
 constexpr int SK_THREADS = SK_BN * SK_RG;
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
@@ -220,10 +220,11 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n"); }
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n"); }
 
-template <int EPI>
+template <int EPI, int SK_TR>
 __global__ void __launch_bounds__(SK_THREADS)
 gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
                    int64_t R, int K, int N, const float* __restrict__ norms, int vec16) {
+    constexpr int SK_ROWS = SK_TR * SK_RG;
     __shared__ __align__(16) float Bs[2][SK_KC][SK_BN];
     __shared__ __align__(16) float As[2][SK_ROWS][SK_KC];
     const int tid = threadIdx.x, col = tid % SK_BN, rg = tid / SK_BN;
@@ -324,13 +325,23 @@ void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N
                GemmEpi epi, const float* norms, cudaStream_t s) {
     if (R <= 0 || N <= 0) return;
     if (R <= 1024) {
-        dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, SK_ROWS));
+        // 1 row per thread for small batches (4x the CTAs), 4 otherwise (a
+        // quarter of the L2 re-reads of B)
+        const int tr = R <= 256 ? 1 : 4;
+        dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, tr * SK_RG));
         const int vec16 = (N % 4 == 0) && (K % 4 == 0) && (((uintptr_t)A | (uintptr_t)B) % 16 == 0);
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");
-        if (epi == EPI_COARSE)
-            gemm_skinny_kernel<EPI_COARSE><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
-        else
-            gemm_skinny_kernel<EPI_STORE><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+        if (tr == 1) {
+            if (epi == EPI_COARSE)
+                gemm_skinny_kernel<EPI_COARSE, 1><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            else
+                gemm_skinny_kernel<EPI_STORE, 1><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+        } else {
+            if (epi == EPI_COARSE)
+                gemm_skinny_kernel<EPI_COARSE, 4><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            else
+                gemm_skinny_kernel<EPI_STORE, 4><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+        }
     } else {
         dim3 grid((unsigned)ceil_div(N, TBN), (unsigned)ceil_div(R, TBM));
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");
