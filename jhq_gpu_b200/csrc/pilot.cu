@@ -37,19 +37,47 @@ pilot_nearest_kernel(PilotArgs a) {
     float* qs = qsm;
     for (int j = tid; j < a.d; j += PL_THREADS) qs[j] = a.q_rot[(int64_t)q * a.d + j];
     __syncthreads();
+    // S threads per centroid (a power of two <= 32), each summing an
+    // interleaved slice of the dimensions; all centroids of a pass at once
+    int S = 32;
+    while (S > 1 && S * a.P > PL_THREADS) S >>= 1;
+    const int per_pass = PL_THREADS / S;
+    const int sl = tid % S;
     float best = __int_as_float(0x7f800000);
     int bc = 0;
-    for (int c = warp; c < a.P; c += PL_THREADS / 32) {
-        const float* pc = a.pcents + (int64_t)c * a.d;
+    for (int c0 = 0; c0 < a.P; c0 += per_pass) {
+        const int c = c0 + tid / S;
         float dot = 0.0f;
-#pragma unroll 4
-        for (int j = lane; j < a.d; j += 32) dot = __fmaf_rn(qs[j], __ldg(pc + j), dot);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        const float sc = a.pnorms[c] - 2.0f * dot;
-        if (sc < best) { best = sc; bc = c; }
+        if (c < a.P) {
+            const float* pc = a.pcents + (int64_t)c * a.d;
+            if ((a.d & 3) == 0) {
+                const float4* p4 = reinterpret_cast<const float4*>(pc);
+                const float4* q4 = reinterpret_cast<const float4*>(qs);
+#pragma unroll 8
+                for (int j = sl; j < a.d / 4; j += S) {
+                    const float4 v = __ldg(p4 + j), w = q4[j];
+                    dot += v.x * w.x + v.y * w.y + v.z * w.z + v.w * w.w;
+                }
+            } else {
+                for (int j = sl; j < a.d; j += S) dot += __ldg(pc + j) * qs[j];
+            }
+        }
+        for (int o = S >> 1; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (c < a.P && sl == 0) {
+            const float sc = a.pnorms[c] - 2.0f * dot;
+            if (sc < best) { best = sc; bc = c; }
+        }
     }
-    if (lane == 0) wk[warp] = ((uint64_t)float_order(best) << 32) | (uint32_t)bc;
+    // block argmin (ties: lowest centroid)
+    {
+        uint64_t key = ((uint64_t)float_order(best) << 32) | (uint32_t)bc;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const uint64_t other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other < key ? other : key;
+        }
+        if (lane == 0) wk[warp] = key;
+    }
     __syncthreads();
     if (tid == 0) {
         uint64_t m = wk[0];
