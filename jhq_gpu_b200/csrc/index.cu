@@ -528,7 +528,7 @@ void Index::prepare_workspace(int k) {
     ws_.cand.ensure((size_t)sh.max_slots * sh.ck);
     if (pilotP_ > 0) {
         ws_.pkeys.ensure((size_t)Bq * PILOT_SPLIT * sh.ck);
-        ws_.pcluster.ensure((size_t)Bq);
+        ws_.pscores.ensure((size_t)Bq * pilotP_);
     }
     ws_.out_d.ensure((size_t)Bq * k);
     ws_.out_i.ensure((size_t)Bq * k);
@@ -625,7 +625,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
         pa.q_rot = b.q_rot; pa.c1d = dc1d_.get(); pa.pcents = dpilot_cents_.get();
         pa.pnorms = dpilot_norms_.get(); pa.pilot_off = dpilot_off_.get();
         pa.pilot_ids = dpilot_ids_.get(); pa.pcodes = dpcodes_.get(); pa.gthr = b.plan.gthr;
-        pa.pkeys = b.pkeys; pa.pcluster = b.pcluster;
+        pa.pkeys = b.pkeys; pa.pscores = b.pscores;
         pa.d_nvalid = d_nvalid; pa.nq = nq; pa.d = d_; pa.M = M_; pa.B = B_; pa.P = pilotP_;
         pa.ck = sh.ck;
         pilot_bound(pa, s);
@@ -655,7 +655,7 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
-    b.pkeys = ws_.pkeys.get(); b.pcluster = ws_.pcluster.get();
+    b.pkeys = ws_.pkeys.get(); b.pscores = ws_.pscores.get();
     enqueue_pipeline(ws_.q.get(), ws_.batch_cap, ws_.nvalid.get(), sh, b, ws_.out_d.get(),
                      ws_.out_i.get(), s, ev);
 }
@@ -800,7 +800,7 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
-    b.pkeys = ws_.pkeys.get(); b.pcluster = ws_.pcluster.get();
+    b.pkeys = ws_.pkeys.get(); b.pscores = ws_.pscores.get();
     const int Bq = ws_.batch_cap;
     for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
         const int nv = (int)std::min<int64_t>(Bq, nq - q0);

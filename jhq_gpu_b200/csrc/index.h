@@ -93,7 +93,7 @@ private:
         DevBuf<int2> bucket;
         DevBuf<int64_t> qslot_off;
         DevBuf<uint64_t> cand, gthr, pkeys;
-        DevBuf<int32_t> pcluster;
+        DevBuf<float> pscores;
         DevBuf<int> nvalid;
         cudaGraph_t graph = nullptr;
         cudaGraphExec_t exec = nullptr;
@@ -131,7 +131,7 @@ private:
         PlanBufs plan;
         uint64_t* cand;
         uint64_t* pkeys = nullptr;     // pilot scratch (flat index with pilot clusters)
-        int32_t* pcluster = nullptr;
+        float* pscores = nullptr;
     };
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,

@@ -109,7 +109,7 @@ struct PilotArgs {
     const int32_t* pilot_off;      // [P+1]
     const int32_t* pilot_ids;      // members grouped by cluster
     const uint8_t* pcodes;         // [N][M] primary codes, id order
-    int32_t* pcluster;             // scratch [nq]
+    float* pscores;                // scratch [nq][P]
     uint64_t* pkeys;               // scratch [nq][PILOT_SPLIT][ck]
     uint64_t* gthr;                // [nq]
     const int* d_nvalid;

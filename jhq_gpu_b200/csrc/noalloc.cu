@@ -93,7 +93,7 @@ void Index::search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_
     b.cand = reinterpret_cast<uint64_t*>(take((size_t)sh.max_slots * sh.ck * 8));
     if (pilot_lists() > 0) {
         b.pkeys = reinterpret_cast<uint64_t*>(take((size_t)Bq * PILOT_SPLIT * sh.ck * 8));
-        b.pcluster = reinterpret_cast<int32_t*>(take((size_t)Bq * 4));
+        b.pscores = reinterpret_cast<float*>(take((size_t)Bq * pilot_lists() * 4));
     }
     if (off > NOALLOC_SCRATCH_BYTES)
         fail(JHQ_EINVAL, "search_device_noalloc: batch needs " + std::to_string(off) +

@@ -26,64 +26,40 @@ namespace {
 constexpr int PL_THREADS = 256;
 constexpr int PL_GMAX = 16;                  // 16-byte code groups per row held in registers
 
-// Stage 1, one block per query: the nearest pilot centroid (fp32 scores, any
-// order: the choice only affects how tight the bound is) -> pcluster[q].
+// Stage 1: CTA (q, g) scores pilot centroids [16g, 16g + 16) for query q
+// (fp32, any order: the choice of cluster only affects how tight the bound
+// is): 16 threads per centroid, each summing an interleaved slice of float4s.
+constexpr int PN_CENTS = 16;
 __global__ void __launch_bounds__(PL_THREADS)
 pilot_nearest_kernel(PilotArgs a) {
-    extern __shared__ float qsm[];
-    __shared__ uint64_t wk[PL_THREADS / 32];
-    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int S = PL_THREADS / PN_CENTS;
+    const int q = blockIdx.x, tid = threadIdx.x, sl = tid % S;
     if (a.d_nvalid && q >= *a.d_nvalid) return;
-    float* qs = qsm;
-    for (int j = tid; j < a.d; j += PL_THREADS) qs[j] = a.q_rot[(int64_t)q * a.d + j];
-    __syncthreads();
-    // S threads per centroid (a power of two <= 32), each summing an
-    // interleaved slice of the dimensions; all centroids of a pass at once
-    int S = 32;
-    while (S > 1 && S * a.P > PL_THREADS) S >>= 1;
-    const int per_pass = PL_THREADS / S;
-    const int sl = tid % S;
-    float best = __int_as_float(0x7f800000);
-    int bc = 0;
-    for (int c0 = 0; c0 < a.P; c0 += per_pass) {
-        const int c = c0 + tid / S;
-        float dot = 0.0f;
-        if (c < a.P) {
-            const float* pc = a.pcents + (int64_t)c * a.d;
-            if ((a.d & 3) == 0) {
-                const float4* p4 = reinterpret_cast<const float4*>(pc);
-                const float4* q4 = reinterpret_cast<const float4*>(qs);
-#pragma unroll 8
-                for (int j = sl; j < a.d / 4; j += S) {
-                    const float4 v = __ldg(p4 + j), w = q4[j];
-                    dot += v.x * w.x + v.y * w.y + v.z * w.z + v.w * w.w;
-                }
-            } else {
-                for (int j = sl; j < a.d; j += S) dot += __ldg(pc + j) * qs[j];
-            }
-        }
-        for (int o = S >> 1; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        if (c < a.P && sl == 0) {
-            const float sc = a.pnorms[c] - 2.0f * dot;
-            if (sc < best) { best = sc; bc = c; }
-        }
-    }
-    // block argmin (ties: lowest centroid)
-    {
-        uint64_t key = ((uint64_t)float_order(best) << 32) | (uint32_t)bc;
+    const int c = blockIdx.y * PN_CENTS + tid / S;
+    const float* qr = a.q_rot + (int64_t)q * a.d;
+    float dot = 0.0f;
+    if (c < a.P) {
+        const float* pc = a.pcents + (int64_t)c * a.d;
+        if ((a.d & 3) == 0) {
+            const float4* p4 = reinterpret_cast<const float4*>(pc);
+            const float4* q4 = reinterpret_cast<const float4*>(qr);
+            const int d4 = a.d / 4;
+            for (int j0 = sl; j0 < d4; j0 += 8 * S) {
+                float4 v[8], w[8];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const uint64_t other = __shfl_xor_sync(0xffffffffu, key, o);
-            key = other < key ? other : key;
+                for (int u = 0; u < 8; ++u)
+                    if (j0 + u * S < d4) { v[u] = __ldg(p4 + j0 + u * S); w[u] = __ldg(q4 + j0 + u * S); }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (j0 + u * S < d4) dot += v[u].x * w[u].x + v[u].y * w[u].y + v[u].z * w[u].z + v[u].w * w[u].w;
+            }
+        } else {
+            for (int j = sl; j < a.d; j += S) dot += __ldg(pc + j) * __ldg(qr + j);
         }
-        if (lane == 0) wk[warp] = key;
     }
-    __syncthreads();
-    if (tid == 0) {
-        uint64_t m = wk[0];
-        for (int w = 1; w < PL_THREADS / 32; ++w) m = wk[w] < m ? wk[w] : m;
-        a.pcluster[q] = (int32_t)(uint32_t)(m & 0xffffffffu);
-    }
+#pragma unroll
+    for (int o = S >> 1; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (c < a.P && sl == 0) a.pscores[(int64_t)q * a.P + c] = a.pnorms[c] - 2.0f * dot;
 }
 
 // Stage 2: CTA (q, part) scores its share (at most PILOT_CHUNK) of the
@@ -93,6 +69,7 @@ __global__ void __launch_bounds__(PL_THREADS)
 pilot_keys_kernel(PilotArgs a) {
     extern __shared__ float psm[];
     __shared__ uint64_t buf[PILOT_CHUNK];
+    __shared__ int cq_sh;
     const int q = blockIdx.x, part = blockIdx.y, tid = threadIdx.x;
     if (a.d_nvalid && q >= *a.d_nvalid) return;
     uint64_t* out = a.pkeys + ((int64_t)q * PILOT_SPLIT + part) * a.ck;
@@ -101,7 +78,29 @@ pilot_keys_kernel(PilotArgs a) {
     float* c1d = qs + a.d;
     for (int j = tid; j < a.d; j += PL_THREADS) qs[j] = a.q_rot[(int64_t)q * a.d + j];
     __syncthreads();
-    const int cq = a.pcluster[q];
+    // nearest pilot cluster from the stage-1 scores (ties: lowest centroid);
+    // every CTA of the query reads the same scores, so all pick the same one
+    {
+        uint64_t key = KEY_EMPTY;
+        for (int c = tid; c < a.P; c += PL_THREADS) {
+            const uint64_t k = ((uint64_t)float_order(a.pscores[(int64_t)q * a.P + c]) << 32) | (uint32_t)c;
+            key = k < key ? k : key;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const uint64_t other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other < key ? other : key;
+        }
+        if ((tid & 31) == 0) buf[tid >> 5] = key;
+        __syncthreads();
+        if (tid == 0) {
+            uint64_t m = buf[0];
+            for (int w = 1; w < PL_THREADS / 32; ++w) m = buf[w] < m ? buf[w] : m;
+            cq_sh = (int)(uint32_t)(m & 0xffffffffu);
+        }
+        __syncthreads();
+    }
+    const int cq = cq_sh;
     const int off0 = a.pilot_off[cq];
     const int cnt = min(a.pilot_off[cq + 1] - off0, PILOT_SPLIT * PILOT_CHUNK);
     const int chunk = (cnt + PILOT_SPLIT - 1) / PILOT_SPLIT;
@@ -212,7 +211,8 @@ void pilot_bound(const PilotArgs& a, cudaStream_t st) {
                                       160 * 1024));
     });
     if (smem > 160 * 1024 || smem3 > 160 * 1024) fail(JHQ_EINVAL, "pilot_bound: sizes too large");
-    pilot_nearest_kernel<<<(unsigned)a.nq, PL_THREADS, (size_t)a.d * sizeof(float), st>>>(a);
+    pilot_nearest_kernel<<<dim3((unsigned)a.nq, (unsigned)((a.P + PN_CENTS - 1) / PN_CENTS)),
+                           PL_THREADS, 0, st>>>(a);
     JHQ_LAUNCH_CHECK();
     count_launch();
     pilot_keys_kernel<<<dim3((unsigned)a.nq, PILOT_SPLIT), PL_THREADS, smem, st>>>(a);
