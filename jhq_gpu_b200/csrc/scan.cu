@@ -458,7 +458,6 @@ scan_kernel(ScanArgs a) {
 // table base is folded into the byte-permute that extracts each nibble offset
 // (the bases are multiples of 256 bytes), so a lookup needs no extra add.
 constexpr int QM_WARPS = 8;
-constexpr int QM_U = 1;                     // pages per warp step (measured: 1 beats 4)
 constexpr int QM_GMAX = 8;                  // code groups per page (Mp <= 128)
 constexpr int QM_THREADS = QM_WARPS * 32;
 
@@ -521,35 +520,43 @@ scan_qmajor_kernel(ScanArgs a) {
             cur_q = q;
         }
         top.reset(lane, merge_n, a.gthr[q]);
-        // QM_U pages per step: every page's ids and code groups are loaded
-        // before the first lookup, so QM_U page fetches are in flight per warp
-        int p = 0;
-        for (int lp0 = first; lp0 < last; lp0 += QM_U) {
-            int32_t id[QM_U];
-            uint4 code[QM_U][QM_GMAX];
-#pragma unroll
-            for (int u = 0; u < QM_U; ++u) {
-                const int lp = lp0 + u;
-                id[u] = -1;
-#pragma unroll
-                for (int g = 0; g < QM_GMAX; ++g) code[u][g] = make_uint4(0, 0, 0, 0);
-                if (lp < last) {
-                    while (lp >= po[p + 1]) ++p;
-                    const int64_t pg = a.list_page_off[pr[p]] + (lp - po[p]);
-                    id[u] = __ldg(a.slot_ids + pg * 32 + lane);
-                    const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
-#pragma unroll
-                    for (int g = 0; g < QM_GMAX; ++g)
-                        if (g < G) code[u][g] = __ldg(pp + g * 32);
+        // The item's page addresses, 32 at a time, one per lane (a binary search
+        // over the query's page prefix, then the list's first page): the
+        // dependent index loads are paid once per 32 pages, in parallel. The
+        // codes of page j+1 are in flight while page j is looked up.
+        constexpr int GM = G_T > 0 ? G_T : QM_GMAX;
+        for (int b0 = first; b0 < last; b0 += 32) {
+            const int npg = min(32, last - b0);
+            int64_t mypg = 0;
+            if (lane < npg) {
+                const int lp = b0 + lane;
+                int plo = 0, phi = a.nprobe;                  // last p with po[p] <= lp
+                while (phi - plo > 1) {
+                    const int mid = (plo + phi) >> 1;
+                    if (po[mid] <= lp) plo = mid; else phi = mid;
                 }
+                mypg = a.list_page_off[pr[plo]] + (lp - po[plo]);
             }
+            auto fetch = [&](int j, int32_t& id, uint4 (&code)[GM]) {
+                const int64_t pg = __shfl_sync(0xffffffffu, mypg, j);
+                id = __ldg(a.slot_ids + pg * 32 + lane);
+                const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
 #pragma unroll
-            for (int u = 0; u < QM_U; ++u) {
+                for (int g = 0; g < GM; ++g)
+                    code[g] = g < G ? __ldg(pp + g * 32) : make_uint4(0, 0, 0, 0);
+            };
+            int32_t id_c;
+            uint4 code_c[GM];
+            fetch(0, id_c, code_c);
+            for (int j = 0; j < npg; ++j) {
+                int32_t id_n = -1;
+                uint4 code_n[GM];
+                if (j + 1 < npg) fetch(j + 1, id_n, code_n);
                 float dist = 0.0f;
 #pragma unroll
-                for (int g = 0; g < QM_GMAX; ++g) {
+                for (int g = 0; g < GM; ++g) {
                     if (g >= G) break;
-                    const uint4 cur = code[u][g];
+                    const uint4 cur = code_c[g];
 #pragma unroll
                     for (int wi = 0; wi < 4; ++wi) {
                         const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
@@ -567,8 +574,11 @@ scan_qmajor_kernel(ScanArgs a) {
                         }
                     }
                 }
-                top.push(id[u] >= 0 ? make_key(dist, id[u]) : KEY_EMPTY, lane, a.ck, a.ck_pad,
+                top.push(id_c >= 0 ? make_key(dist, id_c) : KEY_EMPTY, lane, a.ck, a.ck_pad,
                          merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
+                id_c = id_n;
+#pragma unroll
+                for (int g = 0; g < GM; ++g) code_c[g] = code_n[g];
             }
         }
         top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
