@@ -486,10 +486,22 @@ scan_qmajor_kernel(ScanArgs a) {
     const int Ds = a.d / a.M, bpd = a.B / Ds, kmask = (1 << bpd) - 1, kpn = 4 / bpd;
     const int64_t total = a.qslot_off[a.nq];
     const int64_t nw = (int64_t)gridDim.x * QM_WARPS;
+    const int64_t wid = (int64_t)blockIdx.x * QM_WARPS + warp;
+    // A contiguous range of items per warp: consecutive items of one query form
+    // a run that shares the tables and one top-ck list (written to the run's
+    // first slot; the run's other slots get empty lists, merged away by refine).
+    const int64_t it0 = total * wid / nw, it1 = total * (wid + 1) / nw;
     int cur_q = -1;
+    int64_t run_slot = -1;
     WarpTop top;
     top.s = wl;
-    for (int64_t it = (int64_t)blockIdx.x * QM_WARPS + warp; it < total; it += nw) {
+    auto close_run = [&]() {
+        top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[cur_q]));
+        uint64_t* out = a.cand + run_slot * a.ck;
+        for (int i = lane; i < a.ck; i += 32) out[i] = top.s[i];
+        __syncwarp();
+    };
+    for (int64_t it = it0; it < it1; ++it) {
         int lo = 0, hi = a.nq;                                // last q with qslot_off[q] <= it
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -500,7 +512,9 @@ scan_qmajor_kernel(ScanArgs a) {
         const int32_t* pr = a.probes + (int64_t)q * a.nprobe;
         const int first = (int)(it - a.qslot_off[q]) * a.chunk_pages;
         const int last = min(first + a.chunk_pages, po[a.nprobe]);
-        if (q != cur_q) {                                     // this query's tables
+        if (q != cur_q) {                                     // a new run: this query's tables
+            if (cur_q >= 0) close_run();
+            if (lane == 0) SCAN_STAT(4, 1);
             __syncwarp();
             const float* qv = a.q_rot + (int64_t)q * a.d;
             for (int i = lane; i < a.Mp * 32; i += 32) {
@@ -518,8 +532,14 @@ scan_qmajor_kernel(ScanArgs a) {
             }
             __syncwarp();
             cur_q = q;
+            run_slot = it;
+            top.reset(lane, merge_n, a.gthr[q]);
+        } else {                                              // continuation: empty slot
+            uint64_t* out = a.cand + it * a.ck;
+            for (int i = lane; i < a.ck; i += 32) out[i] = KEY_EMPTY;
+            const uint64_t g = *reinterpret_cast<volatile uint64_t*>(&a.gthr[q]);
+            top.thr = g < top.thr ? g : top.thr;
         }
-        top.reset(lane, merge_n, a.gthr[q]);
         // The item's page addresses, 32 at a time, one per lane (a binary search
         // over the query's page prefix, then the list's first page): the
         // dependent index loads are paid once per 32 pages, in parallel. The
@@ -581,11 +601,8 @@ scan_qmajor_kernel(ScanArgs a) {
                 for (int g = 0; g < GM; ++g) code_c[g] = code_n[g];
             }
         }
-        top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
-        uint64_t* out = a.cand + it * a.ck;
-        for (int i = lane; i < a.ck; i += 32) out[i] = top.s[i];
-        __syncwarp();
     }
+    if (cur_q >= 0) close_run();
 }
 
 template <int G_T, int MODE>
