@@ -224,7 +224,7 @@ class JHQGpuIndex:
                 self._L.jhq_index_destroy(h)
             except Exception:
                 pass
-            self._h = C.c_void_p()
+            self._h = None
 
     def close(self):
         self.__del__()
@@ -394,7 +394,7 @@ class JHQShardedIndex:
                 self._L.jhq_sharded_destroy(h)
             except Exception:
                 pass
-            self._h = C.c_void_p()
+            self._h = None
 
     def close(self):
         self.__del__()
