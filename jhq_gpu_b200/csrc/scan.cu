@@ -390,17 +390,29 @@ scan_kernel(ScanArgs a) {
 
         // ---- score PPW pages at a time: warp w takes pb + PPW*(w + W*i)
         const int64_t pb = unit.pb, pe = unit.pe;
-        for (int64_t pg = pb + PPW * warp; pg < pe; pg += PPW * SCAN_WARPS) {
-            int32_t id[PPW];
-            float dd[PPW][QG];
-            const uint4* pp[PPW];
-            uint4 cur[PPW];
+        // the first group and slot ids of the warp's next pages are in flight
+        // while the current pages are looked up
+        int32_t id[PPW];
+        uint4 cur[PPW];
+        auto fetch_page = [&](int64_t p0, int32_t (&ids)[PPW], uint4 (&c0)[PPW]) {
 #pragma unroll
             for (int u = 0; u < PPW; ++u) {
-                const bool ok = pg + u < pe;
-                id[u] = ok ? __ldg(a.slot_ids + (pg + u) * 32 + lane) : -1;
+                const bool ok = p0 + u < pe;
+                ids[u] = ok ? __ldg(a.slot_ids + (p0 + u) * 32 + lane) : -1;
+                c0[u] = ok ? __ldg(reinterpret_cast<const uint4*>(a.pages) + (p0 + u) * G * 32 + lane)
+                           : make_uint4(0, 0, 0, 0);
+            }
+        };
+        fetch_page(pb + PPW * warp, id, cur);
+        for (int64_t pg = pb + PPW * warp; pg < pe; pg += PPW * SCAN_WARPS) {
+            int32_t idn[PPW];
+            uint4 curn[PPW];
+            fetch_page(pg + PPW * SCAN_WARPS, idn, curn);
+            float dd[PPW][QG];
+            const uint4* pp[PPW];
+#pragma unroll
+            for (int u = 0; u < PPW; ++u) {
                 pp[u] = reinterpret_cast<const uint4*>(a.pages) + (pg + u) * G * 32 + lane;
-                cur[u] = ok ? __ldg(pp[u]) : make_uint4(0, 0, 0, 0);
 #pragma unroll
                 for (int j = 0; j < QG; ++j) dd[u][j] = 0.0f;
             }
@@ -433,15 +445,18 @@ scan_kernel(ScanArgs a) {
                     if (__all_sync(0xffffffffu, dead)) { pruned = true; break; }
                 }
             }
-            if (pruned) continue;
+            if (!pruned) {
 #pragma unroll
-            for (int j = 0; j < QG; ++j) {
-                if (unit.q[j] < 0) continue;
+                for (int j = 0; j < QG; ++j) {
+                    if (unit.q[j] < 0) continue;
 #pragma unroll
-                for (int u = 0; u < PPW; ++u)
-                    top[j].push(id[u] >= 0 ? make_key(dd[u][j], id[u]) : KEY_EMPTY, lane, a.ck,
-                                a.ck_pad, merge_n, tau + j, a.gthr + unit.q[j]);
+                    for (int u = 0; u < PPW; ++u)
+                        top[j].push(id[u] >= 0 ? make_key(dd[u][j], id[u]) : KEY_EMPTY, lane, a.ck,
+                                    a.ck_pad, merge_n, tau + j, a.gthr + unit.q[j]);
+                }
             }
+#pragma unroll
+            for (int u = 0; u < PPW; ++u) { id[u] = idn[u]; cur[u] = curn[u]; }
         }
     }
     if (run_open) close_run();
