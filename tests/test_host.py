@@ -97,3 +97,52 @@ def test_benchmark_shapes_pass_validation(jhq, d, M, nlist):
         idx.close()
     except jhq.JHQError as e:
         assert e.code == jhq.JHQ_EDEVICE
+
+
+def _bf16_rne(x):
+    """bf16 round-to-nearest-even of float32 x, as float32 (coarse_tc.cu bf16_rne)."""
+    u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+@pytest.mark.parametrize("case", ["normal", "offset", "uint8_like", "tiny_query"])
+def test_coarse_margin_bound_holds(case):
+    """The tensor-core coarse scores use x = hi + lo (bf16 RNE pieces) and the sum
+    q_hi.c_hi + q_hi.c_lo + q_lo.c_hi over 3d products; select_probes_margin
+    (ivf.cu) takes every list within 2E of the approximate nprobe-th score, with
+    E = (2 eps |q| cmax + 2^-21 (cmax^2 + 2 |q| cmax)) * 1.01,
+    eps = 6 * 2^-18 + d (3 * 2^-22 + 2^-23). Emulated here with fp32 sums in
+    either order: |s~ - s| <= E must hold for every list."""
+    rng = np.random.default_rng(7)
+    d, n = 128, 3000
+    if case == "normal":
+        c = rng.standard_normal((n, d)).astype(np.float32); q = rng.standard_normal(d).astype(np.float32)
+    elif case == "offset":
+        c = (rng.standard_normal((n, d)) + 50).astype(np.float32); q = (rng.standard_normal(d) + 50).astype(np.float32)
+    elif case == "uint8_like":
+        c = rng.integers(0, 256, (n, d)).astype(np.float32); q = rng.integers(0, 256, d).astype(np.float32)
+    else:
+        c = rng.standard_normal((n, d)).astype(np.float32); q = (rng.standard_normal(d) * 1e-4).astype(np.float32)
+    norms = (c.astype(np.float64) ** 2).sum(1).astype(np.float32)
+    # exact fp32 chain score (gemm_rows EPI_COARSE order)
+    acc = np.zeros(n, np.float32)
+    for j in range(d):
+        acc = (np.float64(q[j]) * c[:, j] + acc).astype(np.float32)      # one rounding: fma
+    s = (norms - np.float32(2) * acc).astype(np.float32)
+    # bf16 split products, summed in fp32 forwards and backwards
+    qh = _bf16_rne(q); ql = _bf16_rne((q - qh).astype(np.float32))
+    ch = _bf16_rne(c); cl = _bf16_rne((c - ch).astype(np.float32))
+    terms = np.concatenate([qh[None, :] * ch, qh[None, :] * cl, ql[None, :] * ch], 1).astype(np.float32)
+    worst = 0.0
+    for order in (slice(None), slice(None, None, -1)):
+        t = np.zeros(n, np.float32)
+        for col in terms.T[order]:
+            t = (t + col).astype(np.float32)
+        st = (norms - np.float32(2) * t).astype(np.float32)
+        worst = max(worst, float(np.max(np.abs(st.astype(np.float64) - s))))
+    qn = float(np.sqrt((q.astype(np.float32) ** 2).sum())) * 1.001
+    cmax = float(np.sqrt(norms.max())) * 1.0001
+    eps = 6 * 2.0 ** -18 + d * (3 * 2.0 ** -22 + 2.0 ** -23)
+    E = (2 * eps * qn * cmax + 2.0 ** -21 * (cmax * cmax + 2 * qn * cmax)) * 1.01
+    assert worst <= E, (worst, E)
