@@ -228,6 +228,15 @@ void Index::upload_pilot(const std::vector<float>& c, int P) {
     JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
+void Index::set_pilot(const float* cents, int P) {
+    DeviceGuard g(dev_);
+    if (!trained_ || ntotal_ > 0) fail(JHQ_ESTATE, "set_pilot: needs a trained, empty index");
+    if (P < 0 || (P > 0 && !cents)) fail(JHQ_EINVAL, "set_pilot: bad clusters");
+    pilot_cents_.assign(cents, cents + (size_t)P * d_);
+    pilotP_ = P;
+    if (P > 0) upload_pilot(pilot_cents_, P);
+}
+
 // ---- train: JHQGpuIndex::train (jhq_gpu_index.cu:333-364) --------------------
 void Index::train(const float* h_x, int64_t n) {
     DeviceGuard g(dev_);

@@ -76,6 +76,9 @@ public:
 
     int K1D() const { return K1D_; }
     int pilot_lists() const { return pilotP_; }
+    // Pilot clusters (flat index): copy out [P][d]; install on a trained, empty index.
+    const std::vector<float>& pilot_centroids() const { return pilot_cents_; }
+    void set_pilot(const float* cents, int P);
     int Kr() const { return Kr_; }
     int bpv() const { return bpv_; }
 

@@ -6,7 +6,7 @@
 // Vectors are placed round-robin by global id: id g lives on shard g % S as
 // local id g / S, so ids need no map and repeated add() calls keep the rule.
 // All shards hold the same trained artefacts (shard 0 trains, the others
-// import its artefacts), so probe choices agree everywhere.
+// import its artefacts and its pilot clusters), so probe choices agree everywhere.
 //
 // search(), per chunk of queries:
 //   1. the queries go to every shard's device;
