@@ -112,6 +112,19 @@ int jhq_search_device_probes(jhq_index* idx, const float* d_q, const int32_t* d_
  * construction; this allows an nprobe sweep on one trained index. */
 int jhq_set_nprobe(jhq_index* idx, int nprobe);
 
+/* Exact rerank over stored vectors. The reference's JHQ indexes return the k
+ * best refined JHQ distances; its hblock graph indexes keep the vectors and
+ * rerank candidates by exact L2 (hblock_v34/jhq_gpu_index.cu:628-629,
+ * hblock_v34/search.cu:531-690). With R > 0 this index keeps every added
+ * vector (fp32, d*4 bytes each, from the next add() on, so enable it before
+ * the first add), a search for k takes the best max(R, k) JHQ candidates
+ * (ck = max(R', ceil(alpha R'))) and returns the k nearest of them by exact L2,
+ * with the distance ||q - x||^2 (no offset). R = 0 restores the reference's
+ * JHQ search. Errors: R outside [0, 256] or d % 4 != 0 -> JHQ_EINVAL; enabling
+ * it on a non-empty index that keeps no vectors -> JHQ_ESTATE. */
+int jhq_set_rerank(jhq_index* idx, int R);
+int jhq_get_rerank(const jhq_index* idx, int* R);
+
 /* Accessors: JHQGpuIndex::ntotal() / dim() (jhq_gpu_index.cuh:44-45). */
 int jhq_ntotal(const jhq_index* idx, int64_t* n);
 int jhq_dim(const jhq_index* idx, int* d);

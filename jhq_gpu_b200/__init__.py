@@ -35,7 +35,8 @@ EXPORTED = [
     "jhq_encode", "jhq_save", "jhq_load", "jhq_merge_shards", "jhq_kernel_launches",
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
-    "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_probe_device",
+    "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_set_rerank", "jhq_get_rerank",
+    "jhq_probe_device",
     "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
     "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
     "jhq_sharded_ntotal",
@@ -101,6 +102,8 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_search_device_noalloc.argtypes = [vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_synchronize.argtypes = [vp, C.c_double]
     L.jhq_set_nprobe.argtypes = [vp, C.c_int]
+    L.jhq_set_rerank.argtypes = [vp, C.c_int]
+    L.jhq_get_rerank.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_probe_device.argtypes = [vp, vp, i64, vp, vp]
     L.jhq_search_device_probes.argtypes = [vp, vp, vp, i64, C.c_int, vp, vp, vp]
     L.jhq_ntotal.argtypes = [vp, C.POINTER(C.c_int64)]
@@ -273,6 +276,17 @@ class JHQGpuIndex:
         """Probe count of later searches (clamped to nlist)."""
         _check(self._L.jhq_set_nprobe(self._h, nprobe))
         self.params.nprobe = min(nprobe, self.params.nlist)
+
+    def set_rerank(self, R: int) -> None:
+        """Exact L2 rerank of the best max(R, k) JHQ candidates over the stored
+        vectors (jhq_set_rerank); enable before the first add(). 0 = off."""
+        _check(self._L.jhq_set_rerank(self._h, R))
+
+    @property
+    def rerank(self) -> int:
+        r = C.c_int()
+        _check(self._L.jhq_get_rerank(self._h, C.byref(r)))
+        return r.value
 
     def synchronize(self, timeout_s: float = 60.0) -> None:
         _check(self._L.jhq_synchronize(self._h, timeout_s))

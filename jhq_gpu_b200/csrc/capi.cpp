@@ -143,6 +143,17 @@ int jhq_set_nprobe(jhq_index* idx, int nprobe) {
     return guarded([&] { need(idx)->set_nprobe(nprobe); });
 }
 
+int jhq_set_rerank(jhq_index* idx, int R) {
+    return guarded([&] { need(idx)->set_rerank(R); });
+}
+
+int jhq_get_rerank(const jhq_index* idx, int* R) {
+    return guarded([&] {
+        if (!R) jhq::fail(JHQ_EINVAL, "null output");
+        *R = need(idx)->rerank();
+    });
+}
+
 int jhq_ntotal(const jhq_index* idx, int64_t* n) {
     return guarded([&] {
         if (!n) jhq::fail(JHQ_EINVAL, "null output");

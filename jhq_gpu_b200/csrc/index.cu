@@ -349,7 +349,12 @@ void Index::grow_master(int64_t need) {
     DevBuf<uint8_t> pc((size_t)nc * M_), rc((size_t)nc * bpv_pad_);
     DevBuf<float> co((size_t)nc);
     DevBuf<int32_t> as((size_t)nc);
+    DevBuf<float> rw;
+    if (keep_raw_) rw.resize((size_t)nc * d_);
     if (ntotal_ > 0) {
+        if (keep_raw_)
+            JHQ_CUDA(cudaMemcpyAsync(rw.get(), draw_.get(), (size_t)ntotal_ * d_ * 4,
+                                     cudaMemcpyDeviceToDevice, stream_));
         JHQ_CUDA(cudaMemcpyAsync(pc.get(), dpcodes_.get(), (size_t)ntotal_ * M_, cudaMemcpyDeviceToDevice, stream_));
         JHQ_CUDA(cudaMemcpyAsync(rc.get(), drcodes_.get(), (size_t)ntotal_ * bpv_pad_, cudaMemcpyDeviceToDevice, stream_));
         JHQ_CUDA(cudaMemcpyAsync(co.get(), dcorr_.get(), (size_t)ntotal_ * 4, cudaMemcpyDeviceToDevice, stream_));
@@ -360,6 +365,7 @@ void Index::grow_master(int64_t need) {
     drcodes_ = std::move(rc);
     dcorr_ = std::move(co);
     dassign_ = std::move(as);
+    if (keep_raw_) draw_ = std::move(rw);
     cap_ = nc;
 }
 
@@ -379,6 +385,9 @@ void Index::add(const float* h_x, int64_t n) {
         const int64_t nr = std::min(AB, n - r0);
         const int64_t at = ntotal_ + r0;
         h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
+        if (keep_raw_)
+            JHQ_CUDA(cudaMemcpyAsync(draw_.get() + at * d_, dx.get(), (size_t)nr * d_ * 4,
+                                     cudaMemcpyDeviceToDevice, stream_));
         rotate_device(dx.get(), nr, dy.get(), stream_);
         assign_device(dy.get(), nr, dassign_.get() + at, stream_);
         if (pilotP_ > 0) {
@@ -453,8 +462,11 @@ void Index::check_search_args(int64_t nq, int k) const {
     if (nq < 0) fail(JHQ_EINVAL, "nq must be >= 0");
     if (k <= 0) fail(JHQ_EINVAL, "k must be positive");
     if (!trained_ || ntotal_ == 0) fail(JHQ_ESTATE, "index is empty");
-    int ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
-    if (next_pow2(ck) > MAX_CK_PAD) fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) must be <= 256");
+    const int kj = stage_k(k);
+    int ck = std::max(kj, (int)std::ceil(p_.alpha * (float)kj));
+    if (next_pow2(ck) > MAX_CK_PAD)
+        fail(JHQ_EINVAL, rerank_ > 0 ? "max(R, ceil(alpha*R)) must be <= 256 (R = rerank depth)"
+                                     : "max(k, ceil(alpha*k)) must be <= 256");
     if (scan_smem_bytes(Mp_, d_, std::max(32, next_pow2(ck)), scan_mode_for(d_, M_, B_, 1.0)) > 227 * 1024)
         fail(JHQ_EINVAL, "max(k, ceil(alpha*k)) too large for this M: the LUT and the top-ck "
                          "lists must fit in shared memory together");
@@ -464,7 +476,8 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
     BatchShape sh;
     sh.Bq = Bq;
     sh.k = k;
-    sh.ck = std::max(k, (int)std::ceil(p_.alpha * (float)k));
+    sh.kr = stage_k(k);
+    sh.ck = std::max(sh.kr, (int)std::ceil(p_.alpha * (float)sh.kr));
     sh.ck_pad = std::max(32, next_pow2(sh.ck));
     // queries per list decide the query-group size; shrink it while the tables
     // and top-ck lists do not fit in shared memory
@@ -648,14 +661,19 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     ra.qslot_off = b.plan.qslot_off; ra.gthr = b.plan.gthr; ra.rcodes = drcodes_.get();
     ra.corr = dcorr_.get(); ra.out_dists = out_d; ra.out_ids = out_i;
     ra.nq = nq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = sh.ck;
-    ra.ck_pad = sh.ck_pad; ra.k = sh.k;
+    ra.ck_pad = sh.ck_pad; ra.k = sh.k; ra.kr = sh.kr;
+    if (keep_raw_ && rerank_ > 0) {
+        ra.q_raw = q_in;
+        ra.raw = draw_.get();
+    }
     refine_topk(ra, s);
     mark(5);
 }
 
 void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     BatchShape sh;
-    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.ck = ws_.ck; sh.ck_pad = ws_.ck_pad;
+    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.kr = stage_k(ws_.k); sh.ck = ws_.ck;
+    sh.ck_pad = ws_.ck_pad;
     sh.grid = ws_.grid; sh.mode = ws_.mode; sh.chunk_pages = ws_.chunk_pages;
     sh.max_slots = ws_.max_slots;
     sh.qmajor = ws_.qmajor;
@@ -687,6 +705,23 @@ void Index::run_batch(cudaStream_t s, int nvalid) {
         stage_ms_[i] += ms;
     }
     ++stage_batches_;
+}
+
+void Index::set_rerank(int R) {
+    if (R < 0 || R > MAX_CK_PAD) fail(JHQ_EINVAL, "rerank: R must be in [0, 256]");
+    if (R > 0 && !keep_raw_) {
+        if (ntotal_ > 0)
+            fail(JHQ_ESTATE, "rerank: enable it before the first add() (the vectors are kept "
+                             "from then on)");
+        if (d_ % 4 != 0) fail(JHQ_EINVAL, "rerank: d must be a multiple of 4");
+        keep_raw_ = true;
+        if (cap_ > 0) draw_.resize((size_t)cap_ * d_);
+    }
+    if (R != rerank_) {
+        rerank_ = R;
+        destroy_graph();
+        ws_.k = 0;                     // re-plan the batch shape
+    }
 }
 
 void Index::set_profiling(bool on) {
@@ -801,7 +836,8 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     prepare_workspace(k);
     cudaStream_t s = stream ? stream : stream_;
     BatchShape sh;
-    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.ck = ws_.ck; sh.ck_pad = ws_.ck_pad;
+    sh.Bq = ws_.batch_cap; sh.k = ws_.k; sh.kr = stage_k(ws_.k); sh.ck = ws_.ck;
+    sh.ck_pad = ws_.ck_pad;
     sh.grid = ws_.grid; sh.mode = ws_.mode; sh.chunk_pages = ws_.chunk_pages;
     sh.max_slots = ws_.max_slots; sh.qmajor = ws_.qmajor;
     BatchBufs b;
@@ -902,7 +938,8 @@ void Index::save(const std::string& path) const {
     put(MAGIC, 8);
     put(&FORMAT_VERSION, 4);
     int32_t hdr[12] = {d_, p_.M, p_.B, p_.Br, p_.nlist, p_.nprobe, p_.ivf_iters,
-                       p_.batch_size, p_.seed, p_.add_batch, pilotP_, 0};
+                       p_.batch_size, p_.seed, p_.add_batch, pilotP_,
+                       (keep_raw_ ? 1 : 0) | (rerank_ << 8)};   // flags: kept vectors, rerank R
     put(hdr, sizeof hdr);
     put(&p_.alpha, 4);
     put(&sigma_, 4);
@@ -922,6 +959,11 @@ void Index::save(const std::string& path) const {
         put(co.data(), co.size() * 4);
         put(as.data(), as.size() * 4);
         if (pilotP_ > 0) put(h_pilot_assign_.data(), (size_t)ntotal_ * 4);
+        if (keep_raw_) {
+            std::vector<float> rw((size_t)ntotal_ * d_);
+            JHQ_CUDA(cudaMemcpy(rw.data(), draw_.get(), rw.size() * 4, cudaMemcpyDeviceToHost));
+            put(rw.data(), rw.size() * 4);
+        }
     }
     if (!f) fail(JHQ_EIO, "save: write failed for " + path);
 }
@@ -969,6 +1011,11 @@ Index* Index::load(const std::string& path, int device) {
             idx->upload_pilot(pc, P);
             idx->pilotP_ = P;
         }
+        const int flags = hdr[11];
+        if ((flags & 1) && idx->d_ % 4 != 0) fail(JHQ_EIO, "load: bad flags");
+        idx->keep_raw_ = (flags & 1) != 0;
+        idx->rerank_ = idx->keep_raw_ ? (flags >> 8) : 0;
+        if (idx->rerank_ < 0 || idx->rerank_ > MAX_CK_PAD) fail(JHQ_EIO, "load: bad rerank depth");
         if (n > 0) {
             DeviceGuard g(idx->dev_);
             std::vector<uint8_t> pc((size_t)n * idx->M_), rc((size_t)n * idx->bpv_);
@@ -994,6 +1041,11 @@ Index* Index::load(const std::string& path, int device) {
                                   idx->bpv_pad_ - idx->bpv_, (size_t)n));
             JHQ_CUDA(cudaMemcpy(idx->dcorr_.get(), co.data(), co.size() * 4, cudaMemcpyHostToDevice));
             JHQ_CUDA(cudaMemcpy(idx->dassign_.get(), as.data(), as.size() * 4, cudaMemcpyHostToDevice));
+            if (idx->keep_raw_) {
+                std::vector<float> rw((size_t)n * d);
+                get(rw.data(), rw.size() * 4);
+                JHQ_CUDA(cudaMemcpy(idx->draw_.get(), rw.data(), rw.size() * 4, cudaMemcpyHostToDevice));
+            }
             idx->h_assign_ = std::move(as);
             idx->ntotal_ = n;
             idx->rebuild_layout();

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <algorithm>
 #include <functional>
 #include <string>
 #include <vector>
@@ -81,6 +82,13 @@ public:
     void set_pilot(const float* cents, int P);
     int Kr() const { return Kr_; }
     int bpv() const { return bpv_; }
+    // Exact rerank: the index keeps its vectors as given (fp32, [N][d]) from the
+    // first add() on; a search for k then takes the best max(R, k) JHQ
+    // candidates and returns the k nearest of them by exact L2. R = 0 turns the
+    // rerank off (the reference's JHQ search); the stored vectors stay.
+    void set_rerank(int R);
+    int rerank() const { return rerank_; }
+    bool keeps_vectors() const { return keep_raw_; }
 
 private:
     struct Workspace {                 // SearchWorkspace (search.cuh:24-46)
@@ -123,7 +131,7 @@ private:
     void destroy_graph();
     // Shapes of one search batch: ck, scan mode / grid / chunking, slot bound.
     struct BatchShape {
-        int Bq, k, ck, ck_pad, grid, mode, chunk_pages, qmajor;
+        int Bq, k, kr, ck, ck_pad, grid, mode, chunk_pages, qmajor;
         int64_t max_slots;
     };
     // Device temporaries of one batch (workspace or fixed scratch array).
@@ -143,6 +151,8 @@ private:
     void enqueue_batch(cudaStream_t s, cudaEvent_t* ev = nullptr);
     void run_batch(cudaStream_t s, int nvalid);
     void check_search_args(int64_t nq, int k) const;
+    // candidates the JHQ stage returns for a search of k: k, or max(R, k) with rerank
+    int stage_k(int k) const { return rerank_ > 0 ? std::max(rerank_, k) : k; }
 
     int d_, M_, B_, Br_, Ds_, bpd_, K1D_, Kr_, bpv_, bpv_pad_, Mp_;
     Params p_;
@@ -175,6 +185,9 @@ private:
     bool coarse_tc_ = false;
     DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
     DevBuf<float> dcorr_;
+    bool keep_raw_ = false;            // stored vectors for the exact rerank
+    int rerank_ = 0;
+    DevBuf<float> draw_;               // [cap][d] vectors as given (keep_raw_)
     DevBuf<int32_t> dassign_, dslot_ids_, dlist_page_off_;
     Workspace ws_;
 };

@@ -157,7 +157,12 @@ struct RefineArgs {
     const float* corr;         // [N]
     float* out_dists;          // [nq][k]
     int32_t* out_ids;          // [nq][k]
+    // exact rerank (optional): the kr best composite candidates are re-scored
+    // by exact L2 against the stored vectors raw [N][d] and the k best returned
+    const float* q_raw = nullptr;   // [nq][d] the queries as given
+    const float* raw = nullptr;     // [N][d] stored vectors, nullptr = no rerank
     int nq, d, Br, bpv_pad, ck, ck_pad, k;
+    int kr = 0;                     // candidates re-scored (k <= kr <= ck)
 };
 void refine_topk(const RefineArgs& a, cudaStream_t st);
 void refine_configure();

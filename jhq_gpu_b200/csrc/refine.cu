@@ -13,6 +13,13 @@
 //      comp = (primary + residual) + corr (search.cu:240);
 //   3. block bitonic sort of the ck composite keys; the first k are written,
 //      missing ones as (+inf, -1) (search.cu:285-286).
+//   4. (exact rerank, when the index keeps its vectors) the first kr composite
+//      keys are re-scored by exact L2 against the stored vectors — warp per
+//      candidate, lane l takes float4 chunks l, l+32, ... of the row as an
+//      in-order fma chain, xor butterfly 16..1 — and the k smallest (distance,
+//      id) keys are written instead. This is the exact L2 rerank over stored
+//      vectors of the reference's hblock indexes (hblock_v34/search.cu:531-690)
+//      applied behind the JHQ refine.
 #include "device_utils.cuh"
 #include "jhq_common.h"
 #include "kernels.cuh"
@@ -35,6 +42,7 @@ refine_kernel(RefineArgs a) {
     // and the padding puts the 32 lanes in 32 different banks.
     float* qs = reinterpret_cast<float*>(buf + RF_CAP + 2);        // d + d/32 + 1
     float* rc1d = qs + a.d + a.d / 32 + 1;                         // 256
+    float* qraw = qs + ((a.d + a.d / 32 + 1 + 256 + 3) & ~3);      // d (rerank only), 16-byte aligned
 
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (q >= a.nq) return;
@@ -42,6 +50,8 @@ refine_kernel(RefineArgs a) {
     for (int i = tid; i < a.ck_pad; i += RF_THREADS) top[i] = KEY_EMPTY;
     for (int i = tid; i < a.d; i += RF_THREADS) qs[i + (i >> 5)] = a.q_rot[(int64_t)q * a.d + i];
     for (int i = tid; i < Kr; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
+    if (a.raw)
+        for (int i = tid; i < a.d; i += RF_THREADS) qraw[i] = a.q_raw[(int64_t)q * a.d + i];
     __syncthreads();
 
     // candidates of query q: its slots [qslot_off[q], qslot_off[q+1]), ck keys
@@ -113,8 +123,38 @@ refine_kernel(RefineArgs a) {
     }
     __syncthreads();
     block_bitonic_sort(comp, a.ck_pad);
+    uint64_t* fin = comp;
+    if (a.raw) {                               // exact rerank of the kr best
+        int kr_pad = 32;
+        while (kr_pad < a.kr) kr_pad <<= 1;
+        const float4* q4 = reinterpret_cast<const float4*>(qraw);
+        const int c4 = a.d / 4;
+        for (int i = warp; i < kr_pad; i += RF_WARPS) {
+            const uint64_t key = (i < a.kr) ? comp[i] : KEY_EMPTY;
+            if (key == KEY_EMPTY) {
+                if (lane == 0) buf[i] = KEY_EMPTY;
+                continue;
+            }
+            const int id = key_id(key);
+            const float4* row = reinterpret_cast<const float4*>(a.raw + (int64_t)id * a.d);
+            float acc = 0.0f;
+            for (int c = lane; c < c4; c += 32) {
+                const float4 v = __ldg(row + c), w = q4[c];
+                float t = w.x - v.x; acc = __fmaf_rn(t, t, acc);
+                t = w.y - v.y; acc = __fmaf_rn(t, t, acc);
+                t = w.z - v.z; acc = __fmaf_rn(t, t, acc);
+                t = w.w - v.w; acc = __fmaf_rn(t, t, acc);
+            }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+            if (lane == 0) buf[i] = make_key(acc, id);
+        }
+        __syncthreads();
+        block_bitonic_sort(buf, kr_pad);
+        fin = buf;
+    }
     for (int i = tid; i < a.k; i += RF_THREADS) {
-        const uint64_t key = comp[i];
+        const uint64_t key = fin[i];
         const bool ok = key != KEY_EMPTY;
         a.out_dists[(int64_t)q * a.k + i] = ok ? key_dist(key) : __int_as_float(0x7f800000);
         a.out_ids[(int64_t)q * a.k + i] = ok ? key_id(key) : -1;
@@ -153,7 +193,7 @@ merge_shards_kernel(const float* __restrict__ in_d, const int32_t* __restrict__ 
 void refine_topk(const RefineArgs& a, cudaStream_t st) {
     if (a.nq <= 0) return;
     size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + 256) * 4 +
-                  (size_t)RF_CAP * 8 + 16;
+                  (size_t)RF_CAP * 8 + 16 + (a.raw ? (size_t)a.d * 4 + 16 : 0);
     refine_kernel<<<a.nq, RF_THREADS, smem, st>>>(a);
     JHQ_LAUNCH_CHECK();
     count_launch();

@@ -65,7 +65,19 @@ class Oracle:
                                     _f32p, _f32p, _u8p, _u8p, _f32p, _i32p, _i64,
                                     _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_float,
                                     C.c_int, _f32p, _i32p]
+        L.oracle_rerank.argtypes = [_f32p, _i64, C.c_int, _f32p, _i64, _i32p, C.c_int, C.c_int,
+                                    _f32p, _i32p]
         self.L = L
+
+    def rerank(self, q, x, cand, k):
+        """Exact L2 rerank of candidate ids cand [nq][kr] against x (oracle_rerank)."""
+        q, x = _f32(q), _f32(x)
+        cand = np.ascontiguousarray(cand, np.int32)
+        D = np.zeros((len(q), k), np.float32)
+        I = np.zeros((len(q), k), np.int32)
+        if self.L.oracle_rerank(q, len(q), q.shape[1], x, len(x), cand, cand.shape[1], k, D, I):
+            raise ValueError("oracle_rerank: bad arguments")
+        return D, I
 
     def sigma(self, x):
         x = _f32(x)
@@ -282,4 +294,63 @@ class RefGPU:
                              batch, reps, I.reshape(-1), C.byref(tr), C.byref(ad), ms)
         if rc != 0:
             raise RuntimeError("reference sweep failed")
+        return I, ms, dict(train_ms=tr.value, add_ms=ad.value)
+
+    def pin(self, y, q_rot, *, M, c1d, res_c1d, cents, sigma=1.0, B=8, Br=4, alpha=4.0, k=10,
+            nlist=1, nprobe=1, batch=64):
+        """Run the reference's own add() encode and search() on the caller's artefacts
+        (identity rotation, already-rotated y and q_rot; see ref_gpu_pin). Returns
+        (primary codes [n][M], residual codes [n][bpv], corr [n], D [nq][k], I [nq][k]),
+        all in id order."""
+        y, q = _f32(y), _f32(q_rot)
+        n, d = y.shape
+        bpv = (d * Br + 7) // 8
+        pc = np.zeros((n, M), np.uint8)
+        rc = np.zeros((n, bpv), np.uint8)
+        co = np.zeros(n, np.float32)
+        D = np.zeros((len(q), k), np.float32)
+        I = np.zeros((len(q), k), np.int32)
+        L = self.L
+        L.ref_gpu_pin.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  _f32p, C.c_int, _f32p, C.c_int, _f32p, C.c_float,
+                                  _u8p, _u8p, _f32p, _f32p, _i32p]
+        c1d, res_c1d = _f32(c1d), _f32(res_c1d)
+        cents = _f32(cents) if nlist > 1 else np.zeros((1, d), np.float32)
+        rcode = L.ref_gpu_pin(y, n, q, len(q), d, M, B, Br, alpha, k, nlist, nprobe, batch,
+                              c1d, len(c1d), res_c1d, len(res_c1d), cents, sigma,
+                              pc, rc, co, D, I)
+        if rcode != 0:
+            raise RuntimeError(f"reference {self.version} pin run failed ({rcode})")
+        return pc, rc, co, D, I
+
+
+class RefHBlock:
+    """The reference's own hblock graph index (v34 / v35 / v36), built from its
+    sources by `make -C oracle ref_hblock`, driven like its demo main: train on
+    min(n, 200k) rows, add all, warm up at max_ef, time `reps` searches per ef."""
+
+    def __init__(self, version: str = "v34"):
+        path = os.path.join(HERE, "_ref", f"libref_hblock_{version}.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = C.CDLL(path)
+        dp = C.POINTER(C.c_double)
+        L.ref_hblock_run.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                     C.c_int, _i32p, C.c_int, C.c_int, _i32p, dp, dp,
+                                     np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        self.L = L
+        self.version = version
+
+    def sweep(self, x, q, *, efs=(8, 16, 32, 64, 128, 256), k=10, batch=1024, reps=5):
+        """Returns (ids [len(efs)][nq][k], mean search ms per ef, dict(train_ms, add_ms))."""
+        x, q = _f32(x), _f32(q)
+        e = np.ascontiguousarray(efs, np.int32)
+        I = np.zeros((len(e), len(q), k), np.int32)
+        ms = np.zeros(len(e), np.float64)
+        tr, ad = C.c_double(), C.c_double()
+        rc = self.L.ref_hblock_run(x, x.shape[0], q, len(q), x.shape[1], k, int(e.max()), batch,
+                                   e, len(e), reps, I.reshape(-1), C.byref(tr), C.byref(ad), ms)
+        if rc != 0:
+            raise RuntimeError(f"reference hblock {self.version} run failed")
         return I, ms, dict(train_ms=tr.value, add_ms=ad.value)

@@ -427,3 +427,52 @@ int oracle_search(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
     free(off); free(members);
     return 0;
 }
+
+/* Exact rerank over stored vectors (the hblock indexes' exact L2 stage,
+ * hblock_v34/search.cu:531-690, applied behind the JHQ refine). For each query,
+ * the first kr ids of cand [nq][kr] (-1 = none) are re-scored by ||q - x||^2
+ * summed as 32 lane partials (lane l takes dims 4c..4c+3 for c = l, l+32, ...,
+ * an in-order fma chain) joined by an xor butterfly, then the k smallest by
+ * (distance, id) are written, missing ones as (+inf, -1). */
+static float exact_l2_lanes(const float* q, const float* x, int d) {
+    float p[32];
+    int c4 = d / 4;
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int c = l; c < c4; c += 32)
+            for (int t = 0; t < 4; ++t) {
+                float diff = q[4 * c + t] - x[4 * c + t];
+                acc = fmaf(diff, diff, acc);
+            }
+        p[l] = acc;
+    }
+    for (int o = 16; o >= 1; o >>= 1) {
+        float t[32];
+        for (int l = 0; l < 32; ++l) t[l] = p[l] + p[l ^ o];
+        memcpy(p, t, sizeof(p));
+    }
+    return p[0];
+}
+
+int oracle_rerank(const float* q, int64_t nq, int d, const float* x, int64_t n,
+                  const int32_t* cand, int kr, int k, float* out_dists, int32_t* out_ids) {
+    if (d % 4 != 0 || kr <= 0 || k <= 0) return 1;
+    #pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t qi = 0; qi < nq; ++qi) {
+        float* bd = out_dists + qi * k;
+        int32_t* bi = out_ids + qi * k;
+        for (int i = 0; i < k; ++i) { bd[i] = INFINITY; bi[i] = -1; }
+        for (int i = 0; i < kr; ++i) {
+            int32_t id = cand[qi * kr + i];
+            if (id < 0 || id >= n) continue;
+            float dv = exact_l2_lanes(q + qi * d, x + (int64_t)id * d, d);
+            if (!better(dv, id, bd[k - 1], bi[k - 1])) continue;
+            int j = k - 1;
+            while (j > 0 && better(dv, id, bd[j - 1], bi[j - 1])) {
+                bd[j] = bd[j - 1]; bi[j] = bi[j - 1]; --j;
+            }
+            bd[j] = dv; bi[j] = id;
+        }
+    }
+    return 0;
+}

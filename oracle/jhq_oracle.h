@@ -78,6 +78,11 @@ int   oracle_search(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
                     int k, float alpha, int nthreads,
                     float* out_dists, int32_t* out_ids);
 
+/* Exact rerank (stored vectors): q [nq][d] and x [n][d] as given, cand [nq][kr]
+ * JHQ candidate ids (-1 = none). Outputs [nq][k]. Returns nonzero on bad args. */
+int   oracle_rerank(const float* q, int64_t nq, int d, const float* x, int64_t n,
+                    const int32_t* cand, int kr, int k, float* out_dists, int32_t* out_ids);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,14 +12,12 @@
 
 // The nprobe sweep below lowers the reference index's private nprobe_ member
 // between searches (the reference fixes it at construction and sizes its probe
-// buffers for it, so the index is built with the largest value of the sweep).
-#ifdef REF_HAS_IVF
+// buffers for it, so the index is built with the largest value of the sweep),
+// and ref_gpu_pin writes trained artefacts into, and reads the encoded lists
+// out of, its private members.
 #define private public
-#endif
 #include REF_INDEX_HEADER
-#ifdef REF_HAS_IVF
 #undef private
-#endif
 
 extern "C" int ref_gpu_run(const float* x, int n, int n_train, const float* q, int nq, int d,
                            int M, int B, int Br, float alpha, int k, int nlist, int nprobe,
@@ -90,3 +88,89 @@ extern "C" int ref_gpu_sweep(const float* x, int n, int n_train, const float* q,
     }
 }
 #endif
+
+// ---------------------------------------------------------------------------
+// Parity pin: run the reference's own add() encode and search() on artefacts
+// given by the caller instead of its train(): the rotation is the identity and
+// the caller passes already-rotated rows y and queries q_rot (I*x is exact in
+// fp32 whatever the GEMM's summation order, so both builds see the same y),
+// c1d / res_c1d / IVF centroids are the caller's. The centroid norms follow the
+// reference's own rule (double sum, jhq_gpu_index.cu:241-247).
+// Outputs, all in id order: primary codes [n][M], residual codes [n][bpv],
+// corrections [n] (read back from the reference's device buffers and, for v14,
+// un-permuted through its list_ids), and the search result [nq][k].
+namespace {
+template <class T>
+static void up(T** dst, const T* src, size_t n) {
+    cudaFree(*dst);
+    *dst = nullptr;
+    if (cudaMalloc((void**)dst, n * sizeof(T)) != cudaSuccess) throw std::bad_alloc();
+    cudaMemcpy(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice);
+}
+template <class T>
+static void down(T* dst, const T* src, size_t n) {
+    cudaMemcpy(dst, src, n * sizeof(T), cudaMemcpyDeviceToHost);
+}
+}  // namespace
+
+extern "C" int ref_gpu_pin(const float* y, int n, const float* q_rot, int nq, int d, int M,
+                           int B, int Br, float alpha, int k, int nlist, int nprobe, int batch,
+                           const float* c1d, int K1D, const float* res_c1d, int Kr,
+                           const float* cents, float sigma, uint8_t* out_pc, uint8_t* out_rc,
+                           float* out_corr, float* out_d, int* out_i) {
+    try {
+        jhq_gpu::JHQGpuIndex::Params p;
+        p.M = M; p.B = B; p.Br = Br; p.alpha = alpha;
+#ifdef REF_HAS_IVF
+        p.nlist = nlist; p.nprobe = nprobe; p.batch_size = batch;
+#else
+        (void)nlist; (void)nprobe; (void)batch; (void)cents;
+#endif
+        jhq_gpu::JHQGpuIndex idx(d, p);
+        if (K1D != idx.K1D_ || Kr != idx.Kr_) return 2;
+        idx.cb_ = std::make_unique<LloydMaxCodebook>(d, M, B, sigma);
+        std::vector<float> eye((size_t)d * d, 0.0f);
+        for (int i = 0; i < d; ++i) eye[(size_t)i * d + i] = 1.0f;
+        up(&idx.d_Pi_, eye.data(), eye.size());
+        up(&idx.d_c1d_, c1d, (size_t)K1D);
+        idx.res_c1d_.assign(res_c1d, res_c1d + Kr);
+        up(&idx.d_res_c1d_, res_c1d, (size_t)Kr);
+#ifdef REF_HAS_IVF
+        idx.centroids_.assign(cents, cents + (size_t)nlist * d);
+        std::vector<float> norms(nlist);
+        for (int c = 0; c < nlist; ++c) {
+            double s = 0.0;
+            for (int j = 0; j < d; ++j) s += (double)cents[(size_t)c * d + j] * cents[(size_t)c * d + j];
+            norms[c] = (float)s;
+        }
+        up(&idx.d_centroids_, cents, (size_t)nlist * d);
+        up(&idx.d_cent_norms_, norms.data(), (size_t)nlist);
+#endif
+        idx.add(y, n);
+        const int bpv = idx.bpv_;
+#ifdef REF_HAS_IVF
+        std::vector<int> ids(n);
+        std::vector<uint8_t> pt((size_t)M * n), rc((size_t)n * bpv);
+        std::vector<float> co(n);
+        down(ids.data(), idx.d_list_ids_, (size_t)n);
+        down(pt.data(), idx.d_list_primary_t_, pt.size());
+        down(rc.data(), idx.d_list_res_, rc.size());
+        down(co.data(), idx.d_list_corr_, (size_t)n);
+        for (int pos = 0; pos < n; ++pos) {
+            const int v = ids[pos];
+            if (v < 0 || v >= n) return 3;
+            for (int m = 0; m < M; ++m) out_pc[(size_t)v * M + m] = pt[(size_t)m * n + pos];
+            std::memcpy(out_rc + (size_t)v * bpv, rc.data() + (size_t)pos * bpv, bpv);
+            out_corr[v] = co[pos];
+        }
+#else
+        down(out_pc, idx.d_primary_codes_, (size_t)n * M);
+        down(out_rc, idx.d_res_codes_, (size_t)n * bpv);
+        down(out_corr, idx.d_corrections_, (size_t)n);
+#endif
+        idx.search(q_rot, nq, k, out_d, out_i);
+        return cudaDeviceSynchronize() == cudaSuccess ? 0 : 4;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}

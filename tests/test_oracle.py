@@ -120,3 +120,25 @@ def test_oracle_vs_live_reference_build():
         c1d = o.c1d(s, K)
         assert np.array_equal(c1d, r.c1d(32, M, 8, s))
         assert np.array_equal(o.encode_primary(y, M, 8, c1d), r.encode(32, M, 8, s, y))
+
+
+def test_oracle_rerank_is_exact_l2(oracle):
+    """oracle_rerank: exact L2 (fp32 lane order) within float rounding of an fp64
+    reference, (distance, id) order, -1 candidates skipped, (+inf, -1) padding."""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((500, 68)).astype(np.float32)
+    q = rng.standard_normal((7, 68)).astype(np.float32)
+    cand = np.stack([rng.permutation(501)[:30] - 1 for _ in range(7)]).astype(np.int32)
+    cand[0, :] = -1
+    cand[1, 5:] = -1
+    D, I = oracle.rerank(q, x, cand, 10)
+    assert (I[0] == -1).all() and np.isinf(D[0]).all()
+    assert (I[1, 5:] == -1).all()
+    for qi in range(2, 7):
+        ids = np.unique(cand[qi][cand[qi] >= 0])
+        ex = ((x[ids].astype(np.float64) - q[qi]) ** 2).sum(1)
+        order = np.lexsort((ids, ex))[:10]
+        assert np.allclose(D[qi], ex[order], rtol=1e-5)
+        np.testing.assert_allclose(D[qi], ((x[I[qi]].astype(np.float64) - q[qi]) ** 2).sum(1),
+                                   rtol=1e-5)
+        assert all((D[qi][j], I[qi][j]) <= (D[qi][j + 1], I[qi][j + 1]) for j in range(9))
