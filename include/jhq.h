@@ -86,12 +86,21 @@ int jhq_search_device(jhq_index* idx, const float* d_q, int64_t nq, int k,
  * loads the library keeps until exit. For callers that may not allocate device
  * memory while serving (a host that owns a fixed pool, real-time paths, a
  * framework that reserved the whole GPU). No counterpart in the reference.
- * The first call on a device looks up that array (cudaGetSymbolAddress); make
- * it before any stream capture. A batch needing more than 16 MiB of
- * temporaries returns JHQ_EINVAL. All calls on a device share the array, so
+ * The first call on a device looks up that array (cudaGetSymbolAddress, once
+ * per device for the life of the process); make it before any stream capture,
+ * and do not use the library on that device after cudaDeviceReset. A batch
+ * needing more than 16 MiB of temporaries returns JHQ_EINVAL. All calls on a device share the array, so
  * calls that overlap on the GPU race: serialise them. */
 int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int k,
                               float* d_dists, int32_t* d_ids, void* stream);
+
+/* Device-side failure report for searches on the CALLER's stream
+ * (jhq_search_device, jhq_search_device_noalloc, jhq_search_device_probes):
+ * after that stream has drained, returns JHQ_ETIMEDOUT (and clears the flag)
+ * if a bounded device wait of such a search gave up — its results are then
+ * not valid — else JHQ_OK. jhq_search and jhq_synchronize check the same flag
+ * themselves. No counterpart in the reference (its device errors exit). */
+int jhq_device_status(jhq_index* idx);
 
 /* Waits for the index's stream with a deadline (replaces the unbounded
  * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
@@ -112,6 +121,11 @@ int jhq_search_device_probes(jhq_index* idx, const float* d_q, const int32_t* d_
  * construction; this allows an nprobe sweep on one trained index. */
 int jhq_set_nprobe(jhq_index* idx, int nprobe);
 
+/* Candidate oversampling alpha (Params::alpha, ck = max(k, ceil(alpha k)),
+ * search.cu:408) on a built index; alpha <= 0 -> JHQ_EINVAL. The reference
+ * fixes alpha at construction; this allows an alpha sweep on one index. */
+int jhq_set_alpha(jhq_index* idx, float alpha);
+
 /* Exact rerank over stored vectors. The reference's JHQ indexes return the k
  * best refined JHQ distances; its hblock graph indexes keep the vectors and
  * rerank candidates by exact L2 (hblock_v34/jhq_gpu_index.cu:628-629,
@@ -129,6 +143,9 @@ int jhq_get_rerank(const jhq_index* idx, int* R);
 int jhq_ntotal(const jhq_index* idx, int64_t* n);
 int jhq_dim(const jhq_index* idx, int* d);
 int jhq_is_trained(const jhq_index* idx, int* trained);
+/* Vectors per IVF list, sizes[nlist] (the reference's list_offsets differences,
+ * jhq_gpu_index.cu:475-495). */
+int jhq_list_sizes(const jhq_index* idx, int64_t* sizes);
 
 /* ---- trained artefacts (Pi, c1d, res_c1d, IVF centroids) -------------
  * The reference keeps these private (jhq_gpu_index.cuh:56-61). They are

@@ -36,6 +36,7 @@ EXPORTED = [
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_set_rerank", "jhq_get_rerank",
+    "jhq_set_alpha", "jhq_list_sizes", "jhq_device_status",
     "jhq_probe_device",
     "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
     "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
@@ -103,6 +104,9 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_synchronize.argtypes = [vp, C.c_double]
     L.jhq_set_nprobe.argtypes = [vp, C.c_int]
     L.jhq_set_rerank.argtypes = [vp, C.c_int]
+    L.jhq_set_alpha.argtypes = [vp, C.c_float]
+    L.jhq_list_sizes.argtypes = [vp, C.POINTER(C.c_int64)]
+    L.jhq_device_status.argtypes = [vp]
     L.jhq_get_rerank.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_probe_device.argtypes = [vp, vp, i64, vp, vp]
     L.jhq_search_device_probes.argtypes = [vp, vp, vp, i64, C.c_int, vp, vp, vp]
@@ -276,6 +280,20 @@ class JHQGpuIndex:
         """Probe count of later searches (clamped to nlist)."""
         _check(self._L.jhq_set_nprobe(self._h, nprobe))
         self.params.nprobe = min(nprobe, self.params.nlist)
+
+    def check_device_status(self) -> None:
+        """Raises JHQError (JHQ_ETIMEDOUT) if a device wait of a search on the
+        caller's stream gave up (jhq_device_status); call after the stream drained."""
+        _check(self._L.jhq_device_status(self._h))
+
+    def list_sizes(self) -> np.ndarray:
+        out = np.zeros(self.params.nlist, np.int64)
+        _check(self._L.jhq_list_sizes(self._h, _ptr(out, C.c_int64)))
+        return out
+
+    def set_alpha(self, alpha: float) -> None:
+        _check(self._L.jhq_set_alpha(self._h, alpha))
+        self.params.alpha = float(alpha)
 
     def set_rerank(self, R: int) -> None:
         """Exact L2 rerank of the best max(R, k) JHQ candidates over the stored

@@ -143,6 +143,21 @@ int jhq_set_nprobe(jhq_index* idx, int nprobe) {
     return guarded([&] { need(idx)->set_nprobe(nprobe); });
 }
 
+int jhq_device_status(jhq_index* idx) {
+    return guarded([&] { need(idx)->check_device_status(); });
+}
+
+int jhq_list_sizes(const jhq_index* idx, int64_t* sizes) {
+    return guarded([&] {
+        if (!sizes) jhq::fail(JHQ_EINVAL, "null output");
+        need(idx)->list_sizes(sizes);
+    });
+}
+
+int jhq_set_alpha(jhq_index* idx, float alpha) {
+    return guarded([&] { need(idx)->set_alpha(alpha); });
+}
+
 int jhq_set_rerank(jhq_index* idx, int R) {
     return guarded([&] { need(idx)->set_rerank(R); });
 }

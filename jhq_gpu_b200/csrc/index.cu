@@ -718,9 +718,11 @@ void Index::set_rerank(int R) {
         if (cap_ > 0) draw_.resize((size_t)cap_ * d_);
     }
     if (R != rerank_) {
+        DeviceGuard g(dev_);
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
         rerank_ = R;
         destroy_graph();
-        ws_.k = 0;                     // re-plan the batch shape
+        ws_.batch_cap = 0;             // workspace and graph are rebuilt
     }
 }
 
@@ -861,6 +863,27 @@ void Index::set_nprobe(int nprobe) {
     p_.nprobe = std::min(nprobe, p_.nlist);
     destroy_graph();
     ws_.batch_cap = 0;                         // workspace and graph are rebuilt
+}
+
+void Index::list_sizes(int64_t* sizes) const {
+    std::fill(sizes, sizes + p_.nlist, (int64_t)0);
+    for (int64_t i = 0; i < ntotal_; ++i) sizes[h_assign_[(size_t)i]]++;
+}
+
+void Index::set_alpha(float alpha) {
+    DeviceGuard g(dev_);
+    if (!(alpha > 0.0f)) fail(JHQ_EINVAL, "alpha must be positive");
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    p_.alpha = alpha;
+    destroy_graph();
+    ws_.batch_cap = 0;
+}
+
+void Index::check_device_status() {
+    DeviceGuard g(dev_);
+    if (coarse_tc_ && coarse_tc_error(true))
+        fail(JHQ_ETIMEDOUT, "a tensor-core coarse wait gave up: the probe lists of that search "
+                            "are not valid");
 }
 
 void Index::synchronize(double timeout_s) {

@@ -52,7 +52,11 @@ public:
     void search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_dists,
                                int32_t* d_ids, cudaStream_t stream);
     void synchronize(double timeout_s);
+    // Raises JHQ_ETIMEDOUT (and clears the flag) when a bounded device wait of a
+    // search enqueued on any stream gave up; call after that stream has drained.
+    void check_device_status();
     void set_nprobe(int nprobe);
+    void set_alpha(float alpha);
     void probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaStream_t stream);
     void search_device_probes(const float* d_q, const int32_t* d_probes, int64_t nq, int k,
                               float* d_dists, int32_t* d_ids, cudaStream_t stream);
@@ -88,6 +92,8 @@ public:
     // rerank off (the reference's JHQ search); the stored vectors stay.
     void set_rerank(int R);
     int rerank() const { return rerank_; }
+    // vectors per IVF list [nlist] (host copy of the assignment; no device work)
+    void list_sizes(int64_t* sizes) const;
     bool keeps_vectors() const { return keep_raw_; }
 
 private:

@@ -474,6 +474,13 @@ scan_kernel(ScanArgs a) {
 // (the bases are multiples of 256 bytes), so a lookup needs no extra add.
 constexpr int QM_WARPS = 8;
 constexpr int QM_GMAX = 8;                  // code groups per page (Mp <= 128)
+#ifndef JHQ_QM_PPS
+#define JHQ_QM_PPS 2
+#endif
+#ifndef JHQ_QM_MINB
+#define JHQ_QM_MINB 2
+#endif
+constexpr int QM_PPS = JHQ_QM_PPS;          // pages scored per warp step
 constexpr int QM_THREADS = QM_WARPS * 32;
 
 __host__ __device__ inline size_t qm_table_bytes(int Mp) { return ((size_t)Mp * 128 + 255) & ~size_t(255); }
@@ -482,7 +489,7 @@ __host__ __device__ inline size_t qm_smem_bytes(int Mp, int ck_pad) {
 }
 
 template <int G_T>
-__global__ void __launch_bounds__(QM_THREADS, 2)
+__global__ void __launch_bounds__(QM_THREADS, JHQ_QM_MINB)
 scan_qmajor_kernel(ScanArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int G = G_T > 0 ? G_T : a.Mp / 16;
@@ -557,8 +564,10 @@ scan_qmajor_kernel(ScanArgs a) {
         }
         // The item's page addresses, 32 at a time, one per lane (a binary search
         // over the query's page prefix, then the list's first page): the
-        // dependent index loads are paid once per 32 pages, in parallel. The
-        // codes of page j+1 are in flight while page j is looked up.
+        // dependent index loads are paid once per 32 pages, in parallel. Pages
+        // are scored QM_PPS at a time with independent accumulators (the chains
+        // of the in-order sums interleave), and the next QM_PPS pages' codes and
+        // slot ids are in flight while the current ones are looked up.
         constexpr int GM = G_T > 0 ? G_T : QM_GMAX;
         for (int b0 = first; b0 < last; b0 += 32) {
             const int npg = min(32, last - b0);
@@ -572,48 +581,67 @@ scan_qmajor_kernel(ScanArgs a) {
                 }
                 mypg = a.list_page_off[pr[plo]] + (lp - po[plo]);
             }
-            auto fetch = [&](int j, int32_t& id, uint4 (&code)[GM]) {
-                const int64_t pg = __shfl_sync(0xffffffffu, mypg, j);
-                id = __ldg(a.slot_ids + pg * 32 + lane);
-                const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
+            auto fetch = [&](int j, int32_t (&id)[QM_PPS], uint4 (&code)[QM_PPS][GM]) {
 #pragma unroll
-                for (int g = 0; g < GM; ++g)
-                    code[g] = g < G ? __ldg(pp + g * 32) : make_uint4(0, 0, 0, 0);
+                for (int u = 0; u < QM_PPS; ++u) {
+                    const int64_t pg = __shfl_sync(0xffffffffu, mypg, (j + u) & 31);
+                    const bool ok = j + u < npg;
+                    id[u] = ok ? __ldg(a.slot_ids + pg * 32 + lane) : -1;
+                    const uint4* pp = reinterpret_cast<const uint4*>(a.pages) + pg * G * 32 + lane;
+#pragma unroll
+                    for (int g = 0; g < GM; ++g)
+                        code[u][g] = (ok && g < G) ? __ldg(pp + g * 32) : make_uint4(0, 0, 0, 0);
+                }
             };
-            int32_t id_c;
-            uint4 code_c[GM];
+            int32_t id_c[QM_PPS];
+            uint4 code_c[QM_PPS][GM];
             fetch(0, id_c, code_c);
-            for (int j = 0; j < npg; ++j) {
-                int32_t id_n = -1;
-                uint4 code_n[GM];
-                if (j + 1 < npg) fetch(j + 1, id_n, code_n);
-                float dist = 0.0f;
+            for (int j = 0; j < npg; j += QM_PPS) {
+                int32_t id_n[QM_PPS];
+                uint4 code_n[QM_PPS][GM];
+                fetch(j + QM_PPS, id_n, code_n);
+                float dist[QM_PPS];
+#pragma unroll
+                for (int u = 0; u < QM_PPS; ++u) dist[u] = 0.0f;
 #pragma unroll
                 for (int g = 0; g < GM; ++g) {
                     if (g >= G) break;
-                    const uint4 cur = code_c[g];
 #pragma unroll
                     for (int wi = 0; wi < 4; ++wi) {
-                        const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
-                        const uint32_t Lo = (w << 2) & 0x3C3C3C3Cu;
-                        const uint32_t Hi = (w >> 2) & 0x3C3C3C3Cu;
+                        uint32_t Lo[QM_PPS], Hi[QM_PPS];
+#pragma unroll
+                        for (int u = 0; u < QM_PPS; ++u) {
+                            const uint4 cur = code_c[u][g];
+                            const uint32_t w = wi == 0 ? cur.x : wi == 1 ? cur.y : wi == 2 ? cur.z : cur.w;
+                            Lo[u] = (w << 2) & 0x3C3C3C3Cu;
+                            Hi[u] = (w >> 2) & 0x3C3C3C3Cu;
+                        }
 #pragma unroll
                         for (int bb = 0; bb < 4; ++bb) {
                             const int b = g * 16 + wi * 4 + bb;           // subspace
-                            // low byte from the nibble offset, upper bytes from the warp base
-                            const uint32_t olo = __byte_perm(Lo, base, 0x7650u | bb);
-                            const uint32_t ohi = __byte_perm(Hi, base, 0x7650u | bb);
-                            const float lo_v = *reinterpret_cast<const float*>(smem + olo + b * 128);
-                            const float hi_v = *reinterpret_cast<const float*>(smem + ohi + b * 128 + 64);
-                            dist = __fadd_rn(dist, __fadd_rn(lo_v, hi_v));
+#pragma unroll
+                            for (int u = 0; u < QM_PPS; ++u) {
+                                // low byte from the nibble offset, upper bytes from the warp base
+                                const uint32_t olo = __byte_perm(Lo[u], base, 0x7650u | bb);
+                                const uint32_t ohi = __byte_perm(Hi[u], base, 0x7650u | bb);
+                                const float lo_v = *reinterpret_cast<const float*>(smem + olo + b * 128);
+                                const float hi_v = *reinterpret_cast<const float*>(smem + ohi + b * 128 + 64);
+                                dist[u] = __fadd_rn(dist[u], __fadd_rn(lo_v, hi_v));
+                            }
                         }
                     }
                 }
-                top.push(id_c >= 0 ? make_key(dist, id_c) : KEY_EMPTY, lane, a.ck, a.ck_pad,
-                         merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
-                id_c = id_n;
 #pragma unroll
-                for (int g = 0; g < GM; ++g) code_c[g] = code_n[g];
+                for (int u = 0; u < QM_PPS; ++u)
+                    if (j + u < npg)                                  // uniform in the warp
+                        top.push(id_c[u] >= 0 ? make_key(dist[u], id_c[u]) : KEY_EMPTY, lane, a.ck,
+                                 a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[q]));
+#pragma unroll
+                for (int u = 0; u < QM_PPS; ++u) {
+                    id_c[u] = id_n[u];
+#pragma unroll
+                    for (int g = 0; g < GM; ++g) code_c[u][g] = code_n[u][g];
+                }
             }
         }
     }

@@ -27,7 +27,7 @@ _i64 = C.c_int64
 def build(ref: bool = False) -> None:
     """Compile the oracle (and, if asked and the reference tree exists, oracle/_ref)."""
     targets = ["oracle"]
-    if ref and os.path.isdir(os.environ.get("REF", "/root/reference")):
+    if ref and os.path.isdir(os.environ.get("JHQ_REFERENCE", "") or "\0"):
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 
@@ -354,3 +354,29 @@ class RefHBlock:
         if rc != 0:
             raise RuntimeError(f"reference hblock {self.version} run failed")
         return I, ms, dict(train_ms=tr.value, add_ms=ad.value)
+
+    def pin_sweep(self, y, q_rot, *, M, c1d, res_c1d, cents, alphas, sigma=1.0, B=8, Br=4,
+                  k=10, nlist=1, nprobe=1, batch=64, reps=5):
+        """Time the reference's search() on the caller's artefacts (identity rotation,
+        already-rotated y / q_rot) for each alpha. Returns (ids [len(alphas)][nq][k],
+        mean search ms per alpha, add ms)."""
+        y, q = _f32(y), _f32(q_rot)
+        n, d = y.shape
+        a = np.ascontiguousarray(alphas, np.float32)
+        I = np.zeros((len(a), len(q), k), np.int32)
+        ms = np.zeros(len(a), np.float64)
+        ad = C.c_double()
+        L = self.L
+        L.ref_gpu_pin_sweep.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        _f32p, C.c_int, _f32p, C.c_int, _f32p, C.c_float,
+                                        _f32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double),
+                                        np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        c1d, res_c1d = _f32(c1d), _f32(res_c1d)
+        cents = _f32(cents) if nlist > 1 else np.zeros((1, d), np.float32)
+        rc = L.ref_gpu_pin_sweep(y, n, q, len(q), d, M, B, Br, k, nlist, nprobe, batch, c1d,
+                                 len(c1d), res_c1d, len(res_c1d), cents, sigma, a, len(a), reps,
+                                 I.reshape(-1), C.byref(ad), ms)
+        if rc != 0:
+            raise RuntimeError(f"reference {self.version} pinned sweep failed")
+        return I, ms, ad.value

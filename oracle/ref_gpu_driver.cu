@@ -6,6 +6,8 @@
 // (examples/demo_jhq_v14_streaming_add.cu:78-106). Built by oracle/Makefile
 // from the reference tree; the product never links it.
 #include <chrono>
+#include <memory>
+#include <stdexcept>
 #include <cstring>
 #include <exception>
 #include <vector>
@@ -113,40 +115,51 @@ static void down(T* dst, const T* src, size_t n) {
 }
 }  // namespace
 
+// Builds the reference index on the caller's artefacts and adds y (see above).
+static std::unique_ptr<jhq_gpu::JHQGpuIndex> pinned_index(
+    const float* y, int n, int d, int M, int B, int Br, float alpha, int nlist, int nprobe,
+    int batch, const float* c1d, int K1D, const float* res_c1d, int Kr, const float* cents,
+    float sigma) {
+    jhq_gpu::JHQGpuIndex::Params p;
+    p.M = M; p.B = B; p.Br = Br; p.alpha = alpha;
+#ifdef REF_HAS_IVF
+    p.nlist = nlist; p.nprobe = nprobe; p.batch_size = batch;
+#else
+    (void)nlist; (void)nprobe; (void)batch; (void)cents;
+#endif
+    auto idx = std::make_unique<jhq_gpu::JHQGpuIndex>(d, p);
+    if (K1D != idx->K1D_ || Kr != idx->Kr_) throw std::invalid_argument("codebook sizes");
+    idx->cb_ = std::make_unique<LloydMaxCodebook>(d, M, B, sigma);
+    std::vector<float> eye((size_t)d * d, 0.0f);
+    for (int i = 0; i < d; ++i) eye[(size_t)i * d + i] = 1.0f;
+    up(&idx->d_Pi_, eye.data(), eye.size());
+    up(&idx->d_c1d_, c1d, (size_t)K1D);
+    idx->res_c1d_.assign(res_c1d, res_c1d + Kr);
+    up(&idx->d_res_c1d_, res_c1d, (size_t)Kr);
+#ifdef REF_HAS_IVF
+    idx->centroids_.assign(cents, cents + (size_t)nlist * d);
+    std::vector<float> norms(nlist);
+    for (int c = 0; c < nlist; ++c) {
+        double s = 0.0;
+        for (int j = 0; j < d; ++j) s += (double)cents[(size_t)c * d + j] * cents[(size_t)c * d + j];
+        norms[c] = (float)s;
+    }
+    up(&idx->d_centroids_, cents, (size_t)nlist * d);
+    up(&idx->d_cent_norms_, norms.data(), (size_t)nlist);
+#endif
+    idx->add(y, n);
+    return idx;
+}
+
 extern "C" int ref_gpu_pin(const float* y, int n, const float* q_rot, int nq, int d, int M,
                            int B, int Br, float alpha, int k, int nlist, int nprobe, int batch,
                            const float* c1d, int K1D, const float* res_c1d, int Kr,
                            const float* cents, float sigma, uint8_t* out_pc, uint8_t* out_rc,
                            float* out_corr, float* out_d, int* out_i) {
     try {
-        jhq_gpu::JHQGpuIndex::Params p;
-        p.M = M; p.B = B; p.Br = Br; p.alpha = alpha;
-#ifdef REF_HAS_IVF
-        p.nlist = nlist; p.nprobe = nprobe; p.batch_size = batch;
-#else
-        (void)nlist; (void)nprobe; (void)batch; (void)cents;
-#endif
-        jhq_gpu::JHQGpuIndex idx(d, p);
-        if (K1D != idx.K1D_ || Kr != idx.Kr_) return 2;
-        idx.cb_ = std::make_unique<LloydMaxCodebook>(d, M, B, sigma);
-        std::vector<float> eye((size_t)d * d, 0.0f);
-        for (int i = 0; i < d; ++i) eye[(size_t)i * d + i] = 1.0f;
-        up(&idx.d_Pi_, eye.data(), eye.size());
-        up(&idx.d_c1d_, c1d, (size_t)K1D);
-        idx.res_c1d_.assign(res_c1d, res_c1d + Kr);
-        up(&idx.d_res_c1d_, res_c1d, (size_t)Kr);
-#ifdef REF_HAS_IVF
-        idx.centroids_.assign(cents, cents + (size_t)nlist * d);
-        std::vector<float> norms(nlist);
-        for (int c = 0; c < nlist; ++c) {
-            double s = 0.0;
-            for (int j = 0; j < d; ++j) s += (double)cents[(size_t)c * d + j] * cents[(size_t)c * d + j];
-            norms[c] = (float)s;
-        }
-        up(&idx.d_centroids_, cents, (size_t)nlist * d);
-        up(&idx.d_cent_norms_, norms.data(), (size_t)nlist);
-#endif
-        idx.add(y, n);
+        auto ip = pinned_index(y, n, d, M, B, Br, alpha, nlist, nprobe, batch, c1d, K1D, res_c1d,
+                               Kr, cents, sigma);
+        jhq_gpu::JHQGpuIndex& idx = *ip;
         const int bpv = idx.bpv_;
 #ifdef REF_HAS_IVF
         std::vector<int> ids(n);
@@ -170,6 +183,38 @@ extern "C" int ref_gpu_pin(const float* y, int n, const float* q_rot, int nq, in
 #endif
         idx.search(q_rot, nq, k, out_d, out_i);
         return cudaDeviceSynchronize() == cudaSuccess ? 0 : 4;
+    } catch (const std::exception&) {
+        return 1;
+    }
+}
+
+// Timing on the caller's artefacts: for each alpha of the sweep (written into
+// the index's private alpha_, which the reference fixes at construction), one
+// warm-up search() and `reps` timed ones with host buffers (the demo's method,
+// examples/demo_jhq_v14_streaming_add.cu:92-99). Ids of sweep point s go to
+// out_i + s*nq*k, the mean search wall time to search_ms[s].
+extern "C" int ref_gpu_pin_sweep(const float* y, int n, const float* q_rot, int nq, int d,
+                                 int M, int B, int Br, int k, int nlist, int nprobe, int batch,
+                                 const float* c1d, int K1D, const float* res_c1d, int Kr,
+                                 const float* cents, float sigma, const float* alphas, int nalpha,
+                                 int reps, int* out_i, double* add_ms, double* search_ms) {
+    using Clock = std::chrono::high_resolution_clock;
+    using Ms = std::chrono::duration<double, std::milli>;
+    try {
+        auto t0 = Clock::now();
+        auto ip = pinned_index(y, n, d, M, B, Br, alphas[0], nlist, nprobe, batch, c1d, K1D,
+                               res_c1d, Kr, cents, sigma);
+        *add_ms = Ms(Clock::now() - t0).count();
+        std::vector<float> dist((size_t)nq * k);
+        for (int s = 0; s < nalpha; ++s) {
+            ip->alpha_ = alphas[s];
+            int* ids = out_i + (size_t)s * nq * k;
+            ip->search(q_rot, nq, k, dist.data(), ids);
+            t0 = Clock::now();
+            for (int r = 0; r < reps; ++r) ip->search(q_rot, nq, k, dist.data(), ids);
+            search_ms[s] = Ms(Clock::now() - t0).count() / reps;
+        }
+        return 0;
     } catch (const std::exception&) {
         return 1;
     }

@@ -146,3 +146,14 @@ def test_coarse_margin_bound_holds(case):
     eps = 6 * 2.0 ** -18 + d * (3 * 2.0 ** -22 + 2.0 ** -23)
     E = (2 * eps * qn * cmax + 2.0 ** -21 * (cmax * cmax + 2 * qn * cmax)) * 1.01
     assert worst <= E, (worst, E)
+
+
+def test_recall_at_k_matches_reference_definition():
+    """datasets.recall_at_k restates examples/demo_jhq_v14_streaming_add.cu:15-27:
+    hits of the returned ids among the first gt_k ground-truth columns / (nq k)."""
+    from jhq_gpu_b200.datasets import recall_at_k
+    labels = np.array([[1, 2, 3], [7, 8, -1]], np.int32)
+    gt = np.array([[3, 1, 9], [8, 0, 5]], np.int32)
+    assert recall_at_k(labels, gt, 3) == 3 / 6          # 1, 3 found; 8 found
+    assert recall_at_k(labels, gt[:, :1], 3) == 2 / 6   # gt_k = 1: only 3 and 8
+    assert recall_at_k(labels[:, :2], gt, 2) == 2 / 4

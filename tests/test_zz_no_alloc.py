@@ -19,23 +19,33 @@ def _index(jhq, d, M, nlist, nprobe, batch, n, seed):
     return idx, rng.standard_normal((150, d), dtype=np.float32)
 
 
+@pytest.mark.parametrize("nq", [150, 20])            # more / fewer queries than one batch
 @pytest.mark.parametrize("d,M,nlist,nprobe,batch", [(128, 32, 1, 1, 64), (64, 16, 16, 4, 50)])
-def test_noalloc_matches_search_device_twice(jhq, d, M, nlist, nprobe, batch):
+def test_noalloc_matches_search_device_twice(jhq, d, M, nlist, nprobe, batch, nq):
+    """Bit-equal to jhq_search_device on two calls in a row, and the device's free
+    memory does not move across the second call (nothing is allocated)."""
     import torch
     idx, q = _index(jhq, d, M, nlist, nprobe, batch, 6000, d + nlist)
-    k, nq = 10, len(q)
+    q = q[:nq]
+    k = 10
     tq = torch.from_numpy(q).cuda()
     ref_d = torch.empty((nq, k), dtype=torch.float32, device="cuda")
     ref_i = torch.empty((nq, k), dtype=torch.int32, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
     idx.search_device(tq.data_ptr(), nq, k, ref_d.data_ptr(), ref_i.data_ptr(), s)
-    for call in range(2):
-        out_d = torch.full((nq, k), -7.0, dtype=torch.float32, device="cuda")
-        out_i = torch.full((nq, k), -7, dtype=torch.int32, device="cuda")
+    outs = [(torch.full((nq, k), -7.0, dtype=torch.float32, device="cuda"),
+             torch.full((nq, k), -7, dtype=torch.int32, device="cuda")) for _ in range(2)]
+    torch.cuda.synchronize()
+    for call, (out_d, out_i) in enumerate(outs):
+        free0 = torch.cuda.mem_get_info()[0]
         idx.search_device_noalloc(tq.data_ptr(), nq, k, out_d.data_ptr(), out_i.data_ptr(), s)
         torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
         assert torch.equal(out_i, ref_i), f"ids differ on call {call}"
         assert torch.equal(out_d, ref_d), f"distances differ on call {call}"
+        if call == 1:                              # after the first call's one-time set-up
+            assert free1 == free0, f"device memory moved by {free0 - free1} bytes"
+    idx.check_device_status()
 
 
 def test_noalloc_rejects_oversized_batch(jhq):
