@@ -909,7 +909,7 @@ def main(argv=None):
                          "c1 = flat 100k x 1024; c2 = IVF 1M nprobe sweep")
     ap.add_argument("--rerank", type=int, default=0,
                     help="exact L2 rerank depth R for c2/c3/c4 (0 = the reference's JHQ search)")
-    ap.add_argument("--c1-rerank", type=int, default=40,
+    ap.add_argument("--c1-rerank", type=int, default=24,
                     help="exact rerank depth of the C1 recall-gate entry")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline legs")
     ap.add_argument("--no-c1", action="store_true", help="skip the C1 block of the N=1 line")

@@ -137,6 +137,16 @@ int jhq_set_alpha(jhq_index* idx, float alpha);
  * JHQ search. Errors: R outside [0, 256] or d % 4 != 0 -> JHQ_EINVAL; enabling
  * it on a non-empty index that keeps no vectors -> JHQ_ESTATE. */
 int jhq_set_rerank(jhq_index* idx, int R);
+
+/* Residual codebooks: per_subspace = 0 keeps the reference's single global
+ * Kr-entry codebook (default); 1 trains M per-subspace codebooks (res_c1d
+ * [M][Kr], dimension j coded against codebook j / Ds) — the ablation the
+ * reference lists as its next step (README.md:66, "M per-subspace codebooks"),
+ * not built there. Choose before jhq_train / jhq_set_trained; afterwards
+ * JHQ_ESTATE. M * 2^Br must be <= 16384 (JHQ_EINVAL). With it, the res_c1d
+ * buffers of jhq_get_trained / jhq_set_trained hold M * Kr floats. */
+int jhq_set_residual_codebooks(jhq_index* idx, int per_subspace);
+int jhq_get_residual_codebooks(const jhq_index* idx, int* per_subspace);
 int jhq_get_rerank(const jhq_index* idx, int* R);
 
 /* Accessors: JHQGpuIndex::ntotal() / dim() (jhq_gpu_index.cuh:44-45). */

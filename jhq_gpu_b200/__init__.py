@@ -36,7 +36,8 @@ EXPORTED = [
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_set_rerank", "jhq_get_rerank",
-    "jhq_set_alpha", "jhq_list_sizes", "jhq_device_status",
+    "jhq_set_alpha", "jhq_list_sizes", "jhq_device_status", "jhq_set_residual_codebooks",
+    "jhq_get_residual_codebooks",
     "jhq_probe_device",
     "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
     "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
@@ -107,6 +108,8 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_set_alpha.argtypes = [vp, C.c_float]
     L.jhq_list_sizes.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_device_status.argtypes = [vp]
+    L.jhq_set_residual_codebooks.argtypes = [vp, C.c_int]
+    L.jhq_get_residual_codebooks.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_get_rerank.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_probe_device.argtypes = [vp, vp, i64, vp, vp]
     L.jhq_search_device_probes.argtypes = [vp, vp, vp, i64, C.c_int, vp, vp, vp]
@@ -281,6 +284,16 @@ class JHQGpuIndex:
         _check(self._L.jhq_set_nprobe(self._h, nprobe))
         self.params.nprobe = min(nprobe, self.params.nlist)
 
+    def set_residual_codebooks(self, per_subspace: bool) -> None:
+        """M per-subspace residual codebooks instead of one (before train)."""
+        _check(self._L.jhq_set_residual_codebooks(self._h, int(bool(per_subspace))))
+
+    @property
+    def residual_per_subspace(self) -> bool:
+        v = C.c_int()
+        _check(self._L.jhq_get_residual_codebooks(self._h, C.byref(v)))
+        return bool(v.value)
+
     def check_device_status(self) -> None:
         """Raises JHQError (JHQ_ETIMEDOUT) if a device wait of a search on the
         caller's stream gave up (jhq_device_status); call after the stream drained."""
@@ -335,7 +348,8 @@ class JHQGpuIndex:
         d, p = self.d, self.params
         Pi = np.empty(d * d, np.float32)
         c1d = np.empty(self.K1D, np.float32)
-        res = np.empty(self.Kr, np.float32)
+        per_sub = self.residual_per_subspace
+        res = np.empty((p.M, self.Kr) if per_sub else self.Kr, np.float32)
         cents = np.empty((p.nlist, d), np.float32)
         sigma = C.c_float()
         _check(self._L.jhq_get_trained(self._h, _ptr(Pi, C.c_float), _ptr(c1d, C.c_float),
@@ -345,7 +359,8 @@ class JHQGpuIndex:
 
     def set_trained(self, Pi, c1d, res_c1d, cents, sigma: float = 1.0) -> None:
         Pi, c1d, res_c1d, cents = _f32(Pi), _f32(c1d), _f32(res_c1d), _f32(cents)
-        if Pi.size != self.d * self.d or c1d.size != self.K1D or res_c1d.size != self.Kr or \
+        nres = self.Kr * (self.params.M if self.residual_per_subspace else 1)
+        if Pi.size != self.d * self.d or c1d.size != self.K1D or res_c1d.size != nres or \
                 cents.size != self.params.nlist * self.d:
             raise ValueError("set_trained: artefact sizes do not match the index")
         _check(self._L.jhq_set_trained(self._h, _ptr(Pi, C.c_float), _ptr(c1d, C.c_float),

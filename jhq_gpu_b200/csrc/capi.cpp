@@ -143,6 +143,17 @@ int jhq_set_nprobe(jhq_index* idx, int nprobe) {
     return guarded([&] { need(idx)->set_nprobe(nprobe); });
 }
 
+int jhq_set_residual_codebooks(jhq_index* idx, int per_subspace) {
+    return guarded([&] { need(idx)->set_residual_codebooks(per_subspace != 0); });
+}
+
+int jhq_get_residual_codebooks(const jhq_index* idx, int* per_subspace) {
+    return guarded([&] {
+        if (!per_subspace) jhq::fail(JHQ_EINVAL, "null output");
+        *per_subspace = need(idx)->residual_per_subspace() ? 1 : 0;
+    });
+}
+
 int jhq_device_status(jhq_index* idx) {
     return guarded([&] { need(idx)->check_device_status(); });
 }

@@ -8,6 +8,7 @@
 //   r_j     = y_j - c1d[bits of code], ri = nearest(res_c1d, r_j)
 //   Br = 4 -> dim j in the low nibble of byte j/2 when j is even (encode.cu:74-78)
 //   corr    = 2 * (in-order fma chain of yhat_j * rhat_j)     (encode.cu:85)
+// With per-subspace residual codebooks, dim j is coded against codebook j / Ds.
 // One thread per row, rows stream from L2; this runs at add() time only.
 #include "jhq_common.h"
 #include "kernels.cuh"
@@ -27,13 +28,13 @@ __device__ __forceinline__ int nearest_sorted(const float* c, int n, float v) {
 
 __global__ void encode_kernel(const float* __restrict__ y, int64_t n, int d, int M, int B, int Br,
                               const float* __restrict__ c1d_g, const float* __restrict__ res_g,
-                              uint8_t* __restrict__ pcodes, uint8_t* __restrict__ rcodes,
-                              int bpv_pad, float* __restrict__ corr) {
+                              int res_per_sub, uint8_t* __restrict__ pcodes,
+                              uint8_t* __restrict__ rcodes, int bpv_pad, float* __restrict__ corr) {
     __shared__ float c1d[256];
     __shared__ float rc1d[256];
     const int Ds = d / M, bpd = B / Ds, K1D = 1 << bpd, kmask = K1D - 1, Kr = 1 << Br;
     for (int i = threadIdx.x; i < K1D; i += blockDim.x) c1d[i] = c1d_g[i];
-    if (res_g)
+    if (res_g && !res_per_sub)
         for (int i = threadIdx.x; i < Kr; i += blockDim.x) rc1d[i] = res_g[i];
     __syncthreads();
     const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -48,18 +49,21 @@ __global__ void encode_kernel(const float* __restrict__ y, int64_t n, int d, int
             code |= (unsigned)nearest_sorted(c1d, K1D, yv[m * Ds + k]) << (k * bpd);
         pcodes[v * M + m] = (uint8_t)code;
         if (rcodes == nullptr) continue;                 // primary codes only (train)
+        // the subspace's own residual codebook (per-subspace mode, read through
+        // L1) or the global one in shared memory
+        const float* rcb = res_per_sub ? res_g + (size_t)m * Kr : rc1d;
         for (int k = 0; k < Ds; ++k) {
             const int j = m * Ds + k;
             const float yh = c1d[(code >> (k * bpd)) & kmask];
             const float r = yv[j] - yh;
-            const int ri = nearest_sorted(rc1d, Kr, r);
+            const int ri = nearest_sorted(rcb, Kr, r);
             if (Br == 4) {
                 if ((j & 1) == 0) cur = (unsigned)ri;
                 else { rc[j >> 1] = (uint8_t)(cur | ((unsigned)ri << 4)); cur = 0; }
             } else {
                 rc[j] = (uint8_t)ri;
             }
-            dot = __fmaf_rn(yh, rc1d[ri], dot);
+            dot = __fmaf_rn(yh, rcb[ri], dot);
         }
     }
     if (rcodes == nullptr) return;
@@ -106,11 +110,12 @@ void set_int(int* dst, int value, cudaStream_t s) {
 }
 
 void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
-                 const float* c1d, const float* res_c1d, uint8_t* pcodes,
+                 const float* c1d, const float* res_c1d, bool res_per_sub, uint8_t* pcodes,
                  uint8_t* rcodes, int bpv_pad, float* corr, cudaStream_t s) {
     if (n <= 0) return;
     encode_kernel<<<(unsigned)ceil_div(n, 128), 128, 0, s>>>(y, n, d, M, B, Br, c1d, res_c1d,
-                                                             pcodes, rcodes, bpv_pad, corr);
+                                                             res_per_sub ? 1 : 0, pcodes, rcodes,
+                                                             bpv_pad, corr);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -123,7 +123,7 @@ void Index::upload_trained() {
     h2d(dPi_.get(), Pi_.data(), Pi_.size(), stream_);
     dc1d_.resize(K1D_);
     h2d(dc1d_.get(), c1d_.data(), c1d_.size(), stream_);
-    dres_.resize(Kr_);
+    dres_.resize((size_t)residual_floats());
     if (!res_c1d_.empty()) h2d(dres_.get(), res_c1d_.data(), res_c1d_.size(), stream_);
     // centroids as the row-major [d][nlist] right operand, plus |c|^2 in double
     // (jhq_gpu_index.cu:243-249)
@@ -168,41 +168,69 @@ void Index::upload_trained() {
 // assign (on the device, through `assign`, which returns the device
 // assignment) + mean update in double, an empty cluster reseeded from the
 // row LCG(c, iter) (jhq_gpu_index.cu:228-299).
-void Index::lloyd(const std::vector<float>& y, int64_t n, int nl, int iters,
-                  std::vector<float>& cents,
+// Lloyd k-means in the rotated space (jhq_gpu_index.cu:228-299): init rows
+// floor(c n / nl), `assign` gives the device assignment for the current
+// centroids, mean update with index-order double sums, empty lists reseeded from
+// row (c * 1103515245 + iter * 12345) % n. The update runs on the device
+// (train_gpu.cu, bit-identical); JHQ_TRAIN_HOST=1 runs it on the host instead.
+void Index::lloyd(const float* d_y, int64_t n, int nl, int iters, std::vector<float>& cents,
                   const std::function<const int32_t*(const std::vector<float>&)>& assign) {
     cents.assign((size_t)nl * d_, 0.0f);
+    DevBuf<float> dc((size_t)nl * d_);
     for (int c = 0; c < nl; ++c) {
         const int64_t src = (int64_t)c * n / nl;
-        std::memcpy(&cents[(size_t)c * d_], &y[(size_t)src * d_], sizeof(float) * d_);
+        JHQ_CUDA(cudaMemcpyAsync(dc.get() + (size_t)c * d_, d_y + (size_t)src * d_, 4 * (size_t)d_,
+                                 cudaMemcpyDeviceToDevice, stream_));
     }
-    std::vector<int32_t> as((size_t)n);
-    std::vector<double> sums((size_t)nl * d_);
-    std::vector<int> counts(nl);
+    d2h(cents.data(), dc.get(), cents.size(), stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    const char* th = std::getenv("JHQ_TRAIN_HOST");
+    if (th && std::string(th) == "1") {                 // host update (train_cpu order)
+        std::vector<float> y((size_t)n * d_);
+        d2h(y.data(), d_y, y.size(), stream_);
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
+        std::vector<int32_t> as((size_t)n);
+        std::vector<double> sums((size_t)nl * d_);
+        std::vector<int> counts(nl);
+        for (int iter = 0; iter < iters; ++iter) {
+            const int32_t* da = assign(cents);
+            d2h(as.data(), da, as.size(), stream_);
+            JHQ_CUDA(cudaStreamSynchronize(stream_));
+            std::fill(sums.begin(), sums.end(), 0.0);
+            std::fill(counts.begin(), counts.end(), 0);
+            for (int64_t i = 0; i < n; ++i) {
+                const int c = as[i];
+                counts[c]++;
+                double* sc = &sums[(size_t)c * d_];
+                const float* yi = &y[(size_t)i * d_];
+                for (int j = 0; j < d_; ++j) sc[j] += yi[j];
+            }
+            for (int c = 0; c < nl; ++c) {
+                float* cc = &cents[(size_t)c * d_];
+                if (counts[c] == 0) {
+                    const int64_t src = ((int64_t)c * 1103515245 + (int64_t)(iter * 12345)) % n;
+                    std::memcpy(cc, &y[(size_t)src * d_], sizeof(float) * d_);
+                    continue;
+                }
+                const double inv = 1.0 / (double)counts[c];
+                const double* sc = &sums[(size_t)c * d_];
+                for (int j = 0; j < d_; ++j) cc[j] = (float)(sc[j] * inv);
+            }
+        }
+        return;
+    }
+    std::vector<int64_t> counts;
     for (int iter = 0; iter < iters; ++iter) {
         const int32_t* da = assign(cents);
-        d2h(as.data(), da, as.size(), stream_);
-        JHQ_CUDA(cudaStreamSynchronize(stream_));
-        std::fill(sums.begin(), sums.end(), 0.0);
-        std::fill(counts.begin(), counts.end(), 0);
-        for (int64_t i = 0; i < n; ++i) {
-            const int c = as[i];
-            counts[c]++;
-            double* sc = &sums[(size_t)c * d_];
-            const float* yi = &y[(size_t)i * d_];
-            for (int j = 0; j < d_; ++j) sc[j] += yi[j];
-        }
-        for (int c = 0; c < nl; ++c) {
-            float* cc = &cents[(size_t)c * d_];
+        lloyd_update_device(d_y, n, d_, nl, da, dc.get(), counts, stream_);
+        for (int c = 0; c < nl; ++c)
             if (counts[c] == 0) {
                 const int64_t src = ((int64_t)c * 1103515245 + (int64_t)(iter * 12345)) % n;
-                std::memcpy(cc, &y[(size_t)src * d_], sizeof(float) * d_);
-                continue;
+                JHQ_CUDA(cudaMemcpyAsync(dc.get() + (size_t)c * d_, d_y + (size_t)src * d_,
+                                         4 * (size_t)d_, cudaMemcpyDeviceToDevice, stream_));
             }
-            const double inv = 1.0 / (double)counts[c];
-            const double* sc = &sums[(size_t)c * d_];
-            for (int j = 0; j < d_; ++j) cc[j] = (float)(sc[j] * inv);
-        }
+        d2h(cents.data(), dc.get(), cents.size(), stream_);
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
     }
 }
 
@@ -261,19 +289,15 @@ void Index::train(const float* h_x, int64_t n) {
         h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
         rotate_device(dx.get(), nr, dy.get() + r0 * d_, stream_);
     }
-    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), nullptr, dcodes.get(), nullptr,
+    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), nullptr, false, dcodes.get(), nullptr,
                 bpv_pad_, nullptr, stream_);
-    std::vector<float> y((size_t)n * d_);
-    std::vector<uint8_t> codes((size_t)n * M_);
-    d2h(y.data(), dy.get(), y.size(), stream_);
-    d2h(codes.data(), dcodes.get(), codes.size(), stream_);
     JHQ_CUDA(cudaStreamSynchronize(stream_));
     dx.release();
 
     // IVF centroids: Lloyd k-means in the rotated space (jhq_gpu_index.cu:228-299)
     {
         DevBuf<int32_t> dassign((size_t)n);
-        lloyd(y, n, p_.nlist, p_.ivf_iters, cents_, [&](const std::vector<float>&) {
+        lloyd(dy.get(), n, p_.nlist, p_.ivf_iters, cents_, [&](const std::vector<float>&) {
             upload_trained();
             assign_device(dy.get(), n, dassign.get(), stream_);
             return dassign.get();
@@ -288,7 +312,7 @@ void Index::train(const float* h_x, int64_t n) {
         const int P = std::max(2, std::min<int>(pl ? std::atoi(pl) : PILOT_LISTS,
                                                 (int)(n / PILOT_MIN_MEMBERS)));
         DevBuf<int32_t> dassign((size_t)n);
-        lloyd(y, n, P, 6, pilot_cents_, [&](const std::vector<float>& c) {
+        lloyd(dy.get(), n, P, 6, pilot_cents_, [&](const std::vector<float>& c) {
             upload_pilot(c, P);
             gemm_argmin(dy.get(), dpilot_centsT_.get(), dpilot_norms_.get(), n, d_, P,
                         dassign.get(), stream_);
@@ -297,19 +321,40 @@ void Index::train(const float* h_x, int64_t n) {
         pilotP_ = P;
         upload_pilot(pilot_cents_, P);
     }
-    dy.release();
 
-    // residual codebook: 1-D k-means of y - yhat (jhq_gpu_index.cu:302-330)
-    {
-        std::vector<float> yhat((size_t)d_);
-        for (int64_t i = 0; i < n; ++i) {
-            train::reconstruct(&codes[(size_t)i * M_], 1, d_, M_, B_, c1d_.data(), yhat.data());
-            float* yi = &y[(size_t)i * d_];
-            for (int j = 0; j < d_; ++j) yi[j] = yi[j] - yhat[j];
+    // residual codebook: 1-D k-means of y - yhat (jhq_gpu_index.cu:302-330), on
+    // the device (train_gpu.cu) or, with JHQ_TRAIN_HOST=1, on the host. Per
+    // subspace: one k-means per subspace m over its residuals in (row, dim) order.
+    residuals_device(dy.get(), dcodes.get(), n, d_, M_, B_, dc1d_.get(), stream_);
+    const char* th = std::getenv("JHQ_TRAIN_HOST");
+    const bool host = th && std::string(th) == "1";
+    auto fit = [&](const float* dv, int64_t cnt) {
+        std::vector<float> c;
+        if (host) {
+            std::vector<float> r((size_t)cnt);
+            d2h(r.data(), dv, r.size(), stream_);
+            JHQ_CUDA(cudaStreamSynchronize(stream_));
+            c = train::kmeans_1d(r.data(), cnt, Kr_);
+        } else {
+            c = kmeans_1d_device(dv, cnt, Kr_, 25, stream_);
         }
-        res_c1d_ = train::kmeans_1d(y.data(), (int64_t)y.size(), Kr_);
-        res_c1d_.resize(Kr_, res_c1d_.empty() ? 0.0f : res_c1d_.back());
+        c.resize(Kr_, c.empty() ? 0.0f : c.back());
+        return c;
+    };
+    if (!res_per_sub_) {
+        res_c1d_ = fit(dy.get(), n * d_);
+    } else {
+        DevBuf<float> seg((size_t)n * Ds_);
+        res_c1d_.clear();
+        for (int m = 0; m < M_; ++m) {
+            JHQ_CUDA(cudaMemcpy2DAsync(seg.get(), (size_t)Ds_ * 4, dy.get() + (size_t)m * Ds_,
+                                       (size_t)d_ * 4, (size_t)Ds_ * 4, (size_t)n,
+                                       cudaMemcpyDeviceToDevice, stream_));
+            const std::vector<float> c = fit(seg.get(), n * Ds_);
+            res_c1d_.insert(res_c1d_.end(), c.begin(), c.end());
+        }
     }
+    dy.release();
     upload_trained();
     trained_ = true;
     layout_dirty_ = true;
@@ -324,7 +369,7 @@ void Index::set_trained(const float* Pi, const float* c1d, const float* res_c1d,
     pilot_cents_.clear();
     Pi_.assign(Pi, Pi + (size_t)d_ * d_);
     c1d_.assign(c1d, c1d + K1D_);
-    res_c1d_.assign(res_c1d, res_c1d + Kr_);
+    res_c1d_.assign(res_c1d, res_c1d + residual_floats());
     cents_.assign(cents, cents + (size_t)p_.nlist * d_);
     sigma_ = sigma;
     upload_trained();
@@ -396,7 +441,7 @@ void Index::add(const float* h_x, int64_t n) {
                         dpa.get(), stream_);
             d2h(h_pilot_assign_.data() + at, dpa.get(), (size_t)nr, stream_);
         }
-        encode_rows(dy.get(), nr, d_, M_, B_, Br_, dc1d_.get(), dres_.get(),
+        encode_rows(dy.get(), nr, d_, M_, B_, Br_, dc1d_.get(), dres_.get(), res_per_sub_,
                     dpcodes_.get() + at * M_, drcodes_.get() + at * bpv_pad_, bpv_pad_,
                     dcorr_.get() + at, stream_);
     }
@@ -658,6 +703,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
     mark(4);
     RefineArgs ra;
     ra.q_rot = b.q_rot; ra.res_c1d = dres_.get(); ra.cand = b.cand;
+    ra.res_per_sub = res_per_sub_ ? 1 : 0; ra.M = M_;
     ra.qslot_off = b.plan.qslot_off; ra.gthr = b.plan.gthr; ra.rcodes = drcodes_.get();
     ra.corr = dcorr_.get(); ra.out_dists = out_d; ra.out_ids = out_i;
     ra.nq = nq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = sh.ck;
@@ -705,6 +751,14 @@ void Index::run_batch(cudaStream_t s, int nvalid) {
         stage_ms_[i] += ms;
     }
     ++stage_batches_;
+}
+
+void Index::set_residual_codebooks(bool per_subspace) {
+    if (per_subspace == res_per_sub_) return;
+    if (trained_) fail(JHQ_ESTATE, "residual codebooks: choose them before train()/set_trained()");
+    if (per_subspace && (size_t)M_ * Kr_ > 16384)
+        fail(JHQ_EINVAL, "per-subspace residual codebooks: M * 2^Br must be <= 16384");
+    res_per_sub_ = per_subspace;
 }
 
 void Index::set_rerank(int R) {
@@ -936,7 +990,7 @@ void Index::encode(const float* h_y, int64_t n, uint8_t* primary, uint8_t* resid
     DevBuf<uint8_t> pc((size_t)n * M_), rc((size_t)n * bpv_pad_);
     DevBuf<float> co((size_t)n);
     h2d(dy.get(), h_y, (size_t)n * d_, stream_);
-    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), dres_.get(), pc.get(), rc.get(),
+    encode_rows(dy.get(), n, d_, M_, B_, Br_, dc1d_.get(), dres_.get(), res_per_sub_, pc.get(), rc.get(),
                 bpv_pad_, co.get(), stream_);
     JHQ_CUDA(cudaStreamSynchronize(stream_));
     if (primary) JHQ_CUDA(cudaMemcpy(primary, pc.get(), (size_t)n * M_, cudaMemcpyDeviceToHost));
@@ -962,7 +1016,8 @@ void Index::save(const std::string& path) const {
     put(&FORMAT_VERSION, 4);
     int32_t hdr[12] = {d_, p_.M, p_.B, p_.Br, p_.nlist, p_.nprobe, p_.ivf_iters,
                        p_.batch_size, p_.seed, p_.add_batch, pilotP_,
-                       (keep_raw_ ? 1 : 0) | (rerank_ << 8)};   // flags: kept vectors, rerank R
+                       (keep_raw_ ? 1 : 0) | (res_per_sub_ ? 2 : 0) | (rerank_ << 8)};
+                       // flags: kept vectors, per-subspace residual codebooks, rerank R
     put(hdr, sizeof hdr);
     put(&p_.alpha, 4);
     put(&sigma_, 4);
@@ -1018,7 +1073,10 @@ Index* Index::load(const std::string& path, int device) {
     Index* idx = new Index(hdr[0], p);
     try {
         const int d = idx->d_;
-        std::vector<float> Pi((size_t)d * d), c1d(idx->K1D_), res(idx->Kr_), cents((size_t)p.nlist * d);
+        idx->res_per_sub_ = (hdr[11] & 2) != 0;
+        if (idx->res_per_sub_ && (size_t)idx->M_ * idx->Kr_ > 16384) fail(JHQ_EIO, "load: bad flags");
+        std::vector<float> Pi((size_t)d * d), c1d(idx->K1D_), res((size_t)idx->residual_floats()),
+            cents((size_t)p.nlist * d);
         get(Pi.data(), Pi.size() * 4);
         get(c1d.data(), c1d.size() * 4);
         get(res.data(), res.size() * 4);

@@ -91,6 +91,12 @@ public:
     // candidates and returns the k nearest of them by exact L2. R = 0 turns the
     // rerank off (the reference's JHQ search); the stored vectors stay.
     void set_rerank(int R);
+    // Residual codebooks: one global Kr-entry codebook (the reference's format,
+    // default) or M per-subspace codebooks, res_c1d [M][Kr] (dim j uses codebook
+    // j / Ds). Chosen before train() / set_trained(); fixed afterwards.
+    void set_residual_codebooks(bool per_subspace);
+    bool residual_per_subspace() const { return res_per_sub_; }
+    int residual_floats() const { return res_per_sub_ ? M_ * Kr_ : Kr_; }
     int rerank() const { return rerank_; }
     // vectors per IVF list [nlist] (host copy of the assignment; no device work)
     void list_sizes(int64_t* sizes) const;
@@ -119,7 +125,7 @@ private:
     };
 
     void upload_trained();
-    void lloyd(const std::vector<float>& y, int64_t n, int nl, int iters, std::vector<float>& cents,
+    void lloyd(const float* d_y, int64_t n, int nl, int iters, std::vector<float>& cents,
                const std::function<const int32_t*(const std::vector<float>&)>& assign);
     void upload_pilot(const std::vector<float>& c, int P);
     void rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const;
@@ -191,6 +197,7 @@ private:
     bool coarse_tc_ = false;
     DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
     DevBuf<float> dcorr_;
+    bool res_per_sub_ = false;         // M per-subspace residual codebooks
     bool keep_raw_ = false;            // stored vectors for the exact rerank
     int rerank_ = 0;
     DevBuf<float> draw_;               // [cap][d] vectors as given (keep_raw_)

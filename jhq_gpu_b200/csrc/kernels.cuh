@@ -6,6 +6,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <vector>
 
 namespace jhq {
 
@@ -28,7 +29,7 @@ void gemm_argmin(const float* A, const float* B, const float* norms, int64_t R, 
 // Primary + residual codes and corr of rotated rows y [n][d]
 // (encode.cu:20-86 of the reference). res rows are bpv_pad bytes apart.
 void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
-                 const float* c1d, const float* res_c1d, uint8_t* pcodes,
+                 const float* c1d, const float* res_c1d, bool res_per_sub, uint8_t* pcodes,
                  uint8_t* rcodes, int bpv_pad, float* corr, cudaStream_t s);
 // dst[0] = value (stream-ordered scalar upload, no host buffer involved).
 void set_int(int* dst, int value, cudaStream_t s);
@@ -163,6 +164,8 @@ struct RefineArgs {
     const float* raw = nullptr;     // [N][d] stored vectors, nullptr = no rerank
     int nq, d, Br, bpv_pad, ck, ck_pad, k;
     int kr = 0;                     // candidates re-scored (k <= kr <= ck)
+    int res_per_sub = 0;            // res_c1d is [M][Kr] (dim j: codebook j / (d / M))
+    int M = 1;
 };
 void refine_topk(const RefineArgs& a, cudaStream_t st);
 void refine_configure();
@@ -173,5 +176,18 @@ void remap_ids(int32_t* ids, int64_t n, int mul, int add, cudaStream_t st);
 // k-way merge of per-shard top-k lists (jhq_merge_shards).
 void merge_shard_lists(const float* in_d, const int32_t* in_i, int nshards, int64_t nq,
                        int k, float* out_d, int32_t* out_i, cudaStream_t st);
+
+// ---- training on the device (train_gpu.cu), bit-identical to train_cpu.cpp ----
+// y <- y - c1d[bits of the primary code], in place ([n][d])
+void residuals_device(float* d_y, const uint8_t* d_codes, int64_t n, int d, int M, int B,
+                      const float* d_c1d, cudaStream_t s);
+// 1-D k-means of n device values (train::kmeans_1d on the device)
+std::vector<float> kmeans_1d_device(const float* d_vals, int64_t n, int Kr, int max_iter,
+                                    cudaStream_t s);
+// one Lloyd mean update: d_cents [nl][d] <- means of the rows of d_y assigned to
+// each list (index-order double sums); lists with no rows keep their value and
+// are reported with count 0
+void lloyd_update_device(const float* d_y, int64_t n, int d, int nl, const int32_t* d_assign,
+                         float* d_cents, std::vector<int64_t>& counts, cudaStream_t s);
 
 }  // namespace jhq

@@ -41,15 +41,16 @@ refine_kernel(RefineArgs a) {
     // q_rot padded by one float per 32: lane l reads dims 32l.. of its chunk,
     // and the padding puts the 32 lanes in 32 different banks.
     float* qs = reinterpret_cast<float*>(buf + RF_CAP + 2);        // d + d/32 + 1
-    float* rc1d = qs + a.d + a.d / 32 + 1;                         // 256
-    float* qraw = qs + ((a.d + a.d / 32 + 1 + 256 + 3) & ~3);      // d (rerank only), 16-byte aligned
+    float* rc1d = qs + a.d + a.d / 32 + 1;                         // nres (Kr, or M*Kr)
+    const int Kr = 1 << a.Br;
+    const int nres = a.res_per_sub ? a.M * Kr : Kr;
+    float* qraw = qs + ((a.d + a.d / 32 + 1 + nres + 3) & ~3);     // d (rerank only), 16-byte aligned
 
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (q >= a.nq) return;
-    const int Kr = 1 << a.Br;
     for (int i = tid; i < a.ck_pad; i += RF_THREADS) top[i] = KEY_EMPTY;
     for (int i = tid; i < a.d; i += RF_THREADS) qs[i + (i >> 5)] = a.q_rot[(int64_t)q * a.d + i];
-    for (int i = tid; i < Kr; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
+    for (int i = tid; i < nres; i += RF_THREADS) rc1d[i] = a.res_c1d[i];
     if (a.raw)
         for (int i = tid; i < a.d; i += RF_THREADS) qraw[i] = a.q_raw[(int64_t)q * a.d + i];
     __syncthreads();
@@ -92,6 +93,7 @@ refine_kernel(RefineArgs a) {
 
     // residual refine, warp per candidate
     const int chunks = a.bpv_pad / 16, dpw = 32 / a.Br, mask = Kr - 1;
+    const int Ds = a.d / a.M;
     for (int i = warp; i < a.ck_pad; i += RF_WARPS) {
         const uint64_t key = (i < a.ck) ? top[i] : KEY_EMPTY;
         if (key == KEY_EMPTY) {
@@ -109,7 +111,8 @@ refine_kernel(RefineArgs a) {
                 for (int t = 0; t < dpw; ++t) {
                     const int j = (c * 4 + w) * dpw + t;
                     if (j >= a.d) break;
-                    const float diff = qs[j + (j >> 5)] - rc1d[(wv[w] >> (t * a.Br)) & mask];
+                    const int cb = a.res_per_sub ? (j / Ds) * Kr : 0;
+                    const float diff = qs[j + (j >> 5)] - rc1d[cb + ((wv[w] >> (t * a.Br)) & mask)];
                     acc = __fmaf_rn(diff, diff, acc);
                 }
             }
@@ -192,7 +195,8 @@ merge_shards_kernel(const float* __restrict__ in_d, const int32_t* __restrict__ 
 
 void refine_topk(const RefineArgs& a, cudaStream_t st) {
     if (a.nq <= 0) return;
-    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + 256) * 4 +
+    const int nres = a.res_per_sub ? a.M * (1 << a.Br) : (1 << a.Br);
+    size_t smem = (size_t)a.ck_pad * 3 * 8 + (size_t)(a.d + a.d / 32 + 1 + nres + 3) * 4 +
                   (size_t)RF_CAP * 8 + 16 + (a.raw ? (size_t)a.d * 4 + 16 : 0);
     refine_kernel<<<a.nq, RF_THREADS, smem, st>>>(a);
     JHQ_LAUNCH_CHECK();

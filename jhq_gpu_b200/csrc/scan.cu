@@ -68,11 +68,8 @@ constexpr size_t SCAN_SMEM_LIMIT = 227 * 1024 - 1024;   // dynamic bytes left af
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
-__host__ __device__ inline int merge_n_of(int ck_pad) {
-    int n = 1;
-    while (n < ck_pad + 64) n <<= 1;
-    return n;
-}
+// keys of one warp top-ck region: two list halves and the append buffer (WarpTop)
+__host__ __device__ inline int merge_n_of(int ck_pad) { return 2 * ck_pad + 64; }
 
 // MODE: 0 = byte LUT (one query), 1/2/4 = nibble tables for 1/2/4 queries.
 __host__ __device__ constexpr int qg_of(int mode) { return mode == 0 ? 1 : mode; }
@@ -198,15 +195,69 @@ namespace {   // pushes, inserts, flushes, runs, units
 #define SCAN_STAT(i, v) ((void)0)
 #endif
 
-// Per-warp exact top-ck of one query: s[0..ck_pad) sorted list,
-// s[ck_pad..merge_n) append buffer. thr = pruning bound (uniform in the warp).
+// Per-warp exact top-ck of one query. Region (merge_n_of(ck_pad) keys):
+// two list halves of ck_pad keys (the current sorted list and the target of
+// the next merge) and a 64-key append buffer. thr = pruning bound (uniform in
+// the warp). A flush sorts the buffer in registers (two keys per lane, bitonic
+// network over shuffles), then merges it into the list by rank: list key i
+// goes to i + #(buffer keys below it), buffer key e to e + #(list keys below
+// it) — keys are unique (distance, id) pairs, so the ranks are a permutation;
+// positions >= ck_pad drop out. Cost ~ (log 64 + log ck_pad) shared loads per
+// key instead of a bitonic sort of list + buffer.
+constexpr int TOP_BUF = 64;
+
+__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
+    const unsigned hi = __shfl_xor_sync(0xffffffffu, (unsigned)(v >> 32), m);
+    const unsigned lo = __shfl_xor_sync(0xffffffffu, (unsigned)v, m);
+    return ((uint64_t)hi << 32) | lo;
+}
+
+// Ascending sort of 64 keys held two per lane (element 2*lane + r in x_r).
+__device__ __forceinline__ void warp_sort64(uint64_t& x0, uint64_t& x1, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 64; k <<= 1) {
+        const bool up = ((2 * lane) & k) == 0;
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j == 1) {
+                const uint64_t lo = x0 < x1 ? x0 : x1, hi = x0 < x1 ? x1 : x0;
+                x0 = up ? lo : hi;
+                x1 = up ? hi : lo;
+            } else {
+                const int m = j >> 1;
+                const uint64_t p0 = shfl_xor64(x0, m), p1 = shfl_xor64(x1, m);
+                const bool keep_min = ((lane & m) == 0) == up;
+                x0 = keep_min ? (p0 < x0 ? p0 : x0) : (p0 > x0 ? p0 : x0);
+                x1 = keep_min ? (p1 < x1 ? p1 : x1) : (p1 > x1 ? p1 : x1);
+            }
+        }
+    }
+}
+
+// number of keys in sorted a[0..n) strictly below v (n a power of two)
+__device__ __forceinline__ int rank_below(const uint64_t* a, int n, uint64_t v) {
+    int lo = 0;
+    for (int step = n >> 1; step > 0; step >>= 1)
+        if (a[lo + step - 1] < v) lo += step;
+    return lo + (a[lo] < v ? 1 : 0);
+}
+
 struct WarpTop {
-    uint64_t* s;
+    uint64_t* base;    // region start
+    uint64_t* s;       // current sorted list [ck_pad]
+    uint64_t* alt;     // merge target [ck_pad]
+    uint64_t* buf;     // append buffer [TOP_BUF]
     uint64_t thr;
     int count;
 
+    __device__ __forceinline__ void init(uint64_t* region, int ck_pad) {
+        base = region;
+        s = region;
+        alt = region + ck_pad;
+        buf = region + 2 * ck_pad;
+    }
     __device__ __forceinline__ void reset(int lane, int merge_n, uint64_t bound) {
-        for (int i = lane; i < merge_n; i += 32) s[i] = KEY_EMPTY;
+        for (int i = lane; i < merge_n; i += 32) base[i] = KEY_EMPTY;
         thr = bound;
         count = 0;
         __syncwarp();
@@ -215,23 +266,38 @@ struct WarpTop {
     // bound and pick up the tightest bound.
     __device__ __forceinline__ void flush(int lane, int ck, int ck_pad, int merge_n, uint64_t* tau,
                                           uint64_t* gbound = nullptr) {
-        const int cap = merge_n - ck_pad;
+        (void)merge_n;
         if (lane == 0) SCAN_STAT(2, 1);
-        for (int i = count + lane; i < cap; i += 32) s[ck_pad + i] = KEY_EMPTY;
+        uint64_t b0 = lane < count ? buf[lane] : KEY_EMPTY;
+        uint64_t b1 = lane + 32 < count ? buf[lane + 32] : KEY_EMPTY;
+        warp_sort64(b0, b1, lane);
         __syncwarp();
-        warp_bitonic_sort(s, merge_n, lane);
+        buf[2 * lane] = b0;
+        buf[2 * lane + 1] = b1;
+        __syncwarp();
+        for (int i = lane; i < ck_pad; i += 32) {
+            const uint64_t v = s[i];
+            const int pos = i + rank_below(buf, TOP_BUF, v);
+            if (pos < ck_pad) alt[pos] = v;
+        }
+        const int p0 = 2 * lane + rank_below(s, ck_pad, b0);
+        const int p1 = 2 * lane + 1 + rank_below(s, ck_pad, b1);
+        if (p0 < ck_pad) alt[p0] = b0;
+        if (p1 < ck_pad) alt[p1] = b1;
+        __syncwarp();
+        uint64_t* t = s; s = alt; alt = t;
         const uint64_t kth = s[ck - 1];
         if (lane == 0 && kth != KEY_EMPTY) {
             atomicMin(reinterpret_cast<unsigned long long*>(tau), (unsigned long long)kth);
             if (gbound) atomicMin(reinterpret_cast<unsigned long long*>(gbound), (unsigned long long)kth);
         }
         __syncwarp();
-        uint64_t t = *reinterpret_cast<volatile uint64_t*>(tau);
+        uint64_t tb = *reinterpret_cast<volatile uint64_t*>(tau);
         if (gbound) {
             const uint64_t g = *reinterpret_cast<volatile uint64_t*>(gbound);
-            t = g < t ? g : t;
+            tb = g < tb ? g : tb;
         }
-        thr = kth < t ? kth : t;
+        thr = kth < tb ? kth : tb;
         count = 0;
     }
     __device__ __forceinline__ void push(uint64_t key, int lane, int ck, int ck_pad, int merge_n,
@@ -240,13 +306,13 @@ struct WarpTop {
         unsigned mask = __ballot_sync(0xffffffffu, take);
         if (lane == 0) { SCAN_STAT(0, 32); SCAN_STAT(1, __popc(mask)); }
         if (mask == 0) return;
-        if (count + __popc(mask) > merge_n - ck_pad) {
+        if (count + __popc(mask) > TOP_BUF) {
             flush(lane, ck, ck_pad, merge_n, tau, gbound);
             take = key < thr;
             mask = __ballot_sync(0xffffffffu, take);
             if (mask == 0) return;
         }
-        if (take) s[ck_pad + count + __popc(mask & ((1u << lane) - 1u))] = key;
+        if (take) buf[count + __popc(mask & ((1u << lane) - 1u))] = key;
         count += __popc(mask);
         __syncwarp();
     }
@@ -301,7 +367,7 @@ scan_kernel(ScanArgs a) {
     }
     WarpTop top[QG];
 #pragma unroll
-    for (int j = 0; j < QG; ++j) top[j].s = wl + ((size_t)warp * QG + j) * merge_n;
+    for (int j = 0; j < QG; ++j) top[j].init(wl + ((size_t)warp * QG + j) * merge_n, a.ck_pad);
 
     // A run = consecutive units of this CTA with the same list and query group
     // (chunks of one list). The warps' top-ck lists live across the whole run;
@@ -475,7 +541,7 @@ scan_kernel(ScanArgs a) {
 constexpr int QM_WARPS = 8;
 constexpr int QM_GMAX = 8;                  // code groups per page (Mp <= 128)
 #ifndef JHQ_QM_PPS
-#define JHQ_QM_PPS 2
+#define JHQ_QM_PPS 1
 #endif
 #ifndef JHQ_QM_MINB
 #define JHQ_QM_MINB 2
@@ -516,7 +582,7 @@ scan_qmajor_kernel(ScanArgs a) {
     int cur_q = -1;
     int64_t run_slot = -1;
     WarpTop top;
-    top.s = wl;
+    top.init(wl, a.ck_pad);
     auto close_run = [&]() {
         top.flush(lane, a.ck, a.ck_pad, merge_n, reinterpret_cast<uint64_t*>(&a.gthr[cur_q]));
         uint64_t* out = a.cand + run_slot * a.ck;

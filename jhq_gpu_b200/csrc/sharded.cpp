@@ -90,11 +90,13 @@ ShardedIndex::~ShardedIndex() {
 
 void ShardedIndex::sync_artefacts() {
     Index& s0 = *sh_[0];
-    std::vector<float> Pi((size_t)d_ * d_), c1d(s0.K1D()), res(s0.Kr()), cents((size_t)p_.nlist * d_);
+    std::vector<float> Pi((size_t)d_ * d_), c1d(s0.K1D()), res((size_t)s0.residual_floats()),
+        cents((size_t)p_.nlist * d_);
     float sigma = 0.0f;
     s0.get_trained(Pi.data(), c1d.data(), res.data(), cents.data(), &sigma);
     const std::vector<float>& pc = s0.pilot_centroids();
     for_each_shard(nshards() - 1, [&](int s) {
+        sh_[s + 1]->set_residual_codebooks(s0.residual_per_subspace());
         sh_[s + 1]->set_trained(Pi.data(), c1d.data(), res.data(), cents.data(), sigma);
         if (s0.pilot_lists() > 0) sh_[s + 1]->set_pilot(pc.data(), s0.pilot_lists());
     });

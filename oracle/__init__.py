@@ -52,6 +52,8 @@ class Oracle:
         L.oracle_encode_primary.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, _f32p, _u8p]
         L.oracle_encode_residual.argtypes = [_f32p, _u8p, _i64, C.c_int, C.c_int, C.c_int,
                                              _f32p, _f32p, C.c_int, _u8p, _f32p]
+        L.oracle_encode_residual_ps.argtypes = [_f32p, _u8p, _i64, C.c_int, C.c_int, C.c_int,
+                                                _f32p, _f32p, C.c_int, C.c_int, _u8p, _f32p]
         L.oracle_cent_norms.argtypes = [_f32p, C.c_int, C.c_int, _f32p]
         L.oracle_assign.argtypes = [_f32p, _i64, C.c_int, _f32p, _f32p, C.c_int, _i32p]
         L.oracle_train_ivf.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, _f32p]
@@ -65,6 +67,10 @@ class Oracle:
                                     _f32p, _f32p, _u8p, _u8p, _f32p, _i32p, _i64,
                                     _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_float,
                                     C.c_int, _f32p, _i32p]
+        L.oracle_search_ps.argtypes = [_f32p, _i64, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       _f32p, _f32p, C.c_int, _u8p, _u8p, _f32p, _i32p, _i64,
+                                       _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_float,
+                                       C.c_int, _f32p, _i32p]
         L.oracle_rerank.argtypes = [_f32p, _i64, C.c_int, _f32p, _i64, _i32p, C.c_int, C.c_int,
                                     _f32p, _i32p]
         self.L = L
@@ -112,14 +118,16 @@ class Oracle:
         self.L.oracle_encode_primary(y, y.shape[0], y.shape[1], M, B, _f32(c1d), codes)
         return codes
 
-    def encode_residual(self, y, codes, M, B, c1d, res_c1d, Br):
+    def encode_residual(self, y, codes, M, B, c1d, res_c1d, Br, per_sub=False):
+        """per_sub: res_c1d is [M][Kr], one residual codebook per subspace."""
         y = _f32(y)
         n, d = y.shape
         bpv = (d * Br + 7) // 8
         rc = np.zeros((n, bpv), np.uint8)
         corr = np.zeros(n, np.float32)
-        self.L.oracle_encode_residual(y, np.ascontiguousarray(codes, np.uint8), n, d, M, B,
-                                      _f32(c1d), _f32(res_c1d), Br, rc, corr)
+        self.L.oracle_encode_residual_ps(y, np.ascontiguousarray(codes, np.uint8), n, d, M, B,
+                                         _f32(c1d), _f32(res_c1d).ravel(), Br, int(per_sub), rc,
+                                         corr)
         return rc, corr
 
     def cent_norms(self, cents):
@@ -156,7 +164,7 @@ class Oracle:
         return self.L.oracle_ck(k, alpha)
 
     def search(self, q_rot, *, M, B, Br, c1d, res_c1d, codes, res, corr, assign,
-               cents, k, alpha, nprobe, norms=None, nthreads=0):
+               cents, k, alpha, nprobe, norms=None, nthreads=0, per_sub=False):
         q = _f32(q_rot)
         nq, d = q.shape
         cents = _f32(cents)
@@ -164,8 +172,8 @@ class Oracle:
             norms = self.cent_norms(cents)
         D = np.zeros((nq, k), np.float32)
         I = np.zeros((nq, k), np.int32)
-        rc = self.L.oracle_search(q, nq, d, M, B, Br, _f32(c1d), _f32(res_c1d),
-                                  np.ascontiguousarray(codes, np.uint8),
+        rc = self.L.oracle_search_ps(q, nq, d, M, B, Br, _f32(c1d), _f32(res_c1d).ravel(),
+                                  int(per_sub), np.ascontiguousarray(codes, np.uint8),
                                   np.ascontiguousarray(res, np.uint8), _f32(corr),
                                   np.ascontiguousarray(assign, np.int32), codes.shape[0],
                                   cents, _f32(norms), cents.shape[0], nprobe, k, alpha,
@@ -324,6 +332,32 @@ class RefGPU:
             raise RuntimeError(f"reference {self.version} pin run failed ({rcode})")
         return pc, rc, co, D, I
 
+    def pin_sweep(self, y, q_rot, *, M, c1d, res_c1d, cents, alphas, sigma=1.0, B=8, Br=4,
+                  k=10, nlist=1, nprobe=1, batch=64, reps=5):
+        """Time the reference's search() on the caller's artefacts (identity rotation,
+        already-rotated y / q_rot) for each alpha. Returns (ids [len(alphas)][nq][k],
+        mean search ms per alpha, add ms)."""
+        y, q = _f32(y), _f32(q_rot)
+        n, d = y.shape
+        a = np.ascontiguousarray(alphas, np.float32)
+        I = np.zeros((len(a), len(q), k), np.int32)
+        ms = np.zeros(len(a), np.float64)
+        ad = C.c_double()
+        L = self.L
+        L.ref_gpu_pin_sweep.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        _f32p, C.c_int, _f32p, C.c_int, _f32p, C.c_float,
+                                        _f32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double),
+                                        np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
+        c1d, res_c1d = _f32(c1d), _f32(res_c1d)
+        cents = _f32(cents) if nlist > 1 else np.zeros((1, d), np.float32)
+        rc = L.ref_gpu_pin_sweep(y, n, q, len(q), d, M, B, Br, k, nlist, nprobe, batch, c1d,
+                                 len(c1d), res_c1d, len(res_c1d), cents, sigma, a, len(a), reps,
+                                 I.reshape(-1), C.byref(ad), ms)
+        if rc != 0:
+            raise RuntimeError(f"reference {self.version} pinned sweep failed")
+        return I, ms, ad.value
+
 
 class RefHBlock:
     """The reference's own hblock graph index (v34 / v35 / v36), built from its
@@ -354,29 +388,3 @@ class RefHBlock:
         if rc != 0:
             raise RuntimeError(f"reference hblock {self.version} run failed")
         return I, ms, dict(train_ms=tr.value, add_ms=ad.value)
-
-    def pin_sweep(self, y, q_rot, *, M, c1d, res_c1d, cents, alphas, sigma=1.0, B=8, Br=4,
-                  k=10, nlist=1, nprobe=1, batch=64, reps=5):
-        """Time the reference's search() on the caller's artefacts (identity rotation,
-        already-rotated y / q_rot) for each alpha. Returns (ids [len(alphas)][nq][k],
-        mean search ms per alpha, add ms)."""
-        y, q = _f32(y), _f32(q_rot)
-        n, d = y.shape
-        a = np.ascontiguousarray(alphas, np.float32)
-        I = np.zeros((len(a), len(q), k), np.int32)
-        ms = np.zeros(len(a), np.float64)
-        ad = C.c_double()
-        L = self.L
-        L.ref_gpu_pin_sweep.argtypes = [_f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int,
-                                        C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
-                                        _f32p, C.c_int, _f32p, C.c_int, _f32p, C.c_float,
-                                        _f32p, C.c_int, C.c_int, _i32p, C.POINTER(C.c_double),
-                                        np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")]
-        c1d, res_c1d = _f32(c1d), _f32(res_c1d)
-        cents = _f32(cents) if nlist > 1 else np.zeros((1, d), np.float32)
-        rc = L.ref_gpu_pin_sweep(y, n, q, len(q), d, M, B, Br, k, nlist, nprobe, batch, c1d,
-                                 len(c1d), res_c1d, len(res_c1d), cents, sigma, a, len(a), reps,
-                                 I.reshape(-1), C.byref(ad), ms)
-        if rc != 0:
-            raise RuntimeError(f"reference {self.version} pinned sweep failed")
-        return I, ms, ad.value

@@ -168,6 +168,16 @@ void oracle_encode_residual(const float* y, const uint8_t* codes, int64_t n,
                             int d, int M, int B, const float* c1d,
                             const float* res_c1d, int Br,
                             uint8_t* res_codes, float* corr) {
+    oracle_encode_residual_ps(y, codes, n, d, M, B, c1d, res_c1d, Br, 0, res_codes, corr);
+}
+
+/* Per-subspace residual codebooks (per_sub != 0): dim j is coded against
+ * codebook m = j / Ds, res_c1d[m * Kr .. m * Kr + Kr); one global codebook
+ * otherwise (the reference's format). */
+void oracle_encode_residual_ps(const float* y, const uint8_t* codes, int64_t n,
+                               int d, int M, int B, const float* c1d,
+                               const float* res_c1d_all, int Br, int per_sub,
+                               uint8_t* res_codes, float* corr) {
     int Ds = d / M, bpd = B / Ds, kmask = (1 << bpd) - 1, Kr = 1 << Br;
     int bpv = (d * Br + 7) / 8;
     for (int64_t i = 0; i < n; ++i) {
@@ -180,6 +190,7 @@ void oracle_encode_residual(const float* y, const uint8_t* codes, int64_t n,
             int m = j / Ds, k = j % Ds;
             float yh = c1d[(pc[m] >> (k * bpd)) & kmask];
             float r = yi[j] - yh;
+            const float* res_c1d = res_c1d_all + (per_sub ? (size_t)m * Kr : 0);
             int ri = nearest_sorted(res_c1d, Kr, r);
             if (Br == 4) {
                 if ((j & 1) == 0) rc[j / 2] = (uint8_t)(ri & 0x0F);
@@ -296,6 +307,11 @@ float oracle_adc(const float* lut, int M, const uint8_t* code) {
  * lane l owns 16-byte chunks l, l+32, ...; inside a chunk the dims ascend. */
 float oracle_residual(const float* q_rot, int d, int Br, const float* res_c1d,
                       const uint8_t* rc) {
+    return oracle_residual_ps(q_rot, d, 1, Br, res_c1d, 0, rc);
+}
+
+float oracle_residual_ps(const float* q_rot, int d, int Ds, int Br, const float* res_c1d_all,
+                         int per_sub, const uint8_t* rc) {
     int bpv = (d * Br + 7) / 8;
     int nchunks = (bpv + 15) / 16;
     int dpc = 128 / Br, mask = (1 << Br) - 1;          /* dims per 16-byte chunk */
@@ -308,6 +324,7 @@ float oracle_residual(const float* q_rot, int d, int Br, const float* res_c1d,
                 if (j >= d) break;
                 int byte = (t * Br) / 8, shift = (t * Br) % 8;
                 int ri = (rc[16 * c + byte] >> shift) & mask;
+                const float* res_c1d = res_c1d_all + (per_sub ? (size_t)(j / Ds) * (mask + 1) : 0);
                 float diff = q_rot[j] - res_c1d[ri];
                 acc = fmaf(diff, diff, acc);
             }
@@ -349,6 +366,17 @@ int oracle_search(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
                   const float* cents, const float* norms, int nlist, int nprobe,
                   int k, float alpha, int nthreads,
                   float* out_dists, int32_t* out_ids) {
+    return oracle_search_ps(q_rot, nq, d, M, B, Br, c1d, res_c1d, 0, codes, res, corr, assign, n,
+                            cents, norms, nlist, nprobe, k, alpha, nthreads, out_dists, out_ids);
+}
+
+int oracle_search_ps(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
+                     const float* c1d, const float* res_c1d, int per_sub,
+                     const uint8_t* codes, const uint8_t* res, const float* corr,
+                     const int32_t* assign, int64_t n,
+                     const float* cents, const float* norms, int nlist, int nprobe,
+                     int k, float alpha, int nthreads,
+                     float* out_dists, int32_t* out_ids) {
     if (d <= 0 || M <= 0 || d % M || k <= 0 || nlist <= 0 || nprobe <= 0) return 1;
     if (nprobe > nlist) nprobe = nlist;
     int bpv = (d * Br + 7) / 8;
@@ -412,7 +440,8 @@ int oracle_search(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
             for (int i = 0; i < ck; ++i) {
                 if (ci[i] == 0x7fffffff) continue;
                 int id = ci[i];
-                float r = oracle_residual(q, d, Br, res_c1d, res + (size_t)id * bpv);
+                float r = oracle_residual_ps(q, d, d / M, Br, res_c1d, per_sub,
+                                             res + (size_t)id * bpv);
                 float comp = (cd[i] + r) + corr[id];
                 topk_insert(fd, fi, k, comp, id);
             }

@@ -78,6 +78,21 @@ int   oracle_search(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
                     int k, float alpha, int nthreads,
                     float* out_dists, int32_t* out_ids);
 
+/* Per-subspace residual codebooks (per_sub != 0): res_c1d is [M][Kr] and dim j
+ * uses codebook j / Ds; per_sub = 0 is the functions above (one codebook). */
+void  oracle_encode_residual_ps(const float* y, const uint8_t* codes, int64_t n, int d, int M,
+                                int B, const float* c1d, const float* res_c1d, int Br,
+                                int per_sub, uint8_t* res_codes, float* corr);
+float oracle_residual_ps(const float* q_rot, int d, int Ds, int Br, const float* res_c1d,
+                         int per_sub, const uint8_t* res_code);
+int   oracle_search_ps(const float* q_rot, int64_t nq, int d, int M, int B, int Br,
+                       const float* c1d, const float* res_c1d, int per_sub,
+                       const uint8_t* codes, const uint8_t* res, const float* corr,
+                       const int32_t* assign, int64_t n,
+                       const float* cents, const float* norms, int nlist, int nprobe,
+                       int k, float alpha, int nthreads,
+                       float* out_dists, int32_t* out_ids);
+
 /* Exact rerank (stored vectors): q [nq][d] and x [n][d] as given, cand [nq][kr]
  * JHQ candidate ids (-1 = none). Outputs [nq][k]. Returns nonzero on bad args. */
 int   oracle_rerank(const float* q, int64_t nq, int d, const float* x, int64_t n,

@@ -484,3 +484,68 @@ def test_c1_generator_flat_pilot_bit_exact_vs_oracle(jhq, oracle):
     ox = _oracle_index(oracle, idx, x)
     for k in (10, 40):
         _assert_same(*idx.search(q, k), *_oracle_search(oracle, idx, ox, q, k))
+
+
+@pytest.mark.parametrize("d,M,nlist,n", [(128, 32, 1, 20000), (64, 16, 64, 6000),
+                                         (64, 16, 500, 1500), (1024, 128, 16, 8000)])
+def test_device_training_equals_host_training(jhq, monkeypatch, d, M, nlist, n):
+    """train() runs the IVF Lloyd update and the residual 1-D k-means on the device
+    (index-order double folds after a stable sort by cluster); JHQ_TRAIN_HOST=1
+    runs the host restatement of the reference's loops. Artefacts must be equal
+    bit for bit, including lists left empty (reseeded, nlist 500 on 1,500 rows)."""
+    x = _data(n, d, 51, 1.5)
+    p = jhq.Params(M=M, nlist=nlist, nprobe=min(8, nlist), ivf_iters=6)
+    a = jhq.JHQGpuIndex(d, p)
+    a.train(x)
+    monkeypatch.setenv("JHQ_TRAIN_HOST", "1")
+    b = jhq.JHQGpuIndex(d, p)
+    b.train(x)
+    ta, tb = a.get_trained(), b.get_trained()
+    for key in ("c1d", "res_c1d", "cents"):
+        assert np.array_equal(ta[key].view(np.uint32), tb[key].view(np.uint32)), key
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(d=128, M=32, nlist=1, nprobe=1, n=6000, Br=4),
+    dict(d=104, M=26, nlist=32, nprobe=6, n=8000, Br=4),
+    dict(d=64, M=8, nlist=8, nprobe=3, n=3000, Br=8),
+])
+def test_per_subspace_residual_codebooks_bit_exact(jhq, oracle, cfg, tmp_path):
+    """M per-subspace residual codebooks: codebook m is the 1-D k-means of the
+    residuals of subspace m's dims in (row, dim) order; encode, corr and the
+    full search equal the oracle's per-subspace restatement bit for bit; the
+    choice survives save/load."""
+    d, M, n = cfg["d"], cfg["M"], cfg["n"]
+    x = _data(n, d, 61)
+    q = _data(45, d, 62)
+    p = jhq.Params(M=M, Br=cfg["Br"], nlist=cfg["nlist"], nprobe=cfg["nprobe"], batch_size=32)
+    idx = jhq.JHQGpuIndex(d, p)
+    idx.set_residual_codebooks(True)
+    idx.train(x[:3000])
+    with pytest.raises(RuntimeError):
+        idx.set_residual_codebooks(False)
+    idx.add(x)
+    t = idx.get_trained()
+    assert t["res_c1d"].shape == (M, idx.Kr)
+    Ds = d // M
+    y = oracle.rotate(t["Pi"], x[:3000])
+    codes = oracle.encode_primary(y, M, 8, t["c1d"])
+    r = y - oracle.reconstruct(codes, d, M, 8, t["c1d"])
+    for m in (0, M // 2, M - 1):
+        exp = oracle.kmeans1d(r[:, m * Ds:(m + 1) * Ds].ravel(), idx.Kr)
+        assert np.array_equal(t["res_c1d"][m][:len(exp)], exp), m
+    yall = oracle.rotate(t["Pi"], x)
+    pc, rc, co, asg = idx.get_codes()
+    orc, oco = oracle.encode_residual(yall, pc, M, 8, t["c1d"], t["res_c1d"], cfg["Br"],
+                                      per_sub=True)
+    assert np.array_equal(rc, orc) and np.array_equal(co, oco)
+    qr = oracle.rotate(t["Pi"], q)
+    D2, I2 = oracle.search(qr, M=M, B=8, Br=cfg["Br"], c1d=t["c1d"], res_c1d=t["res_c1d"],
+                           codes=pc, res=rc, corr=co, assign=asg, cents=t["cents"], k=10,
+                           alpha=4.0, nprobe=min(cfg["nprobe"], cfg["nlist"]), per_sub=True)
+    _assert_same(*idx.search(q, 10), D2, I2)
+    path = str(tmp_path / "ps.jhq")
+    idx.save(path)
+    idx2 = jhq.JHQGpuIndex.load(path)
+    assert idx2.residual_per_subspace
+    _assert_same(*idx2.search(q, 10), D2, I2)
