@@ -397,6 +397,8 @@ def build_shard(args, cfg, dev, ws, rank, rerank):
     t_train = time.perf_counter() - t0
     if rerank:
         idx.set_rerank(rerank)
+    if args.paging_pool_gb:
+        idx.set_list_paging(int(args.paging_pool_gb * (1 << 30)))
     q_dev = datasets.rows_torch(args.config, 0, nq, dev, sub=2)
     st = dict(idx=idx, n=n, nq=nq, k=k, rounds=rounds, round_size=round_size, n_bulk=n_bulk,
               lo=lo, hi=hi, q_dev=q_dev, t_train=t_train)
@@ -417,8 +419,9 @@ def add_rows(args, st, a, b_, dev):
     import torch
     from jhq_gpu_b200 import datasets
     idx, k, nq = st["idx"], st["k"], st["nq"]
-    for s in range(a, b_, 2_000_000):
-        e = min(b_, s + 2_000_000)
+    step = 8_000_000                                 # rows per add() call
+    for s in range(a, b_, step):
+        e = min(b_, s + step)
         x = datasets.rows_torch(args.config, s, e, dev)
         idx.add(x.cpu().numpy())
         for c in range(0, e - s, 50_000):
@@ -529,13 +532,15 @@ def run_sharded(args):
     idx.set_profiling(False)
     # probed vectors per query on this shard -> algorithmic code bytes of the scan
     sizes = idx.list_sizes()
-    pr = torch.empty((nq, cfg["nprobe"]), dtype=torch.int32, device=dev)
-    idx.probe_device(q_dev.data_ptr(), nq, pr.data_ptr(), stream.cuda_stream)
-    torch.cuda.synchronize(dev)
-    probed = int(sizes[pr.cpu().numpy()].sum())
-    scan_bytes = probed * cfg["M"]                      # B = 8: one byte per subspace
     peak, peak_kind = peaks()
-    ach = scan_bytes / (stages["scan"] / 1000.0) / 1e9
+    probed, scan_bytes, ach = 0, 0, None
+    if not args.paging_pool_gb:                         # paged batches have no stage events
+        pr = torch.empty((nq, cfg["nprobe"]), dtype=torch.int32, device=dev)
+        idx.probe_device(q_dev.data_ptr(), nq, pr.data_ptr(), stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+        probed = int(sizes[pr.cpu().numpy()].sum())
+        scan_bytes = probed * cfg["M"]                  # B = 8: one byte per subspace
+        ach = scan_bytes / (stages["scan"] / 1000.0) / 1e9
     gather_ms = None
     if ws > 1:
         import torch.distributed as dist
@@ -581,7 +586,7 @@ def run_sharded(args):
 
     per_rank = {"stage_ms": {kk: round(v, 3) for kk, v in stages.items()},
                 "shard_vectors": st["hi"] - st["lo"], "probed_vectors_per_query": probed / nq,
-                "scan_gbs": round(ach, 1), "allgather_ms": gather_ms}
+                "scan_gbs": round(ach, 1) if ach else None, "allgather_ms": gather_ms}
     all_ranks = [per_rank]
     if ws > 1:
         import torch.distributed as dist
@@ -604,6 +609,7 @@ def run_sharded(args):
                "sample": f"{ns} of the {nq} queries against the same {n // 1_000_000}M index "
                          f"({dt:.1f} s, OpenMP over queries)"}
     t_train, t_add = st["t_train"], st["t_add"]
+    paging_waves = idx.paging_waves
     c1 = None
     if ws == 1 and not args.no_c1:
         del st, idx, ss
@@ -629,13 +635,16 @@ def run_sharded(args):
                        "h2d_bytes_per_step": nq * cfg["d"] * 4,
                        "d2h_bytes_per_step": nq * k * 8},
                "gpu_launches": int(launches),
-               "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak,
-                            "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": peak_kind,
+               "roofline": {"bound": "hbm", "achieved": round(ach, 1) if ach else None,
+                            "peak": peak, "unit": "GB/s",
+                            "frac": round(ach / peak, 4) if ach else None, "peak_kind": peak_kind,
                             "traffic": committed_traffic(f"scan_qmajor_{args.config}_traffic.json"),
                             "kernel": "scan_qmajor_kernel (rank 0; LUT + ADC + top-ck)",
                             "algorithmic_bytes_per_launch": int(scan_bytes)},
                "clocks": clocks, "cpu_baseline": cpu, "per_rank": all_ranks,
                "train_s": round(t_train, 1), "add_s_rank0": round(t_add, 1)}
+        if args.paging_pool_gb:
+            out["paging"] = {"pool_gib": args.paging_pool_gb, "waves": paging_waves}
         if rounds:
             out["metric"] = (f"QPS at recall@10>=0.95 (C4 sharded IVF-JHQ, {n_bulk // 1_000_000}M "
                              f"bulk + {rounds} streaming rounds of {round_size} adds, {ws} B200)")
@@ -918,6 +927,8 @@ def main(argv=None):
     ap.add_argument("--no-hblock", action="store_true",
                     help="skip timing the reference's hblock builds (oracle/_ref)")
     ap.add_argument("--db-size", type=int, default=0, help="c3/c4: database size (default 100M)")
+    ap.add_argument("--paging-pool-gb", type=float, default=0.0,
+                    help="c3/c4: out-of-core lists with a device page pool of this size (GiB)")
     ap.add_argument("--queries", type=int, default=0,
                     help="c3/c4: query count (default 10k; smaller for profiling captures)")
     ap.add_argument("--rounds", type=int, default=10,

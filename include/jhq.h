@@ -147,6 +147,22 @@ int jhq_set_rerank(jhq_index* idx, int R);
  * buffers of jhq_get_trained / jhq_set_trained hold M * Kr floats. */
 int jhq_set_residual_codebooks(jhq_index* idx, int per_subspace);
 int jhq_get_residual_codebooks(const jhq_index* idx, int* per_subspace);
+
+/* Out-of-core list paging (IVF only): pool_bytes > 0 keeps the index's codes
+ * (pages, slot ids, residual codes, corr, and the kept vectors of the exact
+ * rerank) in pinned host memory mapped into the device, and gives the device a
+ * page pool of pool_bytes. Every search batch stages the pages of the lists it
+ * probes into the pool (in waves of consecutive queries when they do not fit
+ * together) and scans them there; results equal the resident index's. The
+ * reference's counterpart is the bounded GPU region pool of its hblock_v39-v43
+ * builds (hblock_v41/README.md). Enable before the first jhq_add (JHQ_ESTATE
+ * otherwise); nlist = 1 or a pool smaller than one page -> JHQ_EINVAL; a search
+ * whose single query's lists exceed the pool -> JHQ_EINVAL. Not combined with
+ * jhq_search_device_noalloc / jhq_probe_device / jhq_search_device_probes
+ * (JHQ_ESTATE). Saved files hold the codes; a loaded index is resident. */
+int jhq_set_list_paging(jhq_index* idx, int64_t pool_bytes);
+/* Waves the paged searches of this index have run so far (diagnostics). */
+int jhq_paging_waves(const jhq_index* idx, int64_t* waves);
 int jhq_get_rerank(const jhq_index* idx, int* R);
 
 /* Accessors: JHQGpuIndex::ntotal() / dim() (jhq_gpu_index.cuh:44-45). */
@@ -177,6 +193,14 @@ int jhq_get_codes(const jhq_index* idx, uint8_t* primary, uint8_t* residual,
 
 /* JL rotation y = Pi x of host rows (jhq_gpu_index.cu:209-225). */
 int jhq_rotate(jhq_index* idx, const float* x, int64_t n, float* y);
+
+/* The rotation search() applies to queries (search.cu:338-339): on B200 a
+ * tcgen05 GEMM on a bf16 three-term split (x = hi + lo + r, |r| <= 2^-18 |x|;
+ * the products hi.hi, hi.lo, lo.hi accumulated in fp32, so |error| <=
+ * 2^-16 |x| |Pi col| per output), unless JHQ_ROTATE=simt selects the exact fp32
+ * chains of jhq_rotate. Database rows (add/train) always use jhq_rotate's path.
+ * Exposed so that a checker can search with the very same rotated queries. */
+int jhq_rotate_queries(jhq_index* idx, const float* x, int64_t n, float* y);
 
 /* Encode already-rotated host rows with the index's codebooks without adding
  * them (primary_encode_kernel + residual_encode_kernel, encode.cu:20-86). */

@@ -36,8 +36,8 @@ EXPORTED = [
     "jhq_last_error", "jhq_version", "jhq_jl_rotation", "jhq_estimate_sigma",
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_set_rerank", "jhq_get_rerank",
-    "jhq_set_alpha", "jhq_list_sizes", "jhq_device_status", "jhq_set_residual_codebooks",
-    "jhq_get_residual_codebooks",
+    "jhq_set_alpha", "jhq_list_sizes", "jhq_rotate_queries", "jhq_device_status", "jhq_set_residual_codebooks",
+    "jhq_get_residual_codebooks", "jhq_set_list_paging", "jhq_paging_waves",
     "jhq_probe_device",
     "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
     "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
@@ -106,9 +106,12 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_set_nprobe.argtypes = [vp, C.c_int]
     L.jhq_set_rerank.argtypes = [vp, C.c_int]
     L.jhq_set_alpha.argtypes = [vp, C.c_float]
+    L.jhq_rotate_queries.argtypes = [vp, f32p, i64, f32p]
     L.jhq_list_sizes.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_device_status.argtypes = [vp]
     L.jhq_set_residual_codebooks.argtypes = [vp, C.c_int]
+    L.jhq_set_list_paging.argtypes = [vp, i64]
+    L.jhq_paging_waves.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_get_residual_codebooks.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_get_rerank.argtypes = [vp, C.POINTER(C.c_int)]
     L.jhq_probe_device.argtypes = [vp, vp, i64, vp, vp]
@@ -294,6 +297,17 @@ class JHQGpuIndex:
         _check(self._L.jhq_get_residual_codebooks(self._h, C.byref(v)))
         return bool(v.value)
 
+    def set_list_paging(self, pool_bytes: int) -> None:
+        """Out-of-core lists: codes in mapped host memory, a device page pool of
+        pool_bytes staged per search batch (jhq_set_list_paging); before add()."""
+        _check(self._L.jhq_set_list_paging(self._h, int(pool_bytes)))
+
+    @property
+    def paging_waves(self) -> int:
+        v = C.c_int64()
+        _check(self._L.jhq_paging_waves(self._h, C.byref(v)))
+        return v.value
+
     def check_device_status(self) -> None:
         """Raises JHQError (JHQ_ETIMEDOUT) if a device wait of a search on the
         caller's stream gave up (jhq_device_status); call after the stream drained."""
@@ -381,6 +395,13 @@ class JHQGpuIndex:
         x = _f32(x)
         y = np.empty_like(x)
         _check(self._L.jhq_rotate(self._h, _ptr(x, C.c_float), x.shape[0], _ptr(y, C.c_float)))
+        return y
+
+    def rotate_queries(self, x) -> np.ndarray:
+        """The rotation search() applies to queries (tensor cores on B200)."""
+        x = _f32(x)
+        y = np.empty_like(x)
+        _check(self._L.jhq_rotate_queries(self._h, _ptr(x, C.c_float), x.shape[0], _ptr(y, C.c_float)))
         return y
 
     def encode(self, y):

@@ -154,6 +154,17 @@ int jhq_get_residual_codebooks(const jhq_index* idx, int* per_subspace) {
     });
 }
 
+int jhq_set_list_paging(jhq_index* idx, int64_t pool_bytes) {
+    return guarded([&] { need(idx)->set_list_paging(pool_bytes); });
+}
+
+int jhq_paging_waves(const jhq_index* idx, int64_t* waves) {
+    return guarded([&] {
+        if (!waves) jhq::fail(JHQ_EINVAL, "null output");
+        *waves = need(idx)->paging_waves();
+    });
+}
+
 int jhq_device_status(jhq_index* idx) {
     return guarded([&] { need(idx)->check_device_status(); });
 }
@@ -214,6 +225,13 @@ int jhq_set_trained(jhq_index* idx, const float* Pi, const float* c1d, const flo
 int jhq_get_codes(const jhq_index* idx, uint8_t* primary, uint8_t* residual, float* corr,
                   int32_t* assign) {
     return guarded([&] { need(idx)->get_codes(primary, residual, corr, assign); });
+}
+
+int jhq_rotate_queries(jhq_index* idx, const float* x, int64_t n, float* y) {
+    return guarded([&] {
+        if (n < 0 || (n > 0 && (!x || !y))) jhq::fail(JHQ_EINVAL, "rotate_queries: bad buffers");
+        need(idx)->rotate_queries(x, n, y);
+    });
 }
 
 int jhq_rotate(jhq_index* idx, const float* x, int64_t n, float* y) {

@@ -101,10 +101,22 @@ __global__ void scatter_pages_kernel(const int32_t* __restrict__ slot_ids, int64
 
 __global__ void set_int_kernel(int* dst, int value) { *dst = value; }
 
+__global__ void scale_kernel(float* __restrict__ v, int64_t n, float f) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) v[i] = __fmul_rn(v[i], f);
+}
+
 }  // namespace
 
 void set_int(int* dst, int value, cudaStream_t s) {
     set_int_kernel<<<1, 1, 0, s>>>(dst, value);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
+void scale_floats(float* v, int64_t n, float f, cudaStream_t s) {
+    if (n <= 0) return;
+    scale_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(v, n, f);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -21,14 +21,6 @@ namespace jhq {
 namespace {
 constexpr int MAX_CK_PAD = 256;
 
-template <class T>
-void h2d(T* dst, const T* src, size_t n, cudaStream_t s) {
-    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyHostToDevice, s));
-}
-template <class T>
-void d2h(T* dst, const T* src, size_t n, cudaStream_t s) {
-    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyDeviceToHost, s));
-}
 }  // namespace
 
 // ---- construction: JHQGpuIndex ctor validation (jhq_gpu_index.cu:103-131) ----
@@ -95,6 +87,26 @@ void Index::rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t 
     gemm_rows(d_x, dPi_.get(), d_y, n, d_, d_, EPI_STORE, nullptr, s);
 }
 
+size_t Index::rotq_scratch_floats(int Bq) const {
+    if (!rot_tc_) return 0;
+    const size_t q3f = (((size_t)Bq * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63;
+    return q3f + (size_t)Bq * coarse_tc_tiles(d_);
+}
+
+void Index::rotate_queries_device(const float* d_x, int64_t n, float* d_y, float* scratch,
+                                  cudaStream_t s) const {
+    if (!rot_tc_) {
+        rotate_device(d_x, n, d_y, s);
+        return;
+    }
+    const size_t q3f = (((size_t)n * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63;
+    uint16_t* q3 = reinterpret_cast<uint16_t*>(scratch);
+    float* tmin = scratch + q3f;
+    split3_rows(d_x, n, d_, q3, s);
+    coarse_scores_tc(q3, (int)n, dPi3_.get(), dzero_.get(), d_, d_, d_y, tmin, s);
+    scale_floats(d_y, n * d_, -0.5f, s);
+}
+
 void Index::assign_device(const float* d_y, int64_t n, int32_t* d_assign, cudaStream_t s) {
     if (p_.nlist == 1) {
         JHQ_CUDA(cudaMemsetAsync(d_assign, 0, n * sizeof(int32_t), s));
@@ -125,6 +137,25 @@ void Index::upload_trained() {
     h2d(dc1d_.get(), c1d_.data(), c1d_.size(), stream_);
     dres_.resize((size_t)residual_floats());
     if (!res_c1d_.empty()) h2d(dres_.get(), res_c1d_.data(), res_c1d_.size(), stream_);
+    // Query rotation on the tensor cores: y = x . Pi as the coarse kernel's
+    // s~ = 0 - 2 x . Pi[:, c] over the d columns of Pi (bf16 split rows of Pi^T,
+    // zero norms), scaled by -1/2 (exact). JHQ_ROTATE=simt keeps the fp32 chains.
+    {
+        const char* rm = std::getenv("JHQ_ROTATE");
+        rot_tc_ = d_ <= 2048 && !(rm && std::string(rm) == "simt");
+        if (rot_tc_) {
+            std::vector<float> piT((size_t)d_ * d_);
+            for (int j = 0; j < d_; ++j)
+                for (int c = 0; c < d_; ++c) piT[(size_t)c * d_ + j] = Pi_[(size_t)j * d_ + c];
+            std::vector<uint16_t> p3((size_t)d_ * coarse_tc_k3(d_));
+            split3_rows_host(piT.data(), d_, d_, 1, p3.data());
+            dPi3_.resize(p3.size());
+            h2d(dPi3_.get(), p3.data(), p3.size(), stream_);
+            std::vector<float> z((size_t)d_, 0.0f);
+            dzero_.resize(z.size());
+            h2d(dzero_.get(), z.data(), z.size(), stream_);
+        }
+    }
     // centroids as the row-major [d][nlist] right operand, plus |c|^2 in double
     // (jhq_gpu_index.cu:243-249)
     const int nl = p_.nlist;
@@ -390,6 +421,16 @@ void Index::get_trained(float* Pi, float* c1d, float* res_c1d, float* cents, flo
 // ---- add: JHQGpuIndex::add (jhq_gpu_index.cu:417-532), repeatable ------------
 void Index::grow_master(int64_t need) {
     if (need <= cap_) return;
+    if (paging()) {                    // host-resident codes (paging.cu)
+        const int64_t nc = std::max<int64_t>(need, cap_ + cap_ / 2);
+        hpcodes_.grow((size_t)nc * M_, (size_t)ntotal_ * M_);
+        hrcodes_.grow((size_t)nc * bpv_pad_, (size_t)ntotal_ * bpv_pad_);
+        hcorr_.grow((size_t)nc, (size_t)ntotal_);
+        if (keep_raw_) hraw_.grow((size_t)nc * d_, (size_t)ntotal_ * d_);
+        dassign_.resize(1);
+        cap_ = nc;
+        return;
+    }
     int64_t nc = std::max<int64_t>(need, cap_ + cap_ / 2);
     DevBuf<uint8_t> pc((size_t)nc * M_), rc((size_t)nc * bpv_pad_);
     DevBuf<float> co((size_t)nc);
@@ -425,11 +466,32 @@ void Index::add(const float* h_x, int64_t n) {
     const int64_t AB = std::min<int64_t>(p_.add_batch, n);
     DevBuf<float> dx((size_t)AB * d_), dy((size_t)AB * d_);
     DevBuf<int32_t> dpa;
+    DevBuf<uint8_t> tp, tr;            // paging: per-batch codes before the host copy
+    DevBuf<float> tc;
+    DevBuf<int32_t> ta;
     if (pilotP_ > 0) h_pilot_assign_.resize((size_t)(ntotal_ + n));
     for (int64_t r0 = 0; r0 < n; r0 += AB) {
         const int64_t nr = std::min(AB, n - r0);
         const int64_t at = ntotal_ + r0;
         h2d(dx.get(), h_x + r0 * d_, (size_t)nr * d_, stream_);
+        if (paging()) {                // encode into batch temporaries, append to host
+            if (keep_raw_) std::memcpy(hraw_.get() + at * d_, h_x + r0 * d_, (size_t)nr * d_ * 4);
+            rotate_device(dx.get(), nr, dy.get(), stream_);
+            tp.ensure((size_t)AB * M_);
+            tr.ensure((size_t)AB * bpv_pad_);
+            tc.ensure((size_t)AB);
+            ta.ensure((size_t)AB);
+            assign_device(dy.get(), nr, ta.get(), stream_);
+            encode_rows(dy.get(), nr, d_, M_, B_, Br_, dc1d_.get(), dres_.get(), res_per_sub_,
+                        tp.get(), tr.get(), bpv_pad_, tc.get(), stream_);
+            h_assign_.resize((size_t)(at + nr));
+            d2h(h_assign_.data() + at, ta.get(), (size_t)nr, stream_);
+            d2h(hpcodes_.get() + at * M_, tp.get(), (size_t)nr * M_, stream_);
+            d2h(hrcodes_.get() + at * bpv_pad_, tr.get(), (size_t)nr * bpv_pad_, stream_);
+            d2h(hcorr_.get() + at, tc.get(), (size_t)nr, stream_);
+            JHQ_CUDA(cudaStreamSynchronize(stream_));
+            continue;
+        }
         if (keep_raw_)
             JHQ_CUDA(cudaMemcpyAsync(draw_.get() + at * d_, dx.get(), (size_t)nr * d_ * 4,
                                      cudaMemcpyDeviceToDevice, stream_));
@@ -445,8 +507,10 @@ void Index::add(const float* h_x, int64_t n) {
                     dpcodes_.get() + at * M_, drcodes_.get() + at * bpv_pad_, bpv_pad_,
                     dcorr_.get() + at, stream_);
     }
-    h_assign_.resize((size_t)(ntotal_ + n));
-    d2h(h_assign_.data() + ntotal_, dassign_.get() + ntotal_, (size_t)n, stream_);
+    if (!paging()) {
+        h_assign_.resize((size_t)(ntotal_ + n));
+        d2h(h_assign_.data() + ntotal_, dassign_.get() + ntotal_, (size_t)n, stream_);
+    }
     JHQ_CUDA(cudaStreamSynchronize(stream_));
     ntotal_ += n;
     rebuild_layout();
@@ -479,6 +543,12 @@ void Index::rebuild_layout() {
     h_list_pages_sorted_.resize(nl);
     for (int c = 0; c < nl; ++c) h_list_pages_sorted_[c] = lpo[c + 1] - lpo[c];
     std::sort(h_list_pages_sorted_.begin(), h_list_pages_sorted_.end(), std::greater<int32_t>());
+    if (paging()) {                    // pages and slot ids built in host memory
+        build_host_pages(lpo, slots);
+        layout_dirty_ = false;
+        destroy_graph();
+        return;
+    }
     dlist_page_off_.resize(nl + 1);
     dslot_ids_.resize(std::max<size_t>(1, slots.size()));
     dpages_.resize(std::max<size_t>(16, (size_t)pages * Mp_ * 32));
@@ -571,7 +641,7 @@ Index::BatchShape Index::batch_shape(int Bq, int k) const {
 
 void Index::prepare_workspace(int k) {
     const int Bq = p_.batch_size;
-    if (ws_.batch_cap == Bq && ws_.k == k && ws_.exec &&
+    if (ws_.batch_cap == Bq && ws_.k == k && (ws_.exec || paging()) &&
         ws_.coarse_floats == coarse_scratch_floats(Bq))
         return;
     destroy_graph();
@@ -581,6 +651,7 @@ void Index::prepare_workspace(int k) {
     const int nl = p_.nlist, np = p_.nprobe;
     ws_.q.ensure((size_t)Bq * d_);
     ws_.q_rot.ensure((size_t)Bq * d_);
+    ws_.rotq.ensure(std::max<size_t>(1, rotq_scratch_floats(Bq)));
     ws_.coarse_floats = coarse_scratch_floats(Bq);
     if (nl > 1) ws_.scores.ensure(ws_.coarse_floats);
     ws_.probes.ensure((size_t)Bq * np);
@@ -613,6 +684,10 @@ void Index::prepare_workspace(int k) {
     ws_.chunk_pages = sh.chunk_pages;
     ws_.max_slots = sh.max_slots;
     ws_.qmajor = sh.qmajor;
+    if (paging()) {                    // paged batches are host-orchestrated (paging.cu)
+        JHQ_CUDA(cudaStreamSynchronize(stream_));
+        return;
+    }
     // capture the per-batch pipeline once (capture_graph, search.cu:315-386)
     const int64_t before = g_kernel_launches.load();
     JHQ_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
@@ -664,7 +739,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
                              const int32_t* probes_in) {
     auto mark = [&](int i) { if (ev) JHQ_CUDA(cudaEventRecord(ev[i], s)); };
     mark(0);
-    rotate_device(q_in, nq, b.q_rot, s);
+    rotate_queries_device(q_in, nq, b.q_rot, b.rotq, s);
     mark(1);
     const int32_t* probes = probes_in ? probes_in : b.probes;
     if (p_.nlist > 1 && !probes_in) {
@@ -725,6 +800,7 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     sh.qmajor = ws_.qmajor;
     BatchBufs b;
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
+    b.rotq = ws_.rotq.get();
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
@@ -823,7 +899,8 @@ void Index::search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t*
             std::memcpy(hq, h_q + q0 * d_, (size_t)nv * d_ * 4);
             if (nv < Bq) std::memset(hq + nv * d_, 0, (size_t)(Bq - nv) * d_ * 4);
             h2d(ws_.q.get(), hq, (size_t)Bq * d_, stream_);
-            run_batch(stream_, (int)nv);
+            if (paging()) run_paged_batch(ws_.q.get(), (int)nv, ws_.out_d.get(), ws_.out_i.get(), stream_);
+            else run_batch(stream_, (int)nv);
             d2h(ws_.h_d.get() + (size_t)slot * Bq * k, ws_.out_d.get(), (size_t)Bq * k, stream_);
             d2h(ws_.h_i.get() + (size_t)slot * Bq * k, ws_.out_i.get(), (size_t)Bq * k, stream_);
             JHQ_CUDA(cudaEventRecord(ev[slot], stream_));
@@ -839,7 +916,7 @@ void Index::search(const float* h_q, int64_t nq, int k, float* h_dists, int32_t*
     }
     cudaEventDestroy(ev[0]);
     cudaEventDestroy(ev[1]);
-    if (coarse_tc_ && coarse_tc_error(true))
+    if ((coarse_tc_ || rot_tc_) && coarse_tc_error(true))
         fail(JHQ_ETIMEDOUT, "search: a tensor-core coarse wait gave up");
 }
 
@@ -856,7 +933,8 @@ void Index::search_device(const float* d_q, int64_t nq, int k, float* d_dists, i
         const int64_t nv = std::min<int64_t>(Bq, nq - q0);
         JHQ_CUDA(cudaMemcpyAsync(ws_.q.get(), d_q + q0 * d_, (size_t)nv * d_ * 4,
                                  cudaMemcpyDeviceToDevice, s));
-        run_batch(s, (int)nv);
+        if (paging()) run_paged_batch(ws_.q.get(), (int)nv, ws_.out_d.get(), ws_.out_i.get(), s);
+        else run_batch(s, (int)nv);
         JHQ_CUDA(cudaMemcpyAsync(d_dists + q0 * k, ws_.out_d.get(), (size_t)nv * k * 4,
                                  cudaMemcpyDeviceToDevice, s));
         JHQ_CUDA(cudaMemcpyAsync(d_ids + q0 * k, ws_.out_i.get(), (size_t)nv * k * 4,
@@ -869,12 +947,13 @@ void Index::probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaSt
     check_search_args(nq, ws_.k ? ws_.k : 10);
     if (nq == 0) return;
     if (!d_q || !d_probes) fail(JHQ_EINVAL, "probe_device: null buffer");
+    if (paging()) fail(JHQ_ESTATE, "probe_device: not available with list paging");
     prepare_workspace(ws_.k ? ws_.k : 10);
     cudaStream_t s = stream ? stream : stream_;
     const int Bq = ws_.batch_cap, np = p_.nprobe;
     for (int64_t q0 = 0; q0 < nq; q0 += Bq) {
         const int nv = (int)std::min<int64_t>(Bq, nq - q0);
-        rotate_device(d_q + q0 * d_, nv, ws_.q_rot.get(), s);
+        rotate_queries_device(d_q + q0 * d_, nv, ws_.q_rot.get(), ws_.rotq.get(), s);
         if (p_.nlist > 1) {
             coarse_probes(ws_.q_rot.get(), nv, Bq, np, ws_.scores.get(), d_probes + q0 * np, s);
         } else {
@@ -889,6 +968,7 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     check_search_args(nq, k);
     if (nq == 0) return;
     if (!d_q || !d_probes || !d_dists || !d_ids) fail(JHQ_EINVAL, "search_device_probes: null buffer");
+    if (paging()) fail(JHQ_ESTATE, "search_device_probes: not available with list paging");
     prepare_workspace(k);
     cudaStream_t s = stream ? stream : stream_;
     BatchShape sh;
@@ -898,6 +978,7 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     sh.max_slots = ws_.max_slots; sh.qmajor = ws_.qmajor;
     BatchBufs b;
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
+    b.rotq = ws_.rotq.get();
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
@@ -935,7 +1016,7 @@ void Index::set_alpha(float alpha) {
 
 void Index::check_device_status() {
     DeviceGuard g(dev_);
-    if (coarse_tc_ && coarse_tc_error(true))
+    if ((coarse_tc_ || rot_tc_) && coarse_tc_error(true))
         fail(JHQ_ETIMEDOUT, "a tensor-core coarse wait gave up: the probe lists of that search "
                             "are not valid");
 }
@@ -946,7 +1027,7 @@ void Index::synchronize(double timeout_s) {
     for (;;) {
         cudaError_t e = cudaStreamQuery(stream_);
         if (e == cudaSuccess) {
-            if (coarse_tc_ && coarse_tc_error(true))
+            if ((coarse_tc_ || rot_tc_) && coarse_tc_error(true))
                 fail(JHQ_ETIMEDOUT, "synchronize: a tensor-core coarse wait gave up");
             return;
         }
@@ -963,12 +1044,25 @@ void Index::get_codes(uint8_t* primary, uint8_t* residual, float* corr, int32_t*
     const int64_t n = ntotal_;
     if (n == 0) return;
     JHQ_CUDA(cudaStreamSynchronize(stream_));
-    if (primary) JHQ_CUDA(cudaMemcpy(primary, dpcodes_.get(), (size_t)n * M_, cudaMemcpyDeviceToHost));
+    const uint8_t* pc = paging() ? hpcodes_.get() : dpcodes_.get();
+    const uint8_t* rc = paging() ? hrcodes_.get() : drcodes_.get();
+    const float* co = paging() ? hcorr_.get() : dcorr_.get();
+    if (primary) JHQ_CUDA(cudaMemcpy(primary, pc, (size_t)n * M_, cudaMemcpyDefault));
     if (residual)
-        JHQ_CUDA(cudaMemcpy2D(residual, bpv_, drcodes_.get(), bpv_pad_, bpv_, (size_t)n,
-                              cudaMemcpyDeviceToHost));
-    if (corr) JHQ_CUDA(cudaMemcpy(corr, dcorr_.get(), (size_t)n * 4, cudaMemcpyDeviceToHost));
+        JHQ_CUDA(cudaMemcpy2D(residual, bpv_, rc, bpv_pad_, bpv_, (size_t)n, cudaMemcpyDefault));
+    if (corr) JHQ_CUDA(cudaMemcpy(corr, co, (size_t)n * 4, cudaMemcpyDefault));
     if (assign) std::memcpy(assign, h_assign_.data(), (size_t)n * 4);
+}
+
+void Index::rotate_queries(const float* h_x, int64_t n, float* h_y) {
+    DeviceGuard g(dev_);
+    if (!trained_) fail(JHQ_ESTATE, "index is not trained");
+    if (n <= 0) return;
+    DevBuf<float> dx((size_t)n * d_), dy((size_t)n * d_), sc(std::max<size_t>(1, rotq_scratch_floats((int)n)));
+    h2d(dx.get(), h_x, (size_t)n * d_, stream_);
+    rotate_queries_device(dx.get(), n, dy.get(), sc.get(), stream_);
+    d2h(h_y, dy.get(), (size_t)n * d_, stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
 }
 
 void Index::rotate(const float* h_x, int64_t n, float* h_y) {
@@ -1039,7 +1133,8 @@ void Index::save(const std::string& path) const {
         if (pilotP_ > 0) put(h_pilot_assign_.data(), (size_t)ntotal_ * 4);
         if (keep_raw_) {
             std::vector<float> rw((size_t)ntotal_ * d_);
-            JHQ_CUDA(cudaMemcpy(rw.data(), draw_.get(), rw.size() * 4, cudaMemcpyDeviceToHost));
+            JHQ_CUDA(cudaMemcpy(rw.data(), paging() ? hraw_.get() : draw_.get(), rw.size() * 4,
+                                cudaMemcpyDefault));
             put(rw.data(), rw.size() * 4);
         }
     }

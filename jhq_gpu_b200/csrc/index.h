@@ -72,6 +72,7 @@ public:
                      float sigma);
     void get_codes(uint8_t* primary, uint8_t* residual, float* corr, int32_t* assign) const;
     void rotate(const float* h_x, int64_t n, float* h_y);
+    void rotate_queries(const float* h_x, int64_t n, float* h_y);
     void encode(const float* h_y, int64_t n, uint8_t* primary, uint8_t* residual, float* corr);
     void save(const std::string& path) const;
     static Index* load(const std::string& path, int device);
@@ -95,6 +96,15 @@ public:
     // default) or M per-subspace codebooks, res_c1d [M][Kr] (dim j uses codebook
     // j / Ds). Chosen before train() / set_trained(); fixed afterwards.
     void set_residual_codebooks(bool per_subspace);
+    // Out-of-core list paging: the codes (page layout, slot ids, residual codes,
+    // corr, kept vectors) live in mapped pinned host memory, and every search
+    // batch stages the pages of the lists it probes into a device pool of
+    // `pool_bytes` (waves of queries when the union does not fit). IVF only
+    // (nlist > 1); enable before the first add(). 0 = off (all resident).
+    void set_list_paging(int64_t pool_bytes);
+    bool paging() const { return pool_pages_ > 0; }
+    int64_t pool_pages() const { return pool_pages_; }
+    int64_t paging_waves() const { return paging_waves_; }
     bool residual_per_subspace() const { return res_per_sub_; }
     int residual_floats() const { return res_per_sub_ ? M_ * Kr_ : Kr_; }
     int rerank() const { return rerank_; }
@@ -111,7 +121,7 @@ private:
         PinnedBuf<float> h_d;          // [batch][k]
         PinnedBuf<int32_t> h_i;
         PinnedBuf<int> h_nvalid;
-        DevBuf<float> q, q_rot, scores, out_d;
+        DevBuf<float> q, q_rot, scores, out_d, rotq;
         DevBuf<int32_t> probes, out_i, cnt, bucket_off, unit_off, fill, cpo;
         DevBuf<int2> bucket;
         DevBuf<int64_t> qslot_off;
@@ -129,6 +139,11 @@ private:
                const std::function<const int32_t*(const std::vector<float>&)>& assign);
     void upload_pilot(const std::vector<float>& c, int P);
     void rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t s) const;
+    // Search-side query rotation: tensor cores (rot_tc_, bf16 split, error below
+    // 2^-16 |x||Pi|) or the exact fp32 chains; scratch holds rotq_scratch_floats(n).
+    void rotate_queries_device(const float* d_x, int64_t n, float* d_y, float* scratch,
+                               cudaStream_t s) const;
+    size_t rotq_scratch_floats(int Bq) const;
     // q_rot [nq][d] -> probes [nq][nprobe] through scores [nq][nlist] (scratch):
     // tensor-core scores + margin selection, or the fp32 SIMT GEMM + exact
     // selection (JHQ_COARSE=simt); both give the same lists.
@@ -155,12 +170,16 @@ private:
         uint64_t* cand;
         uint64_t* pkeys = nullptr;     // pilot scratch (flat index with pilot clusters)
         float* pscores = nullptr;
+        float* rotq = nullptr;         // tensor-core query rotation scratch
     };
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
                           const BatchBufs& b, float* out_d, int32_t* out_i, cudaStream_t s,
                           cudaEvent_t* ev, const int32_t* probes_in = nullptr);
     void enqueue_batch(cudaStream_t s, cudaEvent_t* ev = nullptr);
+    // paged search of one batch (paging.cu): q_in [nq][d] on the device
+    void run_paged_batch(const float* q_in, int nq, float* out_d, int32_t* out_i, cudaStream_t s);
+    void build_host_pages(const std::vector<int32_t>& lpo, const std::vector<int32_t>& slots);
     void run_batch(cudaStream_t s, int nvalid);
     void check_search_args(int64_t nq, int k) const;
     // candidates the JHQ stage returns for a search of k: k, or max(R, k) with rerank
@@ -184,6 +203,9 @@ private:
 
     DevBuf<float> dPi_, dc1d_, dres_, dcentsT_, dcents_, dnorms_;
     DevBuf<uint16_t> dcents3_;         // bf16 split centroids [nlist][K3]
+    bool rot_tc_ = false;              // query rotation on the tensor cores
+    DevBuf<uint16_t> dPi3_;            // bf16 split rows of Pi^T [d][K3]
+    DevBuf<float> dzero_;              // d zeros (the rotation's "norms")
     // Pilot clusters of a flat index: per query, the ADC keys of the nearest
     // cluster's members seed its pruning bound (pilot.cu).
     static constexpr int PILOT_LISTS = 64, PILOT_MIN_MEMBERS = 16;
@@ -198,6 +220,15 @@ private:
     DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
     DevBuf<float> dcorr_;
     bool res_per_sub_ = false;         // M per-subspace residual codebooks
+    // list paging (paging.cu): host-resident codes + device page pool
+    int64_t pool_pages_ = 0, paging_waves_ = 0;
+    MappedBuf<uint8_t> hpcodes_, hrcodes_, hpages_;
+    MappedBuf<float> hcorr_, hraw_;
+    MappedBuf<int32_t> hslot_ids_;
+    std::vector<int32_t> h_lpo_;               // list page offsets (host copy)
+    DevBuf<uint8_t> dpool_pages_;
+    DevBuf<int32_t> dpool_slots_, dlpo_wave_;
+    DevBuf<int64_t> dseg_;
     bool keep_raw_ = false;            // stored vectors for the exact rerank
     int rerank_ = 0;
     DevBuf<float> draw_;               // [cap][d] vectors as given (keep_raw_)

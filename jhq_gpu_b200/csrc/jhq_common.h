@@ -12,6 +12,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 #include <mutex>
@@ -106,7 +107,46 @@ private:
     size_t n_ = 0;
 };
 
+// Pinned, device-mapped host allocation (cudaHostAllocMapped: with unified
+// addressing the same pointer is valid in kernels, which read it over the host
+// link). Grows geometrically and keeps its first `keep` elements.
+template <class T>
+class MappedBuf {
+public:
+    MappedBuf() = default;
+    ~MappedBuf() { release(); }
+    MappedBuf(const MappedBuf&) = delete;
+    MappedBuf& operator=(const MappedBuf&) = delete;
+    void grow(size_t n, size_t keep) {
+        if (n <= n_) return;
+        size_t nc = n_ + n_ / 2 > n ? n_ + n_ / 2 : n;
+        T* p = nullptr;
+        JHQ_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p), nc * sizeof(T),
+                               cudaHostAllocMapped | cudaHostAllocPortable));
+        if (p_ && keep) std::memcpy(p, p_, keep * sizeof(T));
+        release();
+        p_ = p;
+        n_ = nc;
+    }
+    void release() { if (p_) cudaFreeHost(p_); p_ = nullptr; n_ = 0; }
+    T* get() const { return p_; }
+    size_t size() const { return n_; }
+private:
+    T* p_ = nullptr;
+    size_t n_ = 0;
+};
+
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Stream-ordered copies of n elements.
+template <class T>
+void h2d(T* dst, const T* src, size_t n, cudaStream_t s) {
+    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyHostToDevice, s));
+}
+template <class T>
+void d2h(T* dst, const T* src, size_t n, cudaStream_t s) {
+    if (n) JHQ_CUDA(cudaMemcpyAsync(dst, src, n * sizeof(T), cudaMemcpyDeviceToHost, s));
+}
 inline int next_pow2(int x) { int p = 1; while (p < x) p <<= 1; return p; }
 
 // Runs f once per CUDA device of the process, with that device current

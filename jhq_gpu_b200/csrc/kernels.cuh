@@ -31,6 +31,8 @@ void gemm_argmin(const float* A, const float* B, const float* norms, int64_t R, 
 void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
                  const float* c1d, const float* res_c1d, bool res_per_sub, uint8_t* pcodes,
                  uint8_t* rcodes, int bpv_pad, float* corr, cudaStream_t s);
+// v[i] *= f (f a power of two here, so exact)
+void scale_floats(float* v, int64_t n, float f, cudaStream_t s);
 // dst[0] = value (stream-ordered scalar upload, no host buffer involved).
 void set_int(int* dst, int value, cudaStream_t s);
 // Scatter codes into the page layout: slot_ids [npages*32] (-1 = empty slot),

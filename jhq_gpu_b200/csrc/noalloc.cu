@@ -68,6 +68,7 @@ void Index::search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_
     check_search_args(nq, k);
     if (nq == 0) return;
     if (!d_q || !d_dists || !d_ids) fail(JHQ_EINVAL, "search_device_noalloc: null buffer");
+    if (paging()) fail(JHQ_ESTATE, "search_device_noalloc: not available with list paging");
     unsigned char* base = scratch_for(dev_);
     cudaStream_t s = stream ? stream : stream_;
 
@@ -80,6 +81,7 @@ void Index::search_device_noalloc(const float* d_q, int64_t nq, int k, float* d_
     auto take = [&](size_t bytes) { size_t o = off; off = up256(off + bytes); return base + o; };
     BatchBufs b;
     b.q_rot = reinterpret_cast<float*>(take((size_t)Bq * d_ * 4));
+    b.rotq = reinterpret_cast<float*>(take(std::max<size_t>(1, rotq_scratch_floats(Bq)) * 4));
     b.scores = nl > 1 ? reinterpret_cast<float*>(take(coarse_scratch_floats(Bq) * 4)) : nullptr;
     b.probes = reinterpret_cast<int32_t*>(take((size_t)Bq * np * 4));
     b.plan.cnt = reinterpret_cast<int32_t*>(take((size_t)(nl + 1) * 4));

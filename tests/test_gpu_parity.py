@@ -29,7 +29,7 @@ def _oracle_index(oracle, idx, x):
 def _oracle_search(oracle, idx, ox, q, k):
     t, _, codes, rc, corr, assign = ox
     p = idx.params
-    qr = oracle.rotate(t["Pi"], q)
+    qr = idx.rotate_queries(q)             # the search path's own query rotation
     return oracle.search(qr, M=p.M, B=p.B, Br=p.Br, c1d=t["c1d"], res_c1d=t["res_c1d"],
                          codes=codes, res=rc, corr=corr, assign=assign, cents=t["cents"], k=k,
                          alpha=p.alpha, nprobe=min(p.nprobe, p.nlist))
@@ -539,7 +539,7 @@ def test_per_subspace_residual_codebooks_bit_exact(jhq, oracle, cfg, tmp_path):
     orc, oco = oracle.encode_residual(yall, pc, M, 8, t["c1d"], t["res_c1d"], cfg["Br"],
                                       per_sub=True)
     assert np.array_equal(rc, orc) and np.array_equal(co, oco)
-    qr = oracle.rotate(t["Pi"], q)
+    qr = idx.rotate_queries(q)
     D2, I2 = oracle.search(qr, M=M, B=8, Br=cfg["Br"], c1d=t["c1d"], res_c1d=t["res_c1d"],
                            codes=pc, res=rc, corr=co, assign=asg, cents=t["cents"], k=10,
                            alpha=4.0, nprobe=min(cfg["nprobe"], cfg["nlist"]), per_sub=True)
@@ -549,3 +549,115 @@ def test_per_subspace_residual_codebooks_bit_exact(jhq, oracle, cfg, tmp_path):
     idx2 = jhq.JHQGpuIndex.load(path)
     assert idx2.residual_per_subspace
     _assert_same(*idx2.search(q, 10), D2, I2)
+
+
+@pytest.mark.parametrize("pool_pages,rerank", [(10**6, 0), (120, 0), (60, 16)])
+def test_list_paging_equals_resident_index(jhq, pool_pages, rerank):
+    """Out-of-core lists: codes in mapped host memory, staged per batch into a
+    device page pool (several waves when the pool is small); the results equal
+    the resident index's bit for bit, through the host and the device search,
+    with and without the exact rerank over host-resident vectors."""
+    import torch
+    d, M, nlist = 64, 16, 64
+    x = _data(20000, d, 71)
+    q = _data(300, d, 72)
+    p = jhq.Params(M=M, nlist=nlist, nprobe=6, batch_size=100, add_batch=7000)
+    ref = jhq.JHQGpuIndex(d, p)
+    ref.train(x[:5000])
+    pg = jhq.JHQGpuIndex(d, p)
+    pg.set_trained(**{kk: v for kk, v in ref.get_trained().items()})
+    page_bytes = 16 * 32 + 128                               # Mp = 16: 16 bytes per slot + slot id
+    pg.set_list_paging(pool_pages * page_bytes)
+    if rerank:
+        ref.set_rerank(rerank)
+        pg.set_rerank(rerank)
+    ref.add(x[:12000]); ref.add(x[12000:])
+    pg.add(x[:12000]); pg.add(x[12000:])
+    for k in (10, 4):
+        _assert_same(*pg.search(q, k), *ref.search(q, k))
+    tq = torch.from_numpy(q).cuda()
+    D = torch.empty((300, 10), dtype=torch.float32, device="cuda")
+    I = torch.empty((300, 10), dtype=torch.int32, device="cuda")
+    pg.search_device(tq.data_ptr(), 300, 10, D.data_ptr(), I.data_ptr(),
+                     torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    _assert_same(D.cpu().numpy(), I.cpu().numpy(), *ref.search(q, 10))
+    if pool_pages < 1000:
+        assert pg.paging_waves > 3 * 3                       # 3 batches per search, several waves each
+    assert np.array_equal(pg.get_codes()[1], ref.get_codes()[1])
+
+
+def test_list_paging_errors(jhq):
+    d = 32
+    x = _data(3000, d, 73)
+    flat = jhq.JHQGpuIndex(d, jhq.Params(M=8, nlist=1))
+    with pytest.raises(ValueError):
+        flat.set_list_paging(1 << 20)
+    idx = _build(jhq, d, jhq.Params(M=8, nlist=16, nprobe=4), x, x)
+    with pytest.raises(RuntimeError):
+        idx.set_list_paging(1 << 20)                         # after add
+    tiny = jhq.JHQGpuIndex(d, jhq.Params(M=8, nlist=16, nprobe=16))
+    tiny.train(x)
+    tiny.set_list_paging(3 * (32 * 16 + 128))                # 3 pages < one query's 16 lists
+    with pytest.raises(ValueError):
+        tiny.add(x)                                          # largest list exceeds the pool
+
+
+@pytest.mark.parametrize("refine", ["cta", "warp"])
+@pytest.mark.parametrize("cfg", [
+    dict(d=128, M=32, nlist=16, nprobe=4, R=0),       # short residual rows: lane per candidate
+    dict(d=1024, M=128, nlist=1, nprobe=1, R=0),      # long rows: warp per candidate
+    dict(d=128, M=32, nlist=16, nprobe=4, R=24),      # exact rerank, ck = 96
+])
+def test_refine_kernels_bit_exact(jhq, oracle, monkeypatch, refine, cfg):
+    """Both refine kernels (one CTA per query / one warp per query) give the
+    oracle's results bit for bit."""
+    monkeypatch.setenv("JHQ_REFINE", refine)
+    d = cfg["d"]
+    x = _data(5000, d, 81)
+    q = _data(77, d, 82)
+    p = jhq.Params(M=cfg["M"], nlist=cfg["nlist"], nprobe=cfg["nprobe"], batch_size=40)
+    idx = jhq.JHQGpuIndex(d, p)
+    idx.train(x[:3000])
+    if cfg["R"]:
+        idx.set_rerank(cfg["R"])
+    idx.add(x)
+    ox = _oracle_index(oracle, idx, x)
+    for k in (10, 3):
+        D, I = idx.search(q, k)
+        if cfg["R"]:
+            _, Ic = _oracle_search(oracle, idx, ox, q, max(cfg["R"], k))
+            D2, I2 = oracle.rerank(q, x, Ic, k)
+        else:
+            D2, I2 = _oracle_search(oracle, idx, ox, q, k)
+        _assert_same(D, I, D2, I2)
+
+
+@pytest.mark.parametrize("d,M", [(1024, 128), (128, 32), (104, 26)])
+def test_tensor_core_query_rotation(jhq, monkeypatch, d, M):
+    """Search-side query rotation on tcgen05 (bf16 three-term split): every output
+    within 2^-15 ||x|| of the exact fp32 chain (Pi is orthonormal, so its columns
+    have unit norm); JHQ_ROTATE=simt gives the exact chain itself. The end-to-end
+    effect on the returned ids is measured and reported."""
+    from jhq_gpu_b200 import datasets
+    if d == 1024:
+        x, q = datasets.make("c1", seed=0, n=12000, nq=200)
+    else:
+        x = _data(12000, d, 91)
+        q = _data(200, d, 92)
+    p = jhq.Params(M=M, nlist=1, nprobe=1, batch_size=64)
+    idx = _build(jhq, d, p, x[:6000], x)
+    y_exact = idx.rotate(q)
+    y_tc = idx.rotate_queries(q)
+    bound = 2.0 ** -15 * np.linalg.norm(q.astype(np.float64), axis=1, keepdims=True)
+    err = np.abs(y_tc.astype(np.float64) - y_exact)
+    assert (err <= bound).all(), float((err / bound).max())
+    D, I = idx.search(q, 10)
+    monkeypatch.setenv("JHQ_ROTATE", "simt")
+    idx2 = _build(jhq, d, p, x[:6000], x)
+    assert np.array_equal(idx2.rotate_queries(q), idx2.rotate(q))
+    D2, I2 = idx2.search(q, 10)
+    same = np.mean([len(set(a) & set(b)) / 10.0 for a, b in zip(I, I2)])
+    print(f"d={d}: max |err| / bound {float((err / bound).max()):.3f}, "
+          f"returned ids shared with the fp32 rotation {same:.4f}")
+    assert same >= 0.99

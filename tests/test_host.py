@@ -157,3 +157,39 @@ def test_recall_at_k_matches_reference_definition():
     assert recall_at_k(labels, gt, 3) == 3 / 6          # 1, 3 found; 8 found
     assert recall_at_k(labels, gt[:, :1], 3) == 2 / 6   # gt_k = 1: only 3 and 8
     assert recall_at_k(labels[:, :2], gt, 2) == 2 / 4
+
+
+def test_vector_file_formats_roundtrip(tmp_path):
+    """.fvecs / .ivecs / .bvecs / .i8bin readers (the reference demos' inputs,
+    common/fvecs_io.cuh, bvecs_io.cuh, spacev_io.cuh): row ranges, padding,
+    and errors on ragged or truncated files."""
+    from jhq_gpu_b200 import vecio
+    rng = np.random.default_rng(5)
+    f = rng.standard_normal((37, 12)).astype(np.float32)
+    i = rng.integers(0, 1000, (37, 10)).astype(np.int32)
+    b = rng.integers(0, 256, (37, 16)).astype(np.uint8)
+    s = rng.integers(-128, 128, (37, 100)).astype(np.int8)
+    vecio.write_vecs(str(tmp_path / "a.fvecs"), f)
+    vecio.write_vecs(str(tmp_path / "a.ivecs"), i)
+    vecio.write_vecs(str(tmp_path / "a.bvecs"), b)
+    vecio.write_i8bin(str(tmp_path / "a.i8bin"), s)
+    assert vecio.vecs_shape(str(tmp_path / "a.fvecs")) == (37, 12)
+    assert np.array_equal(vecio.read_vecs(str(tmp_path / "a.fvecs")), f)
+    assert np.array_equal(vecio.read_vecs(str(tmp_path / "a.ivecs"), 5, 7), i[5:12])
+    assert np.array_equal(vecio.read_vecs(str(tmp_path / "a.bvecs"), 30), b[30:].astype(np.float32))
+    r = vecio.read_i8bin(str(tmp_path / "a.i8bin"), 3, 4, pad_to=104)
+    assert r.shape == (4, 104) and np.array_equal(r[:, :100], s[3:7]) and not r[:, 100:].any()
+    blocks = list(vecio.iter_rows(str(tmp_path / "a.bvecs"), block=10))
+    assert [len(x) for x in blocks] == [10, 10, 10, 7]
+    raw = open(tmp_path / "a.fvecs", "rb").read()
+    open(tmp_path / "bad.fvecs", "wb").write(raw[:-3])               # truncated
+    with pytest.raises(ValueError):
+        vecio.read_vecs(str(tmp_path / "bad.fvecs"))
+    rag = bytearray(raw)
+    rag[52:56] = np.int32(11).tobytes()                              # second record's dim
+    open(tmp_path / "rag.fvecs", "wb").write(bytes(rag))
+    with pytest.raises(ValueError):
+        vecio.read_vecs(str(tmp_path / "rag.fvecs"))
+    open(tmp_path / "t.i8bin", "wb").write(np.array([37, 100], np.int32).tobytes() + b"\0" * 10)
+    with pytest.raises(ValueError):
+        vecio.read_i8bin(str(tmp_path / "t.i8bin"))

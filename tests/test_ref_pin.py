@@ -81,7 +81,7 @@ def _pin(jhq, version, x, q, *, d, M, nlist=1, nprobe=1, batch=64, k=10, n_train
     idx.add(x)
     t = idx.get_trained()
     y = idx.rotate(x)
-    qr = idx.rotate(q)
+    qr = idx.rotate_queries(q)                  # the rotation search() applies
     rpc, rrc, rco, Dr, Ir = ref.pin(y, qr, M=M, c1d=t["c1d"], res_c1d=t["res_c1d"],
                                     cents=t["cents"], sigma=t["sigma"], k=k, nlist=nlist,
                                     nprobe=nprobe, batch=batch)
