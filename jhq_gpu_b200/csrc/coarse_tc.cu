@@ -45,6 +45,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -98,13 +99,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of parity `parity`; gives up (false) when the
-// CTA's abort flag is set or after TC_WAIT_CYCLES, which sets the flag.
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// CTA's abort flag is set or after `limit` cycles, which sets the flag. The
+// pipeline waits use the launch's limit (TC_WAIT_CYCLES unless a test shortens
+// it); the drain waits (abort == nullptr) always use TC_WAIT_CYCLES.
+__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                          long long limit = TC_WAIT_CYCLES) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(bar, parity)) {
         if (abort && *abort) return false;
-        if (clock64() - t0 > TC_WAIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             atomicExch(&g_tc_error, 1);
             if (abort) *abort = 1;
             return false;
@@ -137,7 +141,8 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __global__ void __launch_bounds__(TC_THREADS, 1)
 coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_c,
                  const float* __restrict__ norms, float* __restrict__ scores,
-                 float* __restrict__ tile_min, int nq, int nlist, int K, int mt, int ntiles) {
+                 float* __restrict__ tile_min, int nq, int nlist, int K, int mt, int ntiles,
+                 long long wait_limit) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* epi = (float*)(smem + TC_STAGES * TC_STAGE_BYTES);
@@ -177,7 +182,7 @@ coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
                 for (int kc = 0; kc < nk; ++kc, ++it) {
                     const int s = it % TC_STAGES;
                     if (it >= TC_STAGES &&
-                        !mbar_wait(empty0 + 8 * s, ((it / TC_STAGES) - 1) & 1, abort))
+                        !mbar_wait(empty0 + 8 * s, ((it / TC_STAGES) - 1) & 1, abort, wait_limit))
                         break;
                     const uint32_t fb = full0 + 8 * s;
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
@@ -196,13 +201,17 @@ coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
             int it = 0, i = 0;
             for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++i) {
                 const int acc = i & 1;
-                if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort)) break;
+                if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort, wait_limit))
+                    break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d_tmem = tmem + (uint32_t)(acc * TC_BN);
                 bool ok = true;
                 for (int kc = 0; kc < nk; ++kc, ++it) {
                     const int s = it % TC_STAGES;
-                    if (!mbar_wait(full0 + 8 * s, (it / TC_STAGES) & 1, abort)) { ok = false; break; }
+                    if (!mbar_wait(full0 + 8 * s, (it / TC_STAGES) & 1, abort, wait_limit)) {
+                        ok = false;
+                        break;
+                    }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a_s = smem_u32(smem + s * TC_STAGE_BYTES);
                     const uint64_t da = sw128_desc(a_s), db = sw128_desc(a_s + TC_A_BYTES);
@@ -232,7 +241,7 @@ coarse_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constan
         int i = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
             const int acc = i & 1;
-            const bool ok = mbar_wait(tfull0 + 8 * acc, (i >> 1) & 1, abort);
+            const bool ok = mbar_wait(tfull0 + 8 * acc, (i >> 1) & 1, abort, wait_limit);
             if (!__all_sync(0xffffffffu, ok)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * TC_BN;
@@ -434,8 +443,13 @@ void coarse_scores_tc(const uint16_t* q3, int nq, const uint16_t* c3, const floa
     const CUtensorMap mq = make_map(q3, nq, K3, TC_BM);
     const CUtensorMap mc = make_map(c3, nlist, K3, TC_BN);
     const int grid = (int)std::min<int64_t>(ntiles, nsm);
+    // Test hook: JHQ_TEST_TC_WAIT_CYCLES shortens the pipeline waits of the
+    // kernels launched (or captured) from now on, so that a test can make a wait
+    // give up and check the JHQ_ETIMEDOUT report; the drain waits keep their limit.
+    long long wait_limit = TC_WAIT_CYCLES;
+    if (const char* e = std::getenv("JHQ_TEST_TC_WAIT_CYCLES")) wait_limit = std::atoll(e);
     coarse_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(mq, mc, norms, scores, tile_min, nq, nlist,
-                                                       K3, mt, (int)ntiles);
+                                                       K3, mt, (int)ntiles, wait_limit);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -374,7 +374,10 @@ select_probes_margin_warp_kernel(const float* __restrict__ s, const float* __res
     for (int i = m + lane; i < P3; i += 32) cb[i] = KEY_EMPTY;
     __syncwarp();
     warp_bitonic_sort(cb, P3, lane);
-    for (int p = lane; p < nprobe; p += 32) out[p] = key_id(cb[p]);
+    for (int p = lane; p < nprobe; p += 32) {
+        const uint64_t e = cb[p];                          // never -1: a list id in range
+        out[p] = (e == KEY_EMPTY) ? 0 : key_id(e);
+    }
 }
 
 // 4-pass 8-bit radix select of the nprobe-th key, then the winners (ties at

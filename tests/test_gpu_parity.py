@@ -661,3 +661,27 @@ def test_tensor_core_query_rotation(jhq, monkeypatch, d, M):
     print(f"d={d}: max |err| / bound {float((err / bound).max()):.3f}, "
           f"returned ids shared with the fp32 rotation {same:.4f}")
     assert same >= 0.99
+
+
+def test_coarse_wait_timeout_is_reported_and_the_index_recovers(jhq, monkeypatch):
+    """The tcgen05 kernel's pipeline waits are bounded. A test-only setting
+    (JHQ_TEST_TC_WAIT_CYCLES, read when the kernel is launched or captured)
+    shortens them to zero cycles, so the first wait that is not already
+    satisfied gives up: the kernel flags the error, drains its own copies and
+    MMAs with full-length waits, frees its TMEM and returns. The search reports
+    JHQ_ETIMEDOUT, and once the graph is captured again with the normal limit
+    the next search is correct. No GPU fault is involved."""
+    d = 128
+    x = _data(8000, d, 95)
+    q = _data(300, d, 96)
+    idx = _build(jhq, d, jhq.Params(M=32, nlist=64, nprobe=8, batch_size=256), x[:4000], x)
+    D0, I0 = idx.search(q, 10)
+    monkeypatch.setenv("JHQ_TEST_TC_WAIT_CYCLES", "0")
+    idx.set_nprobe(8)                                  # re-capture with the short waits
+    with pytest.raises(jhq.JHQError) as e:
+        idx.search(q, 10)
+    assert e.value.code == jhq.JHQ_ETIMEDOUT
+    monkeypatch.delenv("JHQ_TEST_TC_WAIT_CYCLES")
+    idx.set_nprobe(8)
+    _assert_same(*idx.search(q, 10), D0, I0)
+    idx.check_device_status()                          # the flag was cleared by the report
