@@ -236,7 +236,8 @@ refine_warp_kernel(RefineArgs a) {
         n += __popc(m2);
         __syncwarp();
     }
-    int P = 32;
+    // pad to at least ck_pad: buf[0..ck) is read below even when fewer keys came in
+    int P = a.ck_pad;
     while (P < n) P <<= 1;
     for (int t = n + lane; t < P; t += 32) buf[t] = KEY_EMPTY;
     __syncwarp();

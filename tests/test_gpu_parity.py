@@ -551,7 +551,7 @@ def test_per_subspace_residual_codebooks_bit_exact(jhq, oracle, cfg, tmp_path):
     _assert_same(*idx2.search(q, 10), D2, I2)
 
 
-@pytest.mark.parametrize("pool_pages,rerank", [(10**6, 0), (120, 0), (60, 16)])
+@pytest.mark.parametrize("pool_pages,rerank", [(10**6, 0), (120, 0), (160, 16)])
 def test_list_paging_equals_resident_index(jhq, pool_pages, rerank):
     """Out-of-core lists: codes in mapped host memory, staged per batch into a
     device page pool (several waves when the pool is small); the results equal
