@@ -194,12 +194,13 @@ int jhq_get_codes(const jhq_index* idx, uint8_t* primary, uint8_t* residual,
 /* JL rotation y = Pi x of host rows (jhq_gpu_index.cu:209-225). */
 int jhq_rotate(jhq_index* idx, const float* x, int64_t n, float* y);
 
-/* The rotation search() applies to queries (search.cu:338-339): on B200 a
- * tcgen05 GEMM on a bf16 three-term split (x = hi + lo + r, |r| <= 2^-18 |x|;
- * the products hi.hi, hi.lo, lo.hi accumulated in fp32, so |error| <=
- * 2^-16 |x| |Pi col| per output), unless JHQ_ROTATE=simt selects the exact fp32
- * chains of jhq_rotate. Database rows (add/train) always use jhq_rotate's path.
- * Exposed so that a checker can search with the very same rotated queries. */
+/* The rotation search() applies to queries (search.cu:338-339). For indexes
+ * whose batch_size is >= 1024 it is a tcgen05 GEMM on a bf16 three-term split
+ * (x = hi + lo + r, |r| <= 2^-18 |x|; the products hi.hi, hi.lo, lo.hi
+ * accumulated in fp32, so |error| <= 2^-16 |x| |Pi col| per output); smaller
+ * batches use the exact fp32 chains of jhq_rotate (JHQ_ROTATE=simt|tc forces
+ * either). Database rows (add/train) always use jhq_rotate's path. Exposed so
+ * that a checker can search with the very same rotated queries. */
 int jhq_rotate_queries(jhq_index* idx, const float* x, int64_t n, float* y);
 
 /* Encode already-rotated host rows with the index's codebooks without adding

@@ -49,6 +49,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "device_utils.cuh"
 #include "jhq_common.h"
 #include "kernels.cuh"
 
@@ -462,6 +463,438 @@ int coarse_tc_error(bool clear) {
         JHQ_CUDA(cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int)));
     }
     return v;
+}
+
+
+namespace {
+
+// ===========================================================================
+// Flat ADC scan on the tensor cores for 1-bit codes (K1D = 2: B = 8, Ds = 8).
+//
+// With two codewords c0 < c1 per dimension and b_j in {0, 1} the bit of dim j,
+//   s_v = sum_j (q_j - c[b_j])^2 = S0 + D * pop(v) - 2 e * (q . b_v),
+//   S0 = sum_j (q_j - c0)^2,  D = c1^2 - c0^2,  e = c1 - c0,  pop = popcount,
+// so the ADC distance of every (vector, query) pair is one GEMM of the code
+// bits with the queries. flat_tc_kernel computes g = q . b on tcgen05: the A
+// operand (128 vectors x 64 dims per K chunk) is expanded from the code bytes
+// to bf16 0/1 in shared memory by four warps (the 128-byte swizzled K-major
+// layout the TMA would produce: row r at r*128 bytes, 16-byte chunk c stored
+// at c ^ (r & 7)); the B operand is the query block split in bf16 hi / lo
+// planes (TMA); the two MMAs per K step accumulate q_hi.b + q_lo.b in fp32
+// TMEM. The epilogue forms s~ = S0 + D pop - 2 e g, stores it [q][v] and the
+// per-query minimum of each 128-vector tile. The scores are approximate;
+// flat_select (below) turns them into the exact top-ck of the LUT-path keys.
+// Same bounded-wait / abort / drain discipline as coarse_tc_kernel.
+constexpr int FT_BM = 128, FT_BK = 64;
+constexpr int FT_THREADS = 9 * 32;            // warps 0-3 expand A (+TMA), 4 MMA, 5-8 epilogue
+constexpr int FT_A_BYTES = FT_BM * FT_BK * 2; // 16 KB
+
+__host__ __device__ inline int ft_stages(int N) { return N <= 64 ? 4 : 3; }
+__host__ __device__ inline int ft_stage_bytes(int N) { return FT_A_BYTES + 2 * N * FT_BK * 2; }
+__host__ __device__ inline int ft_smem_bytes(int N) { return ft_stages(N) * ft_stage_bytes(N) + 1024 + 256; }
+
+__global__ void __launch_bounds__(FT_THREADS, 1)
+flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restrict__ codes,
+               const int32_t* __restrict__ pop, const float* __restrict__ S0, int nvec, int M,
+               int nq, int N, float Dc, float ec, float* __restrict__ scores,
+               uint32_t* __restrict__ tile_min, int ntiles, long long wait_limit) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int S = ft_stages(N), SB = ft_stage_bytes(N);
+    uint64_t* bars = (uint64_t*)(smem + S * SB);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 4 + 1);
+    volatile int* abort = (volatile int*)(tmem_slot + 1);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int d = M * 8, nk = d / FT_BK;
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, tfull0 = empty0 + 8 * S,
+                   tempty0 = tfull0 + 16, drain = tempty0 + 16;
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+                           ((uint32_t)(FT_BM >> 4) << 24);
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(2 * N)) cols <<= 1;
+    if (tid == 0) {
+        for (int i = 0; i < 2 * S + 5; ++i) {
+            const uint32_t a = full0 + 8 * i;
+            uint32_t cnt = 1;
+            if (a < empty0) cnt = 128 + 1;                 // 128 expanders + the TMA arrive
+            else if (a >= tempty0 && a < drain) cnt = 128; // epilogue threads
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(a), "r"(cnt));
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *abort = 0;
+    }
+    if (warp == 4) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     :: "r"(smem_u32(tmem_slot)), "r"(cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 4) {                                        // A expansion (+ B by TMA)
+        const int r = tid;                                 // tile row = vector
+        int it = 0;
+        bool stop = false;
+        for (int t = blockIdx.x; t < ntiles && !stop && !*abort; t += gridDim.x) {
+            const int v = t * FT_BM + r;
+            const uint8_t* vc = codes + (int64_t)v * M;
+            for (int kc = 0; kc < nk; ++kc, ++it) {
+                const int s = it % S;
+                if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) - 1) & 1, abort, wait_limit)) {
+                    stop = true;
+                    break;
+                }
+                uint8_t* st = smem + s * SB;
+                if (r == 0) {
+                    const uint32_t fb = full0 + 8 * s;
+                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                                 :: "r"(fb), "r"((uint32_t)(2 * N * FT_BK * 2)) : "memory");
+                    const uint32_t b_s = smem_u32(st + FT_A_BYTES);
+                    tma_load_2d(b_s, &map_q, kc * FT_BK, 0, fb);                       // q_hi
+                    tma_load_2d(b_s + N * FT_BK * 2, &map_q, kc * FT_BK, N, fb);       // q_lo
+                }
+                uint2 cw = make_uint2(0u, 0u);
+                if (v < nvec) cw = __ldg(reinterpret_cast<const uint2*>(vc + kc * 8));
+                uint8_t* row = st + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t byte = ((i < 4 ? cw.x : cw.y) >> ((i & 3) * 8)) & 0xFFu;
+                    uint32_t w[4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h)
+                        w[h] = (((byte >> (2 * h)) & 1u) ? 0x3F80u : 0u) |
+                               (((byte >> (2 * h + 1)) & 1u) ? 0x3F800000u : 0u);
+                    *reinterpret_cast<uint4*>(row + ((i ^ (r & 7)) << 4)) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(full0 + 8 * s)
+                             : "memory");
+            }
+        }
+        // every stage this thread armed must complete (its TMA bytes) before exit
+        if (r == 0 && *abort)
+            for (int j = it > S ? it - S : 0; j < it; ++j)
+                mbar_wait(full0 + 8 * (j % S), (j / S) & 1, nullptr);
+    } else if (warp == 4) {
+        if (lane == 0) {                                   // MMA issuer
+            int it = 0, i = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++i) {
+                const int acc = i & 1;
+                if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort, wait_limit))
+                    break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * N);
+                bool ok = true;
+                for (int kc = 0; kc < nk; ++kc, ++it) {
+                    const int s = it % S;
+                    if (!mbar_wait(full0 + 8 * s, (it / S) & 1, abort, wait_limit)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a_s = smem_u32(smem + s * SB);
+                    const uint64_t da = sw128_desc(a_s);
+                    const uint64_t dh = sw128_desc(a_s + FT_A_BYTES);
+                    const uint64_t dl = sw128_desc(a_s + FT_A_BYTES + N * FT_BK * 2);
+#pragma unroll
+                    for (int k = 0; k < FT_BK / 16; ++k) {
+                        const uint32_t accum = (kc | k) != 0;
+                        asm volatile(
+                            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(dh + 2 * k), "r"(idesc), "r"(accum));
+                        asm volatile(
+                            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(dl + 2 * k), "r"(idesc), "r"(1u));
+                    }
+                    mma_commit(empty0 + 8 * s);
+                }
+                if (!ok) break;
+                mma_commit(tfull0 + 8 * acc);
+            }
+            mma_commit(drain);
+            mbar_wait(drain, 0, nullptr);
+        }
+    } else {                                               // epilogue, warps 5-8
+        const int q4 = warp & 3;          // TMEM lane quarter: a warp reads lanes 32 (warp % 4) ..
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            const int acc = i & 1;
+            const bool ok = mbar_wait(tfull0 + 8 * acc, (i >> 1) & 1, abort, wait_limit);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int v = t * FT_BM + q4 * 32 + lane;
+            const float pv = v < nvec ? (float)__ldg(pop + v) : 0.0f;
+            for (int cb = 0; cb < N; cb += 32) {
+                uint32_t rg[32];
+                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * N + cb);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3]), "=r"(rg[4]), "=r"(rg[5]),
+                      "=r"(rg[6]), "=r"(rg[7]), "=r"(rg[8]), "=r"(rg[9]), "=r"(rg[10]), "=r"(rg[11]),
+                      "=r"(rg[12]), "=r"(rg[13]), "=r"(rg[14]), "=r"(rg[15]), "=r"(rg[16]), "=r"(rg[17]),
+                      "=r"(rg[18]), "=r"(rg[19]), "=r"(rg[20]), "=r"(rg[21]), "=r"(rg[22]), "=r"(rg[23]),
+                      "=r"(rg[24]), "=r"(rg[25]), "=r"(rg[26]), "=r"(rg[27]), "=r"(rg[28]), "=r"(rg[29]),
+                      "=r"(rg[30]), "=r"(rg[31])
+                    : "r"(taddr));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int q = cb + c;
+                    if (q >= nq) break;                                 // warp-uniform
+                    const float g = __uint_as_float(rg[c]);
+                    const float sv = __fmaf_rn(-2.0f * ec, g, __fmaf_rn(Dc, pv, __ldg(S0 + q)));
+                    if (v < nvec) scores[(int64_t)q * nvec + v] = sv;
+                    float m = v < nvec ? sv : __int_as_float(0x7f800000);
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    if (lane == 0)
+                        atomicMin(tile_min + (int64_t)q * ntiles + t, float_order(m));
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(tempty0 + 8 * acc)
+                         : "memory");
+        }
+    }
+    __syncwarp();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 4)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(cols));
+}
+
+
+// Per query block row q < nq: the bf16 hi / lo planes q2[0][q], q2[1][q] (rows
+// nq..N-1 zero) and S0[q] = sum_j (q_j - c0)^2 (a per-query constant: its
+// rounding shifts every s~ of the query alike and cancels in the selection).
+__global__ void flat_prep_kernel(const float* __restrict__ q_rot, int nq, int N, int d, float c0,
+                                 uint16_t* __restrict__ q2, float* __restrict__ S0) {
+    const int q = blockIdx.x;
+    float acc = 0.0f;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        const float x = q < nq ? q_rot[(int64_t)q * d + j] : 0.0f;
+        const uint16_t hi = bf16_rne(__float_as_uint(x));
+        const uint16_t lo = bf16_rne(__float_as_uint(x - __uint_as_float((uint32_t)hi << 16)));
+        q2[(int64_t)q * d + j] = hi;
+        q2[((int64_t)N + q) * d + j] = lo;
+        const float t = x - c0;
+        acc = __fmaf_rn(t, t, acc);
+    }
+    __shared__ float red[32];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0 && q < nq) {
+        float tot = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        S0[q] = tot;
+    }
+}
+
+// Exact top-ck from the approximate scores, one warp per query:
+//   tau = ck-th smallest tile minimum of s~ (ck distinct vectors have s~ <= tau);
+//   every exact top-ck member has s~ <= tau + 2E (E bounds |s~ - s| per vector
+//   up to a per-query constant), so only tiles whose minimum is <= tau + 2E are
+//   read, their vectors with s~ <= tau + 2E are rescored with the scan's own
+//   arithmetic (nibble tables lo + hi, in-order sum over m: the oracle's key),
+//   and the exact top-ck by (distance, id) is written as the query's single
+//   candidate slot for the refine.
+constexpr int FS_WARPS = 4;
+constexpr int FS_CAP = 512;                  // exact keys held before a compaction (>= ck_pad + 32)
+constexpr int FS_TILES = 4096;               // tile minima a warp sorts (nvec <= 524,288)
+
+__host__ __device__ inline size_t fs_warp_bytes(int M, int ntiles_pad) {
+    return (size_t)M * 32 * 4 + (size_t)(FS_CAP + ntiles_pad) * 8 + 32 * 4;
+}
+
+__global__ void __launch_bounds__(FS_WARPS * 32)
+flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1d_g,
+                   const uint8_t* __restrict__ codes, const float* __restrict__ scores,
+                   const uint32_t* __restrict__ tile_min, int nvec, int M, int nq, int ck,
+                   int ck_pad, int ntiles, int ntiles_pad, float cmax, float ec, float Dc,
+                   uint64_t* __restrict__ cand, uint64_t* __restrict__ gthr,
+                   int64_t* __restrict__ qslot_off) {
+    extern __shared__ __align__(16) unsigned char fs_smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int q = blockIdx.x * FS_WARPS + warp;
+    if (q >= nq) return;
+    unsigned char* wb = fs_smem + warp * fs_warp_bytes(M, ntiles_pad);
+    float* tab = reinterpret_cast<float*>(wb);                       // [M][32]
+    uint64_t* buf = reinterpret_cast<uint64_t*>(wb + (size_t)M * 32 * 4);
+    uint64_t* tk = buf + FS_CAP;                                       // [ntiles_pad]
+    int* stage = reinterpret_cast<int*>(tk + ntiles_pad);              // 32 candidates
+    const int d = M * 8;
+    const float* qv = q_rot + (int64_t)q * d;
+    const float c0 = c1d_g[0], c1 = c1d_g[1];
+
+    // error bound (all but per-query constants): LUT-path rounding of s, the
+    // bf16 split and fp32 tensor accumulation of g, and the roundings forming s~
+    float V = 0.0f, L1 = 0.0f, S0 = 0.0f;
+    for (int j = lane; j < d; j += 32) {
+        const float x = qv[j], a = fabsf(x) + cmax, t = x - c0;
+        V += a * a;
+        L1 += fabsf(x);
+        S0 += t * t;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        V += __shfl_xor_sync(0xffffffffu, V, o);
+        L1 += __shfl_xor_sync(0xffffffffu, L1, o);
+        S0 += __shfl_xor_sync(0xffffffffu, S0, o);
+    }
+    const float u = 5.9604645e-08f;                                    // 2^-24
+    const float aD = fabsf(Dc), ae = fabsf(ec);
+    const float E = 1.1f * (V * 1.001f * (float)(2 * M + 16) * u + aD * (float)d * u +
+                            2.0f * ae * L1 * (3.8146973e-06f + (float)(2 * d) * 1.1920929e-07f) +
+                            2.0f * u * (S0 + aD * (float)d + 2.0f * ae * L1) * 1.001f);
+
+    // tau from the sorted tile minima
+    for (int i = lane; i < ntiles_pad; i += 32)
+        tk[i] = i < ntiles ? (((uint64_t)tile_min[(int64_t)q * ntiles + i] << 32) | (uint32_t)i)
+                           : KEY_EMPTY;
+    // the query's nibble tables (the scan's mode-1 tables: lo dims 0-3, hi 4-7)
+    for (int i = lane; i < M * 32; i += 32) {
+        const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
+        float acc = 0.0f;
+        for (int k = 0; k < 4; ++k) {
+            const float diff = qv[m * 8 + half * 4 + k] - ((n >> k) & 1 ? c1 : c0);
+            acc = __fmaf_rn(diff, diff, acc);
+        }
+        tab[i] = acc;
+    }
+    __syncwarp();
+    warp_bitonic_sort(tk, ntiles_pad, lane);
+    const float tau = ck <= ntiles ? order_float((uint32_t)(tk[ck - 1] >> 32)) : __int_as_float(0x7f800000);
+    const float T = __fadd_ru(tau, 2.0f * E);
+
+    int n = 0;
+    const float* srow = scores + (int64_t)q * nvec;
+    for (int ti = 0; ti < ntiles; ++ti) {
+        const uint64_t tkey = tk[ti];
+        if (tkey == KEY_EMPTY || !(order_float((uint32_t)(tkey >> 32)) <= T)) break;
+        const int t = (int)(uint32_t)tkey;
+        for (int r0 = 0; r0 < FT_BM; r0 += 32) {
+            const int v = t * FT_BM + r0 + lane;
+            const bool in = v < nvec && srow[v] <= T;
+            const unsigned mk = __ballot_sync(0xffffffffu, in);
+            if (!mk) continue;
+            if (in) stage[__popc(mk & ((1u << lane) - 1u))] = v;
+            __syncwarp();
+            const int cnt = __popc(mk);
+            uint64_t key = KEY_EMPTY;
+            if (lane < cnt) {                                          // exact key, lane per candidate
+                const int id = stage[lane];
+                const uint4* cv = reinterpret_cast<const uint4*>(codes + (int64_t)id * M);
+                float dist = 0.0f;
+                for (int g = 0; g < M / 16; ++g) {
+                    const uint4 w4 = __ldg(cv + g);
+                    const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                        for (int bb = 0; bb < 4; ++bb) {
+                            const int m = g * 16 + wi * 4 + bb;
+                            const uint32_t b = (ws[wi] >> (bb * 8)) & 0xFFu;
+                            dist = __fadd_rn(dist, __fadd_rn(tab[m * 32 + (b & 15u)],
+                                                              tab[m * 32 + 16 + (b >> 4)]));
+                        }
+                }
+                key = make_key(dist, id);
+            }
+            __syncwarp();
+            const unsigned mk2 = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
+            if (n + __popc(mk2) > FS_CAP) {                            // keep the best ck_pad
+                for (int i = n + lane; i < FS_CAP; i += 32) buf[i] = KEY_EMPTY;
+                __syncwarp();
+                warp_bitonic_sort(buf, FS_CAP, lane);
+                n = ck_pad;
+            }
+            if (key != KEY_EMPTY) buf[n + __popc(mk2 & ((1u << lane) - 1u))] = key;
+            n += __popc(mk2);
+            __syncwarp();
+        }
+    }
+    int P = ck_pad;
+    while (P < n) P <<= 1;
+    for (int i = n + lane; i < P; i += 32) buf[i] = KEY_EMPTY;
+    __syncwarp();
+    warp_bitonic_sort(buf, P, lane);
+    for (int i = lane; i < ck; i += 32) cand[(int64_t)q * ck + i] = buf[i];
+    if (lane == 0) {
+        gthr[q] = buf[ck - 1];
+        qslot_off[q + 1] = q + 1;
+        if (q == 0) qslot_off[0] = 0;
+    }
+}
+
+}  // namespace
+
+bool flat_tc_supported(int d, int M, int B, int nvec) {
+    return M > 0 && d == 8 * M && B == 8 && M % 16 == 0 && nvec > 0 &&
+           (nvec + FT_BM - 1) / FT_BM <= FS_TILES;
+}
+
+size_t flat_tc_scratch_bytes(int Bq, int d, int nvec) {
+    const int Nb = std::min(128, (Bq + 31) / 32 * 32);
+    const int ntiles = (nvec + FT_BM - 1) / FT_BM;
+    return (size_t)2 * Nb * d * 2 + 256 + (size_t)Bq * 4 + 256 + (size_t)Bq * nvec * 4 + 256 +
+           (size_t)Bq * ntiles * 4 + 256;
+}
+
+void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
+    if (a.nq <= 0) return;
+    const int d = a.M * 8, ntiles = (a.nvec + FT_BM - 1) / FT_BM;
+    int ntiles_pad = 32;
+    while (ntiles_pad < ntiles) ntiles_pad <<= 1;
+    const int Nb = std::min(128, (a.nq + 31) / 32 * 32);
+    // scratch carve: q2 [2][Nb][d] bf16, S0 [nq], scores [nq][nvec], tile_min [nq][ntiles]
+    unsigned char* p = reinterpret_cast<unsigned char*>(a.scratch);
+    auto take = [&](size_t bytes) { unsigned char* r = p; p += (bytes + 255) & ~size_t(255); return r; };
+    uint16_t* q2 = reinterpret_cast<uint16_t*>(take((size_t)2 * Nb * d * 2));
+    float* S0 = reinterpret_cast<float*>(take((size_t)a.nq * 4));
+    float* scores = reinterpret_cast<float*>(take((size_t)a.nq * a.nvec * 4));
+    uint32_t* tmin = reinterpret_cast<uint32_t*>(take((size_t)a.nq * ntiles * 4));
+    JHQ_CUDA(cudaMemsetAsync(tmin, 0xFF, (size_t)a.nq * ntiles * 4, s));
+    static std::atomic<uint64_t> attr{0};
+    once_per_device(attr, [] {
+        JHQ_CUDA(cudaFuncSetAttribute(flat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      ft_smem_bytes(128)));
+        JHQ_CUDA(cudaFuncSetAttribute(flat_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      227 * 1024));
+    });
+    int dev = 0, nsm = 0;
+    JHQ_CUDA(cudaGetDevice(&dev));
+    JHQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    long long wait_limit = TC_WAIT_CYCLES;
+    if (const char* e = std::getenv("JHQ_TEST_TC_WAIT_CYCLES")) wait_limit = std::atoll(e);
+    const float c0 = a.c1d_host[0], c1 = a.c1d_host[1];
+    const float Dc = c1 * c1 - c0 * c0, ec = c1 - c0;
+    const float cmax = std::max(std::fabs(c0), std::fabs(c1));
+    for (int q0 = 0; q0 < a.nq; q0 += 128) {
+        const int nqb = std::min(128, a.nq - q0);
+        const int N = (nqb + 31) / 32 * 32;        // the epilogue reads 32 TMEM columns at a time
+        flat_prep_kernel<<<N, 256, 0, s>>>(a.q_rot + (int64_t)q0 * d, nqb, N, d, c0, q2, S0 + q0);
+        JHQ_LAUNCH_CHECK();
+        const CUtensorMap mq = make_map(q2, 2 * N, d, N);
+        const int grid = std::min(ntiles, nsm);
+        flat_tc_kernel<<<grid, FT_THREADS, ft_smem_bytes(N), s>>>(
+            mq, a.codes, a.pop, S0 + q0, a.nvec, a.M, nqb, N, Dc, ec, scores + (int64_t)q0 * a.nvec,
+            tmin + (int64_t)q0 * ntiles, ntiles, wait_limit);
+        JHQ_LAUNCH_CHECK();
+        count_launch(2);
+    }
+    const size_t smem = (size_t)FS_WARPS * fs_warp_bytes(a.M, ntiles_pad);
+    if (smem > 227 * 1024) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
+    flat_select_kernel<<<(unsigned)ceil_div(a.nq, FS_WARPS), FS_WARPS * 32, smem, s>>>(
+        a.q_rot, a.c1d, a.codes, scores, tmin, a.nvec, a.M, a.nq, a.ck, a.ck_pad, ntiles,
+        ntiles_pad, cmax, ec, Dc, a.cand, a.gthr, a.qslot_off);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
 }
 
 }  // namespace jhq

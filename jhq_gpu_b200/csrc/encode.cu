@@ -101,6 +101,15 @@ __global__ void scatter_pages_kernel(const int32_t* __restrict__ slot_ids, int64
 
 __global__ void set_int_kernel(int* dst, int value) { *dst = value; }
 
+__global__ void popcount_kernel(const uint8_t* __restrict__ codes, int64_t n, int M,
+                                int32_t* __restrict__ pop) {
+    const int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (v >= n) return;
+    int c = 0;
+    for (int m = 0; m < M; ++m) c += __popc((unsigned)codes[v * M + m]);
+    pop[v] = c;
+}
+
 __global__ void scale_kernel(float* __restrict__ v, int64_t n, float f) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) v[i] = __fmul_rn(v[i], f);
@@ -110,6 +119,13 @@ __global__ void scale_kernel(float* __restrict__ v, int64_t n, float f) {
 
 void set_int(int* dst, int value, cudaStream_t s) {
     set_int_kernel<<<1, 1, 0, s>>>(dst, value);
+    JHQ_LAUNCH_CHECK();
+    count_launch();
+}
+
+void popcount_rows(const uint8_t* codes, int64_t n, int M, int32_t* pop, cudaStream_t s) {
+    if (n <= 0) return;
+    popcount_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(codes, n, M, pop);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

@@ -87,6 +87,14 @@ void Index::rotate_device(const float* d_x, int64_t n, float* d_y, cudaStream_t 
     gemm_rows(d_x, dPi_.get(), d_y, n, d_, d_, EPI_STORE, nullptr, s);
 }
 
+bool Index::flat_tc() const {
+    const char* e = std::getenv("JHQ_FLAT");
+    if (e && std::string(e) == "simt") return false;
+    return p_.nlist == 1 && bpd_ == 1 && ntotal_ > 0 && dpop_.size() >= (size_t)ntotal_ &&
+           flat_tc_supported(d_, M_, B_, (int)std::min<int64_t>(ntotal_, INT32_MAX)) &&
+           !paging();
+}
+
 size_t Index::rotq_scratch_floats(int Bq) const {
     if (!rot_tc_) return 0;
     const size_t q3f = (((size_t)Bq * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63;
@@ -141,8 +149,14 @@ void Index::upload_trained() {
     // s~ = 0 - 2 x . Pi[:, c] over the d columns of Pi (bf16 split rows of Pi^T,
     // zero norms), scaled by -1/2 (exact). JHQ_ROTATE=simt keeps the fp32 chains.
     {
+        // The tensor-core kernel tiles 128 queries x 256 outputs; batches below
+        // ~1k queries leave most SMs idle there and are faster on the fp32
+        // chains (C1, batch 64: 34 vs 27 us per batch), so the choice follows
+        // the index's batch size (and JHQ_ROTATE=simt|tc forces it).
         const char* rm = std::getenv("JHQ_ROTATE");
-        rot_tc_ = d_ <= 2048 && !(rm && std::string(rm) == "simt");
+        rot_tc_ = d_ <= 2048 && p_.batch_size >= 1024;
+        if (rm && std::string(rm) == "simt") rot_tc_ = false;
+        if (rm && std::string(rm) == "tc") rot_tc_ = d_ <= 2048;
         if (rot_tc_) {
             std::vector<float> piT((size_t)d_ * d_);
             for (int j = 0; j < d_; ++j)
@@ -556,6 +570,10 @@ void Index::rebuild_layout() {
     h2d(dslot_ids_.get(), slots.data(), slots.size(), stream_);
     scatter_pages(dslot_ids_.get(), (int64_t)slots.size(), dpcodes_.get(), M_, Mp_, dpages_.get(),
                   stream_);
+    if (p_.nlist == 1 && bpd_ == 1) {  // bit counts for the tensor-core flat scan
+        dpop_.resize((size_t)std::max<int64_t>(1, ntotal_));
+        popcount_rows(dpcodes_.get(), ntotal_, M_, dpop_.get(), stream_);
+    }
     if (pilotP_ > 0) {                 // pilot members, grouped by cluster in id order
         std::vector<int32_t> off(pilotP_ + 1, 0), ids((size_t)std::max<int64_t>(1, ntotal_));
         for (int64_t i = 0; i < ntotal_; ++i) off[h_pilot_assign_[(size_t)i] + 1]++;
@@ -664,6 +682,7 @@ void Index::prepare_workspace(int k) {
     ws_.qslot_off.ensure((size_t)Bq + 1);
     ws_.gthr.ensure((size_t)Bq);
     ws_.cand.ensure((size_t)sh.max_slots * sh.ck);
+    if (flat_tc()) ws_.flat.ensure(flat_tc_scratch_bytes(Bq, d_, (int)ntotal_));
     if (pilotP_ > 0) {
         ws_.pkeys.ensure((size_t)Bq * PILOT_SPLIT * sh.ck);
         ws_.pscores.ensure((size_t)Bq * pilotP_);
@@ -746,6 +765,31 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
         coarse_probes(b.q_rot, nq, sh.Bq, p_.nprobe, b.scores, b.probes, s);
     }
     mark(2);
+    if (p_.nlist == 1 && b.flat && !probes_in) {     // flat, 1-bit codes: tensor-core ADC
+        FlatTcArgs fa;
+        fa.q_rot = b.q_rot; fa.c1d = dc1d_.get(); fa.c1d_host = c1d_.data();
+        fa.codes = dpcodes_.get(); fa.pop = dpop_.get();
+        fa.nvec = (int)ntotal_; fa.M = M_; fa.nq = nq; fa.ck = sh.ck; fa.ck_pad = sh.ck_pad;
+        fa.scratch = b.flat; fa.cand = b.cand; fa.gthr = b.plan.gthr;
+        fa.qslot_off = b.plan.qslot_off;
+        mark(3);                       // no plan: the "scan" stage is the GEMM + selection
+        flat_search_tc(fa, s);
+        mark(4);
+        RefineArgs ra;
+        ra.q_rot = b.q_rot; ra.res_c1d = dres_.get(); ra.cand = b.cand;
+        ra.res_per_sub = res_per_sub_ ? 1 : 0; ra.M = M_;
+        ra.qslot_off = b.plan.qslot_off; ra.gthr = b.plan.gthr; ra.rcodes = drcodes_.get();
+        ra.corr = dcorr_.get(); ra.out_dists = out_d; ra.out_ids = out_i;
+        ra.nq = nq; ra.d = d_; ra.Br = Br_; ra.bpv_pad = bpv_pad_; ra.ck = sh.ck;
+        ra.ck_pad = sh.ck_pad; ra.k = sh.k; ra.kr = sh.kr;
+        if (keep_raw_ && rerank_ > 0) {
+            ra.q_raw = q_in;
+            ra.raw = draw_.get();
+        }
+        refine_topk(ra, s);
+        mark(5);
+        return;
+    }
     const int qg = sh.mode == 0 ? 1 : sh.mode;
     if (sh.qmajor)
         plan_build_qmajor(probes, nq, p_.nprobe, dlist_page_off_.get(), d_nvalid,
@@ -801,6 +845,7 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     BatchBufs b;
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
     b.rotq = ws_.rotq.get();
+    b.flat = flat_tc() ? ws_.flat.get() : nullptr;
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
@@ -979,6 +1024,7 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     BatchBufs b;
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
     b.rotq = ws_.rotq.get();
+    b.flat = flat_tc() ? ws_.flat.get() : nullptr;
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();

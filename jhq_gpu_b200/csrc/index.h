@@ -122,6 +122,7 @@ private:
         PinnedBuf<int32_t> h_i;
         PinnedBuf<int> h_nvalid;
         DevBuf<float> q, q_rot, scores, out_d, rotq;
+        DevBuf<unsigned char> flat;    // flat_search_tc scratch
         DevBuf<int32_t> probes, out_i, cnt, bucket_off, unit_off, fill, cpo;
         DevBuf<int2> bucket;
         DevBuf<int64_t> qslot_off;
@@ -171,6 +172,7 @@ private:
         uint64_t* pkeys = nullptr;     // pilot scratch (flat index with pilot clusters)
         float* pscores = nullptr;
         float* rotq = nullptr;         // tensor-core query rotation scratch
+        void* flat = nullptr;          // tensor-core flat scan scratch (nullptr: SIMT scan)
     };
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
@@ -184,6 +186,9 @@ private:
     void check_search_args(int64_t nq, int k) const;
     // candidates the JHQ stage returns for a search of k: k, or max(R, k) with rerank
     int stage_k(int k) const { return rerank_ > 0 ? std::max(rerank_, k) : k; }
+    // flat index with 1-bit codes: the ADC scan runs as a tensor-core GEMM of
+    // the code bits with the queries (coarse_tc.cu: flat_search_tc)
+    bool flat_tc() const;
 
     int d_, M_, B_, Br_, Ds_, bpd_, K1D_, Kr_, bpv_, bpv_pad_, Mp_;
     Params p_;
@@ -219,6 +224,7 @@ private:
     bool coarse_tc_ = false;
     DevBuf<uint8_t> dpcodes_, drcodes_, dpages_;
     DevBuf<float> dcorr_;
+    DevBuf<int32_t> dpop_;             // popcount of each primary code row (flat tensor-core scan)
     bool res_per_sub_ = false;         // M per-subspace residual codebooks
     // list paging (paging.cu): host-resident codes + device page pool
     int64_t pool_pages_ = 0, paging_waves_ = 0;

@@ -31,6 +31,8 @@ void gemm_argmin(const float* A, const float* B, const float* norms, int64_t R, 
 void encode_rows(const float* y, int64_t n, int d, int M, int B, int Br,
                  const float* c1d, const float* res_c1d, bool res_per_sub, uint8_t* pcodes,
                  uint8_t* rcodes, int bpv_pad, float* corr, cudaStream_t s);
+// pop[v] = number of set bits of code row v ([n][M] bytes)
+void popcount_rows(const uint8_t* codes, int64_t n, int M, int32_t* pop, cudaStream_t s);
 // v[i] *= f (f a power of two here, so exact)
 void scale_floats(float* v, int64_t n, float f, cudaStream_t s);
 // dst[0] = value (stream-ordered scalar upload, no host buffer involved).
@@ -178,6 +180,23 @@ void remap_ids(int32_t* ids, int64_t n, int mul, int add, cudaStream_t st);
 // k-way merge of per-shard top-k lists (jhq_merge_shards).
 void merge_shard_lists(const float* in_d, const int32_t* in_i, int nshards, int64_t nq,
                        int k, float* out_d, int32_t* out_i, cudaStream_t st);
+
+// ---- flat ADC scan on the tensor cores, 1-bit codes (coarse_tc.cu) ----------
+struct FlatTcArgs {
+    const float* q_rot;          // [nq][d]
+    const float* c1d;            // [2] on the device
+    const float* c1d_host;       // [2] on the host
+    const uint8_t* codes;        // [nvec][M] primary codes, id order
+    const int32_t* pop;          // [nvec] popcount of each code row
+    int nvec, M, nq, ck, ck_pad;
+    void* scratch;               // flat_tc_scratch_bytes(nq, d, nvec)
+    uint64_t* cand;              // [nq][ck] out: the exact top-ck, one slot per query
+    uint64_t* gthr;              // [nq] out: the ck-th key
+    int64_t* qslot_off;          // [nq+1] out: q
+};
+bool flat_tc_supported(int d, int M, int B, int nvec);
+size_t flat_tc_scratch_bytes(int Bq, int d, int nvec);
+void flat_search_tc(const FlatTcArgs& a, cudaStream_t s);
 
 // ---- training on the device (train_gpu.cu), bit-identical to train_cpu.cpp ----
 // y <- y - c1d[bits of the primary code], in place ([n][d])

@@ -645,7 +645,7 @@ def test_tensor_core_query_rotation(jhq, monkeypatch, d, M):
     else:
         x = _data(12000, d, 91)
         q = _data(200, d, 92)
-    p = jhq.Params(M=M, nlist=1, nprobe=1, batch_size=64)
+    p = jhq.Params(M=M, nlist=1, nprobe=1, batch_size=1024)   # large batches rotate on tcgen05
     idx = _build(jhq, d, p, x[:6000], x)
     y_exact = idx.rotate(q)
     y_tc = idx.rotate_queries(q)
@@ -685,3 +685,31 @@ def test_coarse_wait_timeout_is_reported_and_the_index_recovers(jhq, monkeypatch
     idx.set_nprobe(8)
     _assert_same(*idx.search(q, 10), D0, I0)
     idx.check_device_status()                          # the flag was cleared by the report
+
+
+@pytest.mark.parametrize("n,nq,batch,k,R", [(30000, 70, 64, 10, 0), (20000, 200, 130, 10, 0),
+                                             (6000, 33, 32, 40, 0), (25000, 64, 64, 10, 24)])
+def test_flat_tensor_core_scan_bit_exact(jhq, oracle, monkeypatch, n, nq, batch, k, R):
+    """Flat index with 1-bit codes (C1: D=1024, M=128): the ADC scan as a tcgen05
+    GEMM of the code bits with the queries, then the margin selection and exact
+    rescoring — the same ids and distances as the oracle and as the SIMT scan
+    (JHQ_FLAT=simt), with query blocks of 64, 128+2, and ck > the tile count."""
+    from jhq_gpu_b200 import datasets
+    x, q = datasets.make("c1", seed=1, n=n, nq=nq)
+    p = jhq.Params(M=128, nlist=1, nprobe=1, batch_size=batch)
+    idx = jhq.JHQGpuIndex(1024, p)
+    idx.train(x[:min(n, 20000)])
+    if R:
+        idx.set_rerank(R)
+    idx.add(x)
+    ox = _oracle_index(oracle, idx, x)
+    D, I = idx.search(q, k)
+    if R:
+        _, Ic = _oracle_search(oracle, idx, ox, q, max(R, k))
+        D2, I2 = oracle.rerank(q, x, Ic, k)
+    else:
+        D2, I2 = _oracle_search(oracle, idx, ox, q, k)
+    _assert_same(D, I, D2, I2)
+    monkeypatch.setenv("JHQ_FLAT", "simt")
+    idx.set_nprobe(1)                                  # re-plan on the SIMT scan
+    _assert_same(*idx.search(q, k), D, I)
