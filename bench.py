@@ -872,7 +872,8 @@ def run_c2(args):
 def run_profile_case(args):
     """Short runs for ncu: C1 (train on 20k rows, add 100k, two searches) or, with
     --config c3, a reduced C3 shard (--db-size rows, --queries queries, two
-    searches) — nothing else launches kernels after the build."""
+    searches). The second search sits in the NVTX range "search", so
+    `ncu --nvtx --nvtx-include search/` captures its launches only."""
     import jhq_gpu_b200 as J
     from jhq_gpu_b200 import datasets
     if args.config in ("c3", "c4"):
@@ -890,8 +891,11 @@ def run_profile_case(args):
         for s in range(0, n, 2_000_000):
             idx.add(datasets.rows_torch(args.config, s, min(n, s + 2_000_000), dev).cpu().numpy())
         q = datasets.rows_torch(args.config, 0, nq, dev, sub=2).cpu().numpy()
-        for _ in range(2):
-            D, I = idx.search(q, 10)
+        D, I = idx.search(q, 10)                   # warm-up (graph capture)
+        torch.cuda.nvtx.range_push("search")       # the captured search (ncu --nvtx-include search/)
+        D, I = idx.search(q, 10)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         print("profile case done", int((I >= 0).sum()))
         return
     base, queries = datasets.make("c1", seed=C1["seed"])
@@ -902,8 +906,12 @@ def run_profile_case(args):
     if args.rerank:
         idx.set_rerank(args.rerank)
     idx.add(base)
-    for _ in range(2):
-        D, I = idx.search(queries, C1["k"])
+    import torch
+    D, I = idx.search(queries, C1["k"])            # warm-up (graph capture)
+    torch.cuda.nvtx.range_push("search")           # the captured search (ncu --nvtx-include search/)
+    D, I = idx.search(queries, C1["k"])
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     print("profile case done", int((I >= 0).sum()))
 
 
