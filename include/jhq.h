@@ -102,6 +102,13 @@ int jhq_search_device_noalloc(jhq_index* idx, const float* d_q, int64_t nq, int 
  * themselves. No counterpart in the reference (its device errors exit). */
 int jhq_device_status(jhq_index* idx);
 
+/* Diagnostics (no counterpart in the reference): the approximate ADC scores
+ * s~[q][v] the tensor-core flat scan computes for nq <= 128 host queries
+ * (scores: [nq][ntotal] floats), so a checker can measure them against the
+ * exact keys and the selection's error bound. JHQ_ESTATE when the index does
+ * not use that scan (IVF, bits per dimension != 1, JHQ_FLAT=simt). */
+int jhq_debug_flat_scores(jhq_index* idx, const float* q, int nq, float* scores);
+
 /* Waits for the index's stream with a deadline (replaces the unbounded
  * cudaStreamQuery spin of search.cu:442-444). JHQ_ETIMEDOUT on expiry. */
 int jhq_synchronize(jhq_index* idx, double timeout_s);

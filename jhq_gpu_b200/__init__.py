@@ -37,7 +37,7 @@ EXPORTED = [
     "jhq_lloyd_max_c1d", "jhq_kmeans_1d", "jhq_set_profiling", "jhq_stage_times",
     "jhq_search_device_noalloc", "jhq_set_nprobe", "jhq_set_rerank", "jhq_get_rerank",
     "jhq_set_alpha", "jhq_list_sizes", "jhq_rotate_queries", "jhq_device_status", "jhq_set_residual_codebooks",
-    "jhq_get_residual_codebooks", "jhq_set_list_paging", "jhq_paging_waves",
+    "jhq_get_residual_codebooks", "jhq_debug_flat_scores", "jhq_set_list_paging", "jhq_paging_waves",
     "jhq_probe_device",
     "jhq_search_device_probes", "jhq_sharded_create", "jhq_sharded_destroy",
     "jhq_sharded_train", "jhq_sharded_add", "jhq_sharded_search", "jhq_sharded_set_nprobe",
@@ -109,6 +109,7 @@ def load_library(path: str = "") -> C.CDLL:
     L.jhq_rotate_queries.argtypes = [vp, f32p, i64, f32p]
     L.jhq_list_sizes.argtypes = [vp, C.POINTER(C.c_int64)]
     L.jhq_device_status.argtypes = [vp]
+    L.jhq_debug_flat_scores.argtypes = [vp, f32p, C.c_int, f32p]
     L.jhq_set_residual_codebooks.argtypes = [vp, C.c_int]
     L.jhq_set_list_paging.argtypes = [vp, i64]
     L.jhq_paging_waves.argtypes = [vp, C.POINTER(C.c_int64)]
@@ -307,6 +308,14 @@ class JHQGpuIndex:
         v = C.c_int64()
         _check(self._L.jhq_paging_waves(self._h, C.byref(v)))
         return v.value
+
+    def debug_flat_scores(self, q) -> np.ndarray:
+        """Approximate ADC scores [nq][ntotal] of the tensor-core flat scan."""
+        q = _f32(q)
+        out = np.empty((q.shape[0], self.ntotal), np.float32)
+        _check(self._L.jhq_debug_flat_scores(self._h, _ptr(q, C.c_float), q.shape[0],
+                                             _ptr(out, C.c_float)))
+        return out
 
     def check_device_status(self) -> None:
         """Raises JHQError (JHQ_ETIMEDOUT) if a device wait of a search on the

@@ -165,6 +165,14 @@ int jhq_paging_waves(const jhq_index* idx, int64_t* waves) {
     });
 }
 
+int jhq_debug_flat_scores(jhq_index* idx, const float* q, int nq, float* scores) {
+    return guarded([&] {
+        if (!q || !scores) jhq::fail(JHQ_EINVAL, "null buffer");
+        if (!need(idx)->flat_tc_scores(q, nq, scores))
+            jhq::fail(JHQ_ESTATE, "this index does not use the tensor-core flat scan (or nq > 128)");
+    });
+}
+
 int jhq_device_status(jhq_index* idx) {
     return guarded([&] { need(idx)->check_device_status(); });
 }

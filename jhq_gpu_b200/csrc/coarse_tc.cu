@@ -704,12 +704,13 @@ __global__ void flat_prep_kernel(const float* __restrict__ q_rot, int nq, int N,
 //   arithmetic (nibble tables lo + hi, in-order sum over m: the oracle's key),
 //   and the exact top-ck by (distance, id) is written as the query's single
 //   candidate slot for the refine.
-constexpr int FS_WARPS = 4;
+constexpr int FS_WARPS = 1;                  // one query per CTA: the selection is latency bound
 constexpr int FS_CAP = 512;                  // exact keys held before a compaction (>= ck_pad + 32)
-constexpr int FS_TILES = 4096;               // tile minima a warp sorts (nvec <= 524,288)
+constexpr int FS_CAND = 1024;                // window candidates gathered before they are rescored
+constexpr int FS_TILES = 4096;               // tile minima per query (nvec <= 524,288)
 
 __host__ __device__ inline size_t fs_warp_bytes(int M, int ntiles_pad) {
-    return (size_t)M * 32 * 4 + (size_t)(FS_CAP + ntiles_pad) * 8 + 32 * 4;
+    return (size_t)M * 32 * 4 + (size_t)FS_CAP * 8 + (size_t)ntiles_pad * 4 * 2 + (size_t)FS_CAND * 4;
 }
 
 __global__ void __launch_bounds__(FS_WARPS * 32)
@@ -724,13 +725,15 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
     const int q = blockIdx.x * FS_WARPS + warp;
     if (q >= nq) return;
     unsigned char* wb = fs_smem + warp * fs_warp_bytes(M, ntiles_pad);
-    float* tab = reinterpret_cast<float*>(wb);                       // [M][32]
-    uint64_t* buf = reinterpret_cast<uint64_t*>(wb + (size_t)M * 32 * 4);
-    uint64_t* tk = buf + FS_CAP;                                       // [ntiles_pad]
-    int* stage = reinterpret_cast<int*>(tk + ntiles_pad);              // 32 candidates
+    float* tab = reinterpret_cast<float*>(wb);                         // [M][32]
+    uint64_t* buf = reinterpret_cast<uint64_t*>(wb + (size_t)M * 32 * 4);   // [FS_CAP] exact keys
+    uint32_t* tk = reinterpret_cast<uint32_t*>(buf + FS_CAP);          // [ntiles] tile minima
+    int* hot = reinterpret_cast<int*>(tk + ntiles_pad);                // tiles inside the window
+    int* cl = hot + ntiles_pad;                                        // [FS_CAND] candidates
     const int d = M * 8;
     const float* qv = q_rot + (int64_t)q * d;
     const float c0 = c1d_g[0], c1 = c1d_g[1];
+    const unsigned lt = (1u << lane) - 1u;
 
     // error bound (all but per-query constants): LUT-path rounding of s, the
     // bf16 split and fp32 tensor accumulation of g, and the roundings forming s~
@@ -753,10 +756,6 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
                             2.0f * ae * L1 * (3.8146973e-06f + (float)(2 * d) * 1.1920929e-07f) +
                             2.0f * u * (S0 + aD * (float)d + 2.0f * ae * L1) * 1.001f);
 
-    // tau from the sorted tile minima
-    for (int i = lane; i < ntiles_pad; i += 32)
-        tk[i] = i < ntiles ? (((uint64_t)tile_min[(int64_t)q * ntiles + i] << 32) | (uint32_t)i)
-                           : KEY_EMPTY;
     // the query's nibble tables (the scan's mode-1 tables: lo dims 0-3, hi 4-7)
     for (int i = lane; i < M * 32; i += 32) {
         const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
@@ -767,28 +766,41 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
         }
         tab[i] = acc;
     }
+    for (int i = lane; i < ntiles; i += 32) tk[i] = tile_min[(int64_t)q * ntiles + i];
     __syncwarp();
-    warp_bitonic_sort(tk, ntiles_pad, lane);
-    const float tau = ck <= ntiles ? order_float((uint32_t)(tk[ck - 1] >> 32)) : __int_as_float(0x7f800000);
+
+    // tau = the ck-th smallest tile minimum: bisection over the order keys
+    float tau = __int_as_float(0x7f800000);
+    if (ck <= ntiles) {
+        uint32_t lo = 0, hi = 0xFFFFFFFFu;                 // smallest x with count(k <= x) >= ck
+        while (lo < hi) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            int c = 0;
+            for (int i = lane; i < ntiles; i += 32) c += tk[i] <= mid;
+            c = __reduce_add_sync(0xffffffffu, c);
+            if (c >= ck) hi = mid; else lo = mid + 1;
+        }
+        tau = order_float(lo);
+    }
     const float T = __fadd_ru(tau, 2.0f * E);
 
-    int n = 0;
-    const float* srow = scores + (int64_t)q * nvec;
-    for (int ti = 0; ti < ntiles; ++ti) {
-        const uint64_t tkey = tk[ti];
-        if (tkey == KEY_EMPTY || !(order_float((uint32_t)(tkey >> 32)) <= T)) break;
-        const int t = (int)(uint32_t)tkey;
-        for (int r0 = 0; r0 < FT_BM; r0 += 32) {
-            const int v = t * FT_BM + r0 + lane;
-            const bool in = v < nvec && srow[v] <= T;
-            const unsigned mk = __ballot_sync(0xffffffffu, in);
-            if (!mk) continue;
-            if (in) stage[__popc(mk & ((1u << lane) - 1u))] = v;
-            __syncwarp();
-            const int cnt = __popc(mk);
+    // tiles whose minimum is inside the window (index order)
+    int nhot = 0;
+    for (int b0 = 0; b0 < ntiles; b0 += 32) {
+        const int t = b0 + lane;
+        const bool in = t < ntiles && order_float(tk[t]) <= T;
+        const unsigned mk = __ballot_sync(0xffffffffu, in);
+        if (in) hot[nhot + __popc(mk & lt)] = t;
+        nhot += __popc(mk);
+    }
+    __syncwarp();
+
+    int n = 0;                                             // exact keys in buf
+    auto rescore = [&](int cnt) {                          // cl[0..cnt) -> exact keys into buf
+        for (int c0i = 0; c0i < cnt; c0i += 32) {
             uint64_t key = KEY_EMPTY;
-            if (lane < cnt) {                                          // exact key, lane per candidate
-                const int id = stage[lane];
+            if (c0i + lane < cnt) {
+                const int id = cl[c0i + lane];
                 const uint4* cv = reinterpret_cast<const uint4*>(codes + (int64_t)id * M);
                 float dist = 0.0f;
                 for (int g = 0; g < M / 16; ++g) {
@@ -806,19 +818,40 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
                 }
                 key = make_key(dist, id);
             }
-            __syncwarp();
-            const unsigned mk2 = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
-            if (n + __popc(mk2) > FS_CAP) {                            // keep the best ck_pad
+            const unsigned mk = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
+            if (n + __popc(mk) > FS_CAP) {                 // keep the best ck_pad
                 for (int i = n + lane; i < FS_CAP; i += 32) buf[i] = KEY_EMPTY;
                 __syncwarp();
                 warp_bitonic_sort(buf, FS_CAP, lane);
                 n = ck_pad;
             }
-            if (key != KEY_EMPTY) buf[n + __popc(mk2 & ((1u << lane) - 1u))] = key;
-            n += __popc(mk2);
+            if (key != KEY_EMPTY) buf[n + __popc(mk & lt)] = key;
+            n += __popc(mk);
+            __syncwarp();
+        }
+    };
+    // window candidates of the hot tiles, rescored FS_CAND at a time
+    const float* srow = scores + (int64_t)q * nvec;
+    int nc = 0;
+    for (int h = 0; h < nhot; ++h) {
+        const int t = hot[h];
+        for (int r0 = 0; r0 < FT_BM; r0 += 32) {
+            const int v = t * FT_BM + r0 + lane;
+            const bool in = v < nvec && srow[v] <= T;
+            const unsigned mk = __ballot_sync(0xffffffffu, in);
+            if (!mk) continue;
+            if (nc + __popc(mk) > FS_CAND) {
+                __syncwarp();
+                rescore(nc);
+                nc = 0;
+            }
+            if (in) cl[nc + __popc(mk & lt)] = v;
+            nc += __popc(mk);
             __syncwarp();
         }
     }
+    __syncwarp();
+    rescore(nc);
     int P = ck_pad;
     while (P < n) P <<= 1;
     for (int i = n + lane; i < P; i += 32) buf[i] = KEY_EMPTY;
@@ -837,6 +870,14 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
 bool flat_tc_supported(int d, int M, int B, int nvec) {
     return M > 0 && d == 8 * M && B == 8 && M % 16 == 0 && nvec > 0 &&
            (nvec + FT_BM - 1) / FT_BM <= FS_TILES;
+}
+
+float* flat_tc_scores_of(void* scratch, int Bq, int d) {
+    const int Nb = std::min(128, (Bq + 31) / 32 * 32);
+    unsigned char* p = reinterpret_cast<unsigned char*>(scratch);
+    p += (((size_t)2 * Nb * d * 2) + 255) & ~size_t(255);
+    p += (((size_t)Bq * 4) + 255) & ~size_t(255);
+    return reinterpret_cast<float*>(p);
 }
 
 size_t flat_tc_scratch_bytes(int Bq, int d, int nvec) {
@@ -888,6 +929,7 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
         JHQ_LAUNCH_CHECK();
         count_launch(2);
     }
+    if (a.scores_only) return;                     // diagnostics: the approximate scores
     const size_t smem = (size_t)FS_WARPS * fs_warp_bytes(a.M, ntiles_pad);
     if (smem > 227 * 1024) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
     flat_select_kernel<<<(unsigned)ceil_div(a.nq, FS_WARPS), FS_WARPS * 32, smem, s>>>(

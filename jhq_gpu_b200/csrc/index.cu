@@ -1060,6 +1060,28 @@ void Index::set_alpha(float alpha) {
     ws_.batch_cap = 0;
 }
 
+bool Index::flat_tc_scores(const float* h_q, int nq, float* h_scores) {
+    DeviceGuard g(dev_);
+    if (!flat_tc() || nq <= 0 || nq > 128) return false;
+    DevBuf<float> dq((size_t)nq * d_), dr((size_t)nq * d_);
+    DevBuf<float> sc(std::max<size_t>(1, rotq_scratch_floats(nq)));
+    DevBuf<unsigned char> fl(flat_tc_scratch_bytes(nq, d_, (int)ntotal_));
+    DevBuf<uint64_t> cand((size_t)nq * 256), gth((size_t)nq);
+    DevBuf<int64_t> qs((size_t)nq + 1);
+    h2d(dq.get(), h_q, (size_t)nq * d_, stream_);
+    rotate_queries_device(dq.get(), nq, dr.get(), sc.get(), stream_);
+    FlatTcArgs fa;
+    fa.q_rot = dr.get(); fa.c1d = dc1d_.get(); fa.c1d_host = c1d_.data();
+    fa.codes = dpcodes_.get(); fa.pop = dpop_.get();
+    fa.nvec = (int)ntotal_; fa.M = M_; fa.nq = nq; fa.ck = 10; fa.ck_pad = 32;
+    fa.scratch = fl.get(); fa.cand = cand.get(); fa.gthr = gth.get(); fa.qslot_off = qs.get();
+    fa.scores_only = true;
+    flat_search_tc(fa, stream_);
+    d2h(h_scores, flat_tc_scores_of(fl.get(), nq, d_), (size_t)nq * ntotal_, stream_);
+    JHQ_CUDA(cudaStreamSynchronize(stream_));
+    return true;
+}
+
 void Index::check_device_status() {
     DeviceGuard g(dev_);
     if ((coarse_tc_ || rot_tc_) && coarse_tc_error(true))

@@ -55,6 +55,10 @@ public:
     // Raises JHQ_ETIMEDOUT (and clears the flag) when a bounded device wait of a
     // search enqueued on any stream gave up; call after that stream has drained.
     void check_device_status();
+    // Diagnostics of the tensor-core flat scan: the approximate ADC scores
+    // s~[q][v] of host queries (same rotation and GEMM as search), or false when
+    // this index does not use the tensor-core flat scan.
+    bool flat_tc_scores(const float* h_q, int nq, float* h_scores);
     void set_nprobe(int nprobe);
     void set_alpha(float alpha);
     void probe_device(const float* d_q, int64_t nq, int32_t* d_probes, cudaStream_t stream);

@@ -193,7 +193,10 @@ struct FlatTcArgs {
     uint64_t* cand;              // [nq][ck] out: the exact top-ck, one slot per query
     uint64_t* gthr;              // [nq] out: the ck-th key
     int64_t* qslot_off;          // [nq+1] out: q
+    bool scores_only = false;    // stop after the GEMM (diagnostics)
 };
+// the approximate scores [nq][nvec] inside a flat_search_tc scratch block
+float* flat_tc_scores_of(void* scratch, int Bq, int d);
 bool flat_tc_supported(int d, int M, int B, int nvec);
 size_t flat_tc_scratch_bytes(int Bq, int d, int nvec);
 void flat_search_tc(const FlatTcArgs& a, cudaStream_t s);
