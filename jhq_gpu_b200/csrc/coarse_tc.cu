@@ -537,10 +537,19 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
         const int r = tid;                                 // tile row = vector
         int it = 0;
         bool stop = false;
-        for (int t = blockIdx.x; t < ntiles && !stop && !*abort; t += gridDim.x) {
+        // the code bytes of the next chunk are loaded one chunk ahead (across
+        // tiles too), so their latency overlaps the wait and expansion of this one
+        auto load_cw = [&](int t, int kc) {
             const int v = t * FT_BM + r;
-            const uint8_t* vc = codes + (int64_t)v * M;
+            return (t < ntiles && v < nvec)
+                       ? __ldg(reinterpret_cast<const uint2*>(codes + (int64_t)v * M + kc * 8))
+                       : make_uint2(0u, 0u);
+        };
+        uint2 cw_next = load_cw(blockIdx.x, 0);
+        for (int t = blockIdx.x; t < ntiles && !stop && !*abort; t += gridDim.x) {
             for (int kc = 0; kc < nk; ++kc, ++it) {
+                const uint2 cw = cw_next;
+                cw_next = kc + 1 < nk ? load_cw(t, kc + 1) : load_cw(t + gridDim.x, 0);
                 const int s = it % S;
                 if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) - 1) & 1, abort, wait_limit)) {
                     stop = true;
@@ -555,8 +564,6 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                     tma_load_2d(b_s, &map_q, kc * FT_BK, 0, fb);                       // q_hi
                     tma_load_2d(b_s + N * FT_BK * 2, &map_q, kc * FT_BK, N, fb);       // q_lo
                 }
-                uint2 cw = make_uint2(0u, 0u);
-                if (v < nvec) cw = __ldg(reinterpret_cast<const uint2*>(vc + kc * 8));
                 uint8_t* row = st + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -719,11 +726,22 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
                    const uint32_t* __restrict__ tile_min, int nvec, int M, int nq, int ck,
                    int ck_pad, int ntiles, int ntiles_pad, float cmax, float ec, float Dc,
                    uint64_t* __restrict__ cand, uint64_t* __restrict__ gthr,
-                   int64_t* __restrict__ qslot_off) {
+                   int64_t* __restrict__ qslot_off, const int* __restrict__ d_nvalid) {
     extern __shared__ __align__(16) unsigned char fs_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int q = blockIdx.x * FS_WARPS + warp;
     if (q >= nq) return;
+    if (d_nvalid && q >= *d_nvalid) {
+        // padding row of a partial batch (zeros: every vector ties, so the
+        // window would take them all): no candidates
+        for (int i = lane; i < ck; i += 32) cand[(int64_t)q * ck + i] = KEY_EMPTY;
+        if (lane == 0) {
+            gthr[q] = KEY_EMPTY;
+            qslot_off[q + 1] = q + 1;
+            if (q == 0) qslot_off[0] = 0;
+        }
+        return;
+    }
     unsigned char* wb = fs_smem + warp * fs_warp_bytes(M, ntiles_pad);
     float* tab = reinterpret_cast<float*>(wb);                         // [M][32]
     uint64_t* buf = reinterpret_cast<uint64_t*>(wb + (size_t)M * 32 * 4);   // [FS_CAP] exact keys
@@ -934,7 +952,7 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
     if (smem > 227 * 1024) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
     flat_select_kernel<<<(unsigned)ceil_div(a.nq, FS_WARPS), FS_WARPS * 32, smem, s>>>(
         a.q_rot, a.c1d, a.codes, scores, tmin, a.nvec, a.M, a.nq, a.ck, a.ck_pad, ntiles,
-        ntiles_pad, cmax, ec, Dc, a.cand, a.gthr, a.qslot_off);
+        ntiles_pad, cmax, ec, Dc, a.cand, a.gthr, a.qslot_off, a.d_nvalid);
     JHQ_LAUNCH_CHECK();
     count_launch();
 }

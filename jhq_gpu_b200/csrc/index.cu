@@ -771,7 +771,7 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
         fa.codes = dpcodes_.get(); fa.pop = dpop_.get();
         fa.nvec = (int)ntotal_; fa.M = M_; fa.nq = nq; fa.ck = sh.ck; fa.ck_pad = sh.ck_pad;
         fa.scratch = b.flat; fa.cand = b.cand; fa.gthr = b.plan.gthr;
-        fa.qslot_off = b.plan.qslot_off;
+        fa.qslot_off = b.plan.qslot_off; fa.d_nvalid = d_nvalid;
         mark(3);                       // no plan: the "scan" stage is the GEMM + selection
         flat_search_tc(fa, s);
         mark(4);

@@ -193,6 +193,7 @@ struct FlatTcArgs {
     uint64_t* cand;              // [nq][ck] out: the exact top-ck, one slot per query
     uint64_t* gthr;              // [nq] out: the ck-th key
     int64_t* qslot_off;          // [nq+1] out: q
+    const int* d_nvalid = nullptr;   // device count of valid rows (rest: no candidates)
     bool scores_only = false;    // stop after the GEMM (diagnostics)
 };
 // the approximate scores [nq][nvec] inside a flat_search_tc scratch block
