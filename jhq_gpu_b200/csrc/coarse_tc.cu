@@ -39,7 +39,7 @@
 // gives up sets g_tc_error and a shared abort flag that ends every role's
 // loop; the producer then waits (bounded) for the copies it issued, the MMA
 // warp for its MMAs (a final commit), and the CTA frees its TMEM and returns.
-// No TMA load here uses cluster multicast; the operands are this GPU's own memory.
+// Every TMA load here reads this GPU's own memory into its own CTA only.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -493,6 +493,20 @@ __host__ __device__ inline int ft_stages(int N) { return N <= 64 ? 4 : 3; }
 __host__ __device__ inline int ft_stage_bytes(int N) { return FT_A_BYTES + 2 * N * FT_BK * 2; }
 __host__ __device__ inline int ft_smem_bytes(int N) { return ft_stages(N) * ft_stage_bytes(N) + 1024 + 256; }
 
+// 32 consecutive fp32 TMEM columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
 __global__ void __launch_bounds__(FT_THREADS, 1)
 flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restrict__ codes,
                const int32_t* __restrict__ pop, const float* __restrict__ S0, int nvec, int M,
@@ -508,10 +522,12 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
     const int d = M * 8, nk = d / FT_BK;
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, tfull0 = empty0 + 8 * S,
                    tempty0 = tfull0 + 16, drain = tempty0 + 16;
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+    // one MMA of N' = 2N: the hi and lo planes are consecutive B rows, so TMEM
+    // columns [0, N) accumulate q_hi . b and [N, 2N) q_lo . b
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(2 * N >> 3) << 17) |
                            ((uint32_t)(FT_BM >> 4) << 24);
     uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * N)) cols <<= 1;
+    while (cols < (uint32_t)(4 * N)) cols <<= 1;
     if (tid == 0) {
         for (int i = 0; i < 2 * S + 5; ++i) {
             const uint32_t a = full0 + 8 * i;
@@ -593,7 +609,7 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                 if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort, wait_limit))
                     break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t d_tmem = tmem + (uint32_t)(acc * N);
+                const uint32_t d_tmem = tmem + (uint32_t)(acc * 2 * N);
                 bool ok = true;
                 for (int kc = 0; kc < nk; ++kc, ++it) {
                     const int s = it % S;
@@ -601,19 +617,14 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t a_s = smem_u32(smem + s * SB);
                     const uint64_t da = sw128_desc(a_s);
-                    const uint64_t dh = sw128_desc(a_s + FT_A_BYTES);
-                    const uint64_t dl = sw128_desc(a_s + FT_A_BYTES + N * FT_BK * 2);
+                    const uint64_t db = sw128_desc(a_s + FT_A_BYTES);   // hi rows, then lo rows
 #pragma unroll
                     for (int k = 0; k < FT_BK / 16; ++k) {
                         const uint32_t accum = (kc | k) != 0;
                         asm volatile(
                             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(dh + 2 * k), "r"(idesc), "r"(accum));
-                        asm volatile(
-                            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(dl + 2 * k), "r"(idesc), "r"(1u));
+                            :: "r"(d_tmem), "l"(da + 2 * k), "l"(db + 2 * k), "r"(idesc), "r"(accum));
                     }
                     mma_commit(empty0 + 8 * s);
                 }
@@ -634,33 +645,39 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
             const int v = t * FT_BM + q4 * 32 + lane;
             const float pv = v < nvec ? (float)__ldg(pop + v) : 0.0f;
             for (int cb = 0; cb < N; cb += 32) {
-                uint32_t rg[32];
-                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * N + cb);
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                    "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3]), "=r"(rg[4]), "=r"(rg[5]),
-                      "=r"(rg[6]), "=r"(rg[7]), "=r"(rg[8]), "=r"(rg[9]), "=r"(rg[10]), "=r"(rg[11]),
-                      "=r"(rg[12]), "=r"(rg[13]), "=r"(rg[14]), "=r"(rg[15]), "=r"(rg[16]), "=r"(rg[17]),
-                      "=r"(rg[18]), "=r"(rg[19]), "=r"(rg[20]), "=r"(rg[21]), "=r"(rg[22]), "=r"(rg[23]),
-                      "=r"(rg[24]), "=r"(rg[25]), "=r"(rg[26]), "=r"(rg[27]), "=r"(rg[28]), "=r"(rg[29]),
-                      "=r"(rg[30]), "=r"(rg[31])
-                    : "r"(taddr));
+                uint32_t rh[32], rl[32];
+                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * 2 * N + cb);
+                tmem_ld32(taddr, rh);
+                tmem_ld32(taddr + (uint32_t)N, rl);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float m[32];
 #pragma unroll
                 for (int c = 0; c < 32; ++c) {
                     const int q = cb + c;
-                    if (q >= nq) break;                                 // warp-uniform
-                    const float g = __uint_as_float(rg[c]);
-                    const float sv = __fmaf_rn(-2.0f * ec, g, __fmaf_rn(Dc, pv, __ldg(S0 + q)));
-                    if (v < nvec) scores[(int64_t)q * nvec + v] = sv;
-                    float m = v < nvec ? sv : __int_as_float(0x7f800000);
-#pragma unroll
-                    for (int o = 16; o; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                    if (lane == 0)
-                        atomicMin(tile_min + (int64_t)q * ntiles + t, float_order(m));
+                    m[c] = __int_as_float(0x7f800000);
+                    if (q < nq) {                                       // warp-uniform
+                        const float g = __uint_as_float(rh[c]) + __uint_as_float(rl[c]);
+                        const float sv = __fmaf_rn(-2.0f * ec, g, __fmaf_rn(Dc, pv, __ldg(S0 + q)));
+                        if (v < nvec) {
+                            scores[(int64_t)q * nvec + v] = sv;
+                            m[c] = sv;
+                        }
+                    }
                 }
+                // transpose-reduce: after the 5 halving steps lane c holds the
+                // minimum of column c over the warp's 32 rows (31 shuffles)
+#pragma unroll
+                for (int h = 16; h; h >>= 1) {
+                    const bool up = lane & h;
+#pragma unroll
+                    for (int i = 0; i < h; ++i) {
+                        const float send = up ? m[i] : m[i + h];
+                        const float keep = up ? m[i + h] : m[i];
+                        m[i] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+                    }
+                }
+                if (cb + lane < nq)
+                    atomicMin(tile_min + (int64_t)(cb + lane) * ntiles + t, float_order(m[0]));
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(tempty0 + 8 * acc)
@@ -703,24 +720,27 @@ __global__ void flat_prep_kernel(const float* __restrict__ q_rot, int nq, int N,
     }
 }
 
-// Exact top-ck from the approximate scores, one warp per query:
+// Exact top-ck from the approximate scores, one CTA (8 warps) per query:
 //   tau = ck-th smallest tile minimum of s~ (ck distinct vectors have s~ <= tau);
 //   every exact top-ck member has s~ <= tau + 2E (E bounds |s~ - s| per vector
 //   up to a per-query constant), so only tiles whose minimum is <= tau + 2E are
 //   read, their vectors with s~ <= tau + 2E are rescored with the scan's own
 //   arithmetic (nibble tables lo + hi, in-order sum over m: the oracle's key),
 //   and the exact top-ck by (distance, id) is written as the query's single
-//   candidate slot for the refine.
-constexpr int FS_WARPS = 1;                  // one query per CTA: the selection is latency bound
-constexpr int FS_CAP = 512;                  // exact keys held before a compaction (>= ck_pad + 32)
-constexpr int FS_CAND = 1024;                // window candidates gathered before they are rescored
+//   candidate slot for the refine. The keys are unique (they hold the id), so
+//   the result does not depend on the order the threads find the candidates in.
+constexpr int FS_THREADS = 256;
+constexpr int FS_CAP = 1024;                 // exact keys held before a compaction (>= ck_pad + 256)
+constexpr int FS_ROUND = 64;                 // hot tiles read per round (8 per warp)
+constexpr int FS_CAND = FS_ROUND * FT_BM;    // window candidates of one round
 constexpr int FS_TILES = 4096;               // tile minima per query (nvec <= 524,288)
+constexpr int FS_SMEM_MAX = 200 * 1024;      // dynamic shared memory (the kernel has static too)
 
-__host__ __device__ inline size_t fs_warp_bytes(int M, int ntiles_pad) {
+__host__ __device__ inline size_t fs_smem_bytes(int M, int ntiles_pad) {
     return (size_t)M * 32 * 4 + (size_t)FS_CAP * 8 + (size_t)ntiles_pad * 4 * 2 + (size_t)FS_CAND * 4;
 }
 
-__global__ void __launch_bounds__(FS_WARPS * 32)
+__global__ void __launch_bounds__(FS_THREADS, 1)
 flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1d_g,
                    const uint8_t* __restrict__ codes, const float* __restrict__ scores,
                    const uint32_t* __restrict__ tile_min, int nvec, int M, int nq, int ck,
@@ -728,26 +748,29 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
                    uint64_t* __restrict__ cand, uint64_t* __restrict__ gthr,
                    int64_t* __restrict__ qslot_off, const int* __restrict__ d_nvalid) {
     extern __shared__ __align__(16) unsigned char fs_smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int q = blockIdx.x * FS_WARPS + warp;
+    __shared__ float red[3][FS_THREADS / 32];
+    __shared__ int cnt[2][FS_THREADS / 32];
+    __shared__ int nhot_s, nc_s, n_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = FS_THREADS / 32;
+    const int q = blockIdx.x;
     if (q >= nq) return;
+    if (tid == 0) {
+        qslot_off[q + 1] = q + 1;
+        if (q == 0) qslot_off[0] = 0;
+    }
     if (d_nvalid && q >= *d_nvalid) {
         // padding row of a partial batch (zeros: every vector ties, so the
         // window would take them all): no candidates
-        for (int i = lane; i < ck; i += 32) cand[(int64_t)q * ck + i] = KEY_EMPTY;
-        if (lane == 0) {
-            gthr[q] = KEY_EMPTY;
-            qslot_off[q + 1] = q + 1;
-            if (q == 0) qslot_off[0] = 0;
-        }
+        for (int i = tid; i < ck; i += FS_THREADS) cand[(int64_t)q * ck + i] = KEY_EMPTY;
+        if (tid == 0) gthr[q] = KEY_EMPTY;
         return;
     }
-    unsigned char* wb = fs_smem + warp * fs_warp_bytes(M, ntiles_pad);
-    float* tab = reinterpret_cast<float*>(wb);                         // [M][32]
-    uint64_t* buf = reinterpret_cast<uint64_t*>(wb + (size_t)M * 32 * 4);   // [FS_CAP] exact keys
-    uint32_t* tk = reinterpret_cast<uint32_t*>(buf + FS_CAP);          // [ntiles] tile minima
-    int* hot = reinterpret_cast<int*>(tk + ntiles_pad);                // tiles inside the window
-    int* cl = hot + ntiles_pad;                                        // [FS_CAND] candidates
+    float* tab = reinterpret_cast<float*>(fs_smem);                              // [M][32]
+    uint64_t* buf = reinterpret_cast<uint64_t*>(fs_smem + (size_t)M * 32 * 4);   // [FS_CAP] exact keys
+    uint32_t* tk = reinterpret_cast<uint32_t*>(buf + FS_CAP);                    // [ntiles] tile minima
+    int* hot = reinterpret_cast<int*>(tk + ntiles_pad);                          // tiles in the window
+    int* cl = hot + ntiles_pad;                                                  // [FS_CAND] candidates
     const int d = M * 8;
     const float* qv = q_rot + (int64_t)q * d;
     const float c0 = c1d_g[0], c1 = c1d_g[1];
@@ -756,7 +779,7 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
     // error bound (all but per-query constants): LUT-path rounding of s, the
     // bf16 split and fp32 tensor accumulation of g, and the roundings forming s~
     float V = 0.0f, L1 = 0.0f, S0 = 0.0f;
-    for (int j = lane; j < d; j += 32) {
+    for (int j = tid; j < d; j += FS_THREADS) {
         const float x = qv[j], a = fabsf(x) + cmax, t = x - c0;
         V += a * a;
         L1 += fabsf(x);
@@ -768,57 +791,111 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
         L1 += __shfl_xor_sync(0xffffffffu, L1, o);
         S0 += __shfl_xor_sync(0xffffffffu, S0, o);
     }
+    if (lane == 0) { red[0][warp] = V; red[1][warp] = L1; red[2][warp] = S0; }
+    if (tid == 0) { nhot_s = 0; n_s = 0; }
+
+    // the query's nibble tables (the scan's mode-1 tables: lo dims 0-3, hi 4-7)
+    for (int i = tid; i < M * 32; i += FS_THREADS) {
+        const int m = i >> 5, t = i & 31, half = t >> 4, nb = t & 15;
+        float acc = 0.0f;
+        for (int k = 0; k < 4; ++k) {
+            const float diff = qv[m * 8 + half * 4 + k] - ((nb >> k) & 1 ? c1 : c0);
+            acc = __fmaf_rn(diff, diff, acc);
+        }
+        tab[i] = acc;
+    }
+    for (int i = tid; i < ntiles; i += FS_THREADS) tk[i] = tile_min[(int64_t)q * ntiles + i];
+    __syncthreads();
+    V = L1 = S0 = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) { V += red[0][w]; L1 += red[1][w]; S0 += red[2][w]; }
+    // the 1.001 factors cover the fp32 rounding of V and S0 themselves
     const float u = 5.9604645e-08f;                                    // 2^-24
     const float aD = fabsf(Dc), ae = fabsf(ec);
     const float E = 1.1f * (V * 1.001f * (float)(2 * M + 16) * u + aD * (float)d * u +
                             2.0f * ae * L1 * (3.8146973e-06f + (float)(2 * d) * 1.1920929e-07f) +
                             2.0f * u * (S0 + aD * (float)d + 2.0f * ae * L1) * 1.001f);
 
-    // the query's nibble tables (the scan's mode-1 tables: lo dims 0-3, hi 4-7)
-    for (int i = lane; i < M * 32; i += 32) {
-        const int m = i >> 5, t = i & 31, half = t >> 4, n = t & 15;
-        float acc = 0.0f;
-        for (int k = 0; k < 4; ++k) {
-            const float diff = qv[m * 8 + half * 4 + k] - ((n >> k) & 1 ? c1 : c0);
-            acc = __fmaf_rn(diff, diff, acc);
-        }
-        tab[i] = acc;
-    }
-    for (int i = lane; i < ntiles; i += 32) tk[i] = tile_min[(int64_t)q * ntiles + i];
-    __syncwarp();
-
     // tau = the ck-th smallest tile minimum: bisection over the order keys
+    // (one barrier per step: the warp counts alternate between two rows)
     float tau = __int_as_float(0x7f800000);
     if (ck <= ntiles) {
         uint32_t lo = 0, hi = 0xFFFFFFFFu;                 // smallest x with count(k <= x) >= ck
+        int it = 0;
         while (lo < hi) {
             const uint32_t mid = lo + ((hi - lo) >> 1);
             int c = 0;
-            for (int i = lane; i < ntiles; i += 32) c += tk[i] <= mid;
+            for (int i = tid; i < ntiles; i += FS_THREADS) c += tk[i] <= mid;
             c = __reduce_add_sync(0xffffffffu, c);
-            if (c >= ck) hi = mid; else lo = mid + 1;
+            if (lane == 0) cnt[it & 1][warp] = c;
+            __syncthreads();
+            int tot = 0;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) tot += cnt[it & 1][w];
+            if (tot >= ck) hi = mid; else lo = mid + 1;
+            ++it;
         }
         tau = order_float(lo);
     }
     const float T = __fadd_ru(tau, 2.0f * E);
 
-    // tiles whose minimum is inside the window (index order)
-    int nhot = 0;
-    for (int b0 = 0; b0 < ntiles; b0 += 32) {
-        const int t = b0 + lane;
+    // tiles whose minimum is inside the window
+    for (int b0 = 0; b0 < ntiles; b0 += FS_THREADS) {
+        const int t = b0 + tid;
         const bool in = t < ntiles && order_float(tk[t]) <= T;
         const unsigned mk = __ballot_sync(0xffffffffu, in);
-        if (in) hot[nhot + __popc(mk & lt)] = t;
-        nhot += __popc(mk);
+        int base = 0;
+        if (lane == 0 && mk) base = atomicAdd(&nhot_s, __popc(mk));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (in) hot[base + __popc(mk & lt)] = t;
     }
-    __syncwarp();
-
-    int n = 0;                                             // exact keys in buf
-    auto rescore = [&](int cnt) {                          // cl[0..cnt) -> exact keys into buf
-        for (int c0i = 0; c0i < cnt; c0i += 32) {
+    __syncthreads();
+    const int nhot = nhot_s;
+    const float* srow = scores + (int64_t)q * nvec;
+    int n = 0;                                             // exact keys in buf (block-uniform)
+    for (int h0 = 0; h0 < nhot; h0 += FS_ROUND) {
+        if (tid == 0) nc_s = 0;
+        __syncthreads();
+        // gather: warp w reads hot tiles h0 + w + 8j, all loads issued first
+        float sv[FS_ROUND / NW][4];
+        int tt[FS_ROUND / NW];
+#pragma unroll
+        for (int j = 0; j < FS_ROUND / NW; ++j) {
+            const int h = h0 + warp + NW * j;
+            tt[j] = h < nhot ? hot[h] : -1;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                // rows past nvec (or no tile) read NaN: never <= T, even when T = +inf
+                const int v = tt[j] * FT_BM + c * 32 + lane;
+                sv[j][c] = (tt[j] >= 0 && v < nvec) ? __ldg(srow + v) : __int_as_float(0x7fc00000);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < FS_ROUND / NW; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const bool in = sv[j][c] <= T;
+                const unsigned mk = __ballot_sync(0xffffffffu, in);
+                if (!mk) continue;
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&nc_s, __popc(mk));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (in) cl[base + __popc(mk & lt)] = tt[j] * FT_BM + c * 32 + lane;
+            }
+        __syncthreads();
+        const int nc = nc_s;
+        // rescore: one candidate per thread, appended to buf
+        for (int c0i = 0; c0i < nc; c0i += FS_THREADS) {
+            if (n + FS_THREADS > FS_CAP) {                 // keep the best ck_pad
+                for (int i = n + tid; i < FS_CAP; i += FS_THREADS) buf[i] = KEY_EMPTY;
+                __syncthreads();
+                block_bitonic_sort(buf, FS_CAP);
+                n = ck_pad;
+                if (tid == 0) n_s = n;
+            }
             uint64_t key = KEY_EMPTY;
-            if (c0i + lane < cnt) {
-                const int id = cl[c0i + lane];
+            if (c0i + tid < nc) {
+                const int id = cl[c0i + tid];
                 const uint4* cv = reinterpret_cast<const uint4*>(codes + (int64_t)id * M);
                 float dist = 0.0f;
                 for (int g = 0; g < M / 16; ++g) {
@@ -837,50 +914,21 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
                 key = make_key(dist, id);
             }
             const unsigned mk = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
-            if (n + __popc(mk) > FS_CAP) {                 // keep the best ck_pad
-                for (int i = n + lane; i < FS_CAP; i += 32) buf[i] = KEY_EMPTY;
-                __syncwarp();
-                warp_bitonic_sort(buf, FS_CAP, lane);
-                n = ck_pad;
-            }
-            if (key != KEY_EMPTY) buf[n + __popc(mk & lt)] = key;
-            n += __popc(mk);
-            __syncwarp();
-        }
-    };
-    // window candidates of the hot tiles, rescored FS_CAND at a time
-    const float* srow = scores + (int64_t)q * nvec;
-    int nc = 0;
-    for (int h = 0; h < nhot; ++h) {
-        const int t = hot[h];
-        for (int r0 = 0; r0 < FT_BM; r0 += 32) {
-            const int v = t * FT_BM + r0 + lane;
-            const bool in = v < nvec && srow[v] <= T;
-            const unsigned mk = __ballot_sync(0xffffffffu, in);
-            if (!mk) continue;
-            if (nc + __popc(mk) > FS_CAND) {
-                __syncwarp();
-                rescore(nc);
-                nc = 0;
-            }
-            if (in) cl[nc + __popc(mk & lt)] = v;
-            nc += __popc(mk);
-            __syncwarp();
+            int base = 0;
+            if (lane == 0 && mk) base = atomicAdd(&n_s, __popc(mk));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (key != KEY_EMPTY) buf[base + __popc(mk & lt)] = key;
+            __syncthreads();
+            n = n_s;
         }
     }
-    __syncwarp();
-    rescore(nc);
     int P = ck_pad;
     while (P < n) P <<= 1;
-    for (int i = n + lane; i < P; i += 32) buf[i] = KEY_EMPTY;
-    __syncwarp();
-    warp_bitonic_sort(buf, P, lane);
-    for (int i = lane; i < ck; i += 32) cand[(int64_t)q * ck + i] = buf[i];
-    if (lane == 0) {
-        gthr[q] = buf[ck - 1];
-        qslot_off[q + 1] = q + 1;
-        if (q == 0) qslot_off[0] = 0;
-    }
+    for (int i = n + tid; i < P; i += FS_THREADS) buf[i] = KEY_EMPTY;
+    __syncthreads();
+    block_bitonic_sort(buf, P);
+    for (int i = tid; i < ck; i += FS_THREADS) cand[(int64_t)q * ck + i] = buf[i];
+    if (tid == 0) gthr[q] = buf[ck - 1];
 }
 
 }  // namespace
@@ -924,7 +972,7 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
         JHQ_CUDA(cudaFuncSetAttribute(flat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       ft_smem_bytes(128)));
         JHQ_CUDA(cudaFuncSetAttribute(flat_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      227 * 1024));
+                                      FS_SMEM_MAX));
     });
     int dev = 0, nsm = 0;
     JHQ_CUDA(cudaGetDevice(&dev));
@@ -948,9 +996,9 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
         count_launch(2);
     }
     if (a.scores_only) return;                     // diagnostics: the approximate scores
-    const size_t smem = (size_t)FS_WARPS * fs_warp_bytes(a.M, ntiles_pad);
-    if (smem > 227 * 1024) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
-    flat_select_kernel<<<(unsigned)ceil_div(a.nq, FS_WARPS), FS_WARPS * 32, smem, s>>>(
+    const size_t smem = fs_smem_bytes(a.M, ntiles_pad);
+    if (smem > (size_t)FS_SMEM_MAX) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
+    flat_select_kernel<<<(unsigned)a.nq, FS_THREADS, smem, s>>>(
         a.q_rot, a.c1d, a.codes, scores, tmin, a.nvec, a.M, a.nq, a.ck, a.ck_pad, ntiles,
         ntiles_pad, cmax, ec, Dc, a.cand, a.gthr, a.qslot_off, a.d_nvalid);
     JHQ_LAUNCH_CHECK();
