@@ -475,25 +475,45 @@ namespace {
 //   s_v = sum_j (q_j - c[b_j])^2 = S0 + D * pop(v) - 2 e * (q . b_v),
 //   S0 = sum_j (q_j - c0)^2,  D = c1^2 - c0^2,  e = c1 - c0,  pop = popcount,
 // so the ADC distance of every (vector, query) pair is one GEMM of the code
-// bits with the queries. flat_tc_kernel computes g = q . b on tcgen05: the A
-// operand (128 vectors x 64 dims per K chunk) is expanded from the code bytes
-// to bf16 0/1 in shared memory by four warps (the 128-byte swizzled K-major
-// layout the TMA would produce: row r at r*128 bytes, 16-byte chunk c stored
-// at c ^ (r & 7)); the B operand is the query block split in bf16 hi / lo
-// planes (TMA); the two MMAs per K step accumulate q_hi.b + q_lo.b in fp32
-// TMEM. The epilogue forms s~ = S0 + D pop - 2 e g, stores it [q][v] and the
-// per-query minimum of each 128-vector tile. The scores are approximate;
-// flat_select (below) turns them into the exact top-ck of the LUT-path keys.
-// Same bounded-wait / abort / drain discipline as coarse_tc_kernel.
-constexpr int FT_BM = 128, FT_BK = 64;
-constexpr int FT_THREADS = 9 * 32;            // warps 0-3 expand A (+TMA), 4 MMA, 5-8 epilogue
-constexpr int FT_A_BYTES = FT_BM * FT_BK * 2; // 16 KB
+// bits with the queries. flat_tc_kernel computes g = q . b on tcgen05 in
+// integer arithmetic (kind::i8, exact s32 accumulation):
+//   * each query is quantised to Q = rint(q / s), s = max|q| / 32000, and Q is
+//     split in two signed bytes Q = 256 Qh + Ql; the residual
+//     R1 = sum_j |q_j - s Q_j| bounds |q . b - s Q . b| for every b;
+//   * the B operand (the block's Qh rows, then its Ql rows, all K) is loaded
+//     into shared memory once per CTA by TMA and stays there;
+//   * the A operand (128 vectors x 128 dims per K chunk) is expanded from the
+//     code bytes to s8 0/1 in shared memory by four warps, in the 128-byte
+//     swizzled K-major layout a TMA would produce (row r at r * 128 bytes,
+//     16-byte chunk c stored at c ^ (r & 7));
+//   * one MMA of N' = 2N columns per 32-dim step: TMEM columns [0, N) collect
+//     Qh . b and [N, 2N) Ql . b.
+// The epilogue forms g~ = s (256 Gh + Gl), s~ = S0 + D pop - 2 e g~, stores s~
+// [q][v] and the per-query minimum of each 128-vector tile. The scores are
+// approximate; flat_select (below) turns them into the exact top-ck of the
+// LUT-path keys. Same bounded-wait / abort / drain discipline as
+// coarse_tc_kernel.
+constexpr int FT_BM = 128, FT_BK = 128;       // BK in bytes = dims (u8 / s8 operands)
+constexpr int FT_THREADS = 9 * 32;            // warps 0-3 expand A (+ the B load), 4 MMA, 5-8 epilogue
+constexpr int FT_A_BYTES = FT_BM * FT_BK;     // 16 KB per stage
+constexpr int FT_B_MAX = 128 * 1024;          // resident query block
+constexpr int FT_SMEM_MAX = 227 * 1024;
+constexpr float FT_QMAX = 32000.0f;           // |Q| bound: Qh in [-125, 125], Ql in [-128, 127]
 
-__host__ __device__ inline int ft_stages(int N) { return N <= 64 ? 4 : 3; }
-__host__ __device__ inline int ft_stage_bytes(int N) { return FT_A_BYTES + 2 * N * FT_BK * 2; }
-__host__ __device__ inline int ft_smem_bytes(int N) { return ft_stages(N) * ft_stage_bytes(N) + 1024 + 256; }
+// queries per block for dimension d: the resident 2N x d bytes fit FT_B_MAX
+__host__ __device__ inline int ft_block_queries(int d) {
+    const int n = FT_B_MAX / (2 * d) / 32 * 32;
+    return n < 128 ? n : 128;
+}
+__host__ __device__ inline int ft_stages(int N, int d) {
+    const int s = (FT_SMEM_MAX - 2048 - 2 * N * d) / FT_A_BYTES;
+    return s < 6 ? s : 6;
+}
+__host__ __device__ inline int ft_smem_bytes(int N, int d) {
+    return 2 * N * d + ft_stages(N, d) * FT_A_BYTES + 1024 + 256;
+}
 
-// 32 consecutive fp32 TMEM columns of this warp's 32 lanes
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -507,32 +527,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
+// bits 0-3 of x -> bytes 0-3 of the result, each 0 or 1 (the four shifted
+// copies of x occupy disjoint bit ranges, so the product has no carries)
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
+
 __global__ void __launch_bounds__(FT_THREADS, 1)
 flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restrict__ codes,
-               const int32_t* __restrict__ pop, const float* __restrict__ S0, int nvec, int M,
-               int nq, int N, float Dc, float ec, float* __restrict__ scores,
-               uint32_t* __restrict__ tile_min, int ntiles, long long wait_limit) {
+               const int32_t* __restrict__ pop, const float* __restrict__ S0,
+               const float* __restrict__ qscale, int nvec, int M, int nq, int N, float Dc,
+               float ec, float* __restrict__ scores, uint32_t* __restrict__ tile_min, int ntiles,
+               long long wait_limit) {
     extern __shared__ uint8_t smem_raw[];
+    const int d = M * 8, nk = d / FT_BK;
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    const int S = ft_stages(N), SB = ft_stage_bytes(N);
-    uint64_t* bars = (uint64_t*)(smem + S * SB);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 4 + 1);
+    uint8_t* bsm = smem;                                   // [nk][2N][128] resident B
+    uint8_t* asm_ = smem + 2 * N * d;                      // [S][128][128] A stages
+    const int S = ft_stages(N, d);
+    uint64_t* bars = (uint64_t*)(asm_ + S * FT_A_BYTES);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 6);
     volatile int* abort = (volatile int*)(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int d = M * 8, nk = d / FT_BK;
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, tfull0 = empty0 + 8 * S,
-                   tempty0 = tfull0 + 16, drain = tempty0 + 16;
-    // one MMA of N' = 2N: the hi and lo planes are consecutive B rows, so TMEM
-    // columns [0, N) accumulate q_hi . b and [N, 2N) q_lo . b
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(2 * N >> 3) << 17) |
+                   tempty0 = tfull0 + 16, drain = tempty0 + 16, bfull = drain + 8;
+    // s32 accumulate (bits 4-5 = 2), A and B s8 (bits 7-9, 10-12 = 1; the code
+    // bits are 0 / 1), both K-major, N' = 2N at bit 17, M at bit 24
+    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(2 * N >> 3) << 17) |
                            ((uint32_t)(FT_BM >> 4) << 24);
     uint32_t cols = 32;
     while (cols < (uint32_t)(4 * N)) cols <<= 1;
     if (tid == 0) {
-        for (int i = 0; i < 2 * S + 5; ++i) {
+        for (int i = 0; i < 2 * S + 6; ++i) {
             const uint32_t a = full0 + 8 * i;
             uint32_t cnt = 1;
-            if (a < empty0) cnt = 128 + 1;                 // 128 expanders + the TMA arrive
+            if (a < empty0) cnt = 128;                     // the 128 expanders
             else if (a >= tempty0 && a < drain) cnt = 128; // epilogue threads
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(a), "r"(cnt));
         }
@@ -549,81 +576,83 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {                                        // A expansion (+ B by TMA)
+    if (warp < 4) {                                        // A expansion (+ the B load)
         const int r = tid;                                 // tile row = vector
-        int it = 0;
-        bool stop = false;
-        // the code bytes of the next chunk are loaded one chunk ahead (across
-        // tiles too), so their latency overlaps the wait and expansion of this one
-        auto load_cw = [&](int t, int kc) {
+        if (r == 0) {
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                         :: "r"(bfull), "r"((uint32_t)(2 * N * d)) : "memory");
+            for (int kb = 0; kb < nk; ++kb)
+                tma_load_2d(smem_u32(bsm + kb * 2 * N * FT_BK), &map_q, kb * FT_BK, 0, bfull);
+        }
+        // the CTA's (tile, K chunk) items in order: item i is chunk i % nk of the
+        // CTA's tile i / nk. The code bytes of a group of 8 items are loaded
+        // while the previous group is expanded (8 loads in flight per thread).
+        const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+        const int total = my_tiles * nk;
+        auto load_item = [&](int item) {
+            const int t = blockIdx.x + (item / nk) * gridDim.x, kc = item % nk;
             const int v = t * FT_BM + r;
-            return (t < ntiles && v < nvec)
-                       ? __ldg(reinterpret_cast<const uint2*>(codes + (int64_t)v * M + kc * 8))
-                       : make_uint2(0u, 0u);
+            return (item < total && v < nvec)
+                       ? __ldg(reinterpret_cast<const uint4*>(codes + (int64_t)v * M + kc * 16))
+                       : make_uint4(0u, 0u, 0u, 0u);
         };
-        uint2 cw_next = load_cw(blockIdx.x, 0);
-        for (int t = blockIdx.x; t < ntiles && !stop && !*abort; t += gridDim.x) {
-            for (int kc = 0; kc < nk; ++kc, ++it) {
-                const uint2 cw = cw_next;
-                cw_next = kc + 1 < nk ? load_cw(t, kc + 1) : load_cw(t + gridDim.x, 0);
+        uint4 cur[8], nxt[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cur[j] = load_item(j);
+        bool stop = false;
+        for (int g = 0; g * 8 < total && !stop && !*abort; ++g) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nxt[j] = load_item((g + 1) * 8 + j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int it = g * 8 + j;
+                if (it >= total) break;
                 const int s = it % S;
                 if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) - 1) & 1, abort, wait_limit)) {
                     stop = true;
                     break;
                 }
-                uint8_t* st = smem + s * SB;
-                if (r == 0) {
-                    const uint32_t fb = full0 + 8 * s;
-                    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
-                                 :: "r"(fb), "r"((uint32_t)(2 * N * FT_BK * 2)) : "memory");
-                    const uint32_t b_s = smem_u32(st + FT_A_BYTES);
-                    tma_load_2d(b_s, &map_q, kc * FT_BK, 0, fb);                       // q_hi
-                    tma_load_2d(b_s + N * FT_BK * 2, &map_q, kc * FT_BK, N, fb);       // q_lo
-                }
-                uint8_t* row = st + (r >> 3) * 1024 + (r & 7) * 128;
+                uint8_t* row = asm_ + s * FT_A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
+                const uint32_t w[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const uint32_t byte = ((i < 4 ? cw.x : cw.y) >> ((i & 3) * 8)) & 0xFFu;
-                    uint32_t w[4];
-#pragma unroll
-                    for (int h = 0; h < 4; ++h)
-                        w[h] = (((byte >> (2 * h)) & 1u) ? 0x3F80u : 0u) |
-                               (((byte >> (2 * h + 1)) & 1u) ? 0x3F800000u : 0u);
-                    *reinterpret_cast<uint4*>(row + ((i ^ (r & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
+                for (int c = 0; c < 8; ++c) {              // 16 dims = code bytes 2c, 2c + 1
+                    const uint32_t b2 = w[c >> 1] >> ((c & 1) * 16);
+                    const uint4 o = make_uint4(spread4(b2 & 15u), spread4((b2 >> 4) & 15u),
+                                               spread4((b2 >> 8) & 15u), spread4((b2 >> 12) & 15u));
+                    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = o;
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(full0 + 8 * s)
                              : "memory");
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
         }
-        // every stage this thread armed must complete (its TMA bytes) before exit
-        if (r == 0 && *abort)
-            for (int j = it > S ? it - S : 0; j < it; ++j)
-                mbar_wait(full0 + 8 * (j % S), (j / S) & 1, nullptr);
+        // the B copy must complete before the CTA exits
+        if (r == 0) mbar_wait(bfull, 0, nullptr);
     } else if (warp == 4) {
         if (lane == 0) {                                   // MMA issuer
             int it = 0, i = 0;
-            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++i) {
+            bool ok = mbar_wait(bfull, 0, abort, wait_limit);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            for (int t = blockIdx.x; ok && t < ntiles && !*abort; t += gridDim.x, ++i) {
                 const int acc = i & 1;
                 if (i >= 2 && !mbar_wait(tempty0 + 8 * acc, ((i >> 1) - 1) & 1, abort, wait_limit))
                     break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d_tmem = tmem + (uint32_t)(acc * 2 * N);
-                bool ok = true;
                 for (int kc = 0; kc < nk; ++kc, ++it) {
                     const int s = it % S;
                     if (!mbar_wait(full0 + 8 * s, (it / S) & 1, abort, wait_limit)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t a_s = smem_u32(smem + s * SB);
-                    const uint64_t da = sw128_desc(a_s);
-                    const uint64_t db = sw128_desc(a_s + FT_A_BYTES);   // hi rows, then lo rows
+                    const uint64_t da = sw128_desc(smem_u32(asm_ + s * FT_A_BYTES));
+                    const uint64_t db = sw128_desc(smem_u32(bsm + kc * 2 * N * FT_BK));  // Qh rows, then Ql
 #pragma unroll
-                    for (int k = 0; k < FT_BK / 16; ++k) {
+                    for (int k = 0; k < FT_BK / 32; ++k) {   // 32 dims = 32 bytes per MMA
                         const uint32_t accum = (kc | k) != 0;
                         asm volatile(
                             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
                             :: "r"(d_tmem), "l"(da + 2 * k), "l"(db + 2 * k), "r"(idesc), "r"(accum));
                     }
                     mma_commit(empty0 + 8 * s);
@@ -656,7 +685,9 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                     const int q = cb + c;
                     m[c] = __int_as_float(0x7f800000);
                     if (q < nq) {                                       // warp-uniform
-                        const float g = __uint_as_float(rh[c]) + __uint_as_float(rl[c]);
+                        // |256 Gh + Gl| <= 32000 d: exact in int32
+                        const int gi = (int)rh[c] * 256 + (int)rl[c];
+                        const float g = __fmul_rn(__ldg(qscale + q), (float)gi);
                         const float sv = __fmaf_rn(-2.0f * ec, g, __fmaf_rn(Dc, pv, __ldg(S0 + q)));
                         if (v < nvec) {
                             scores[(int64_t)q * nvec + v] = sv;
@@ -670,10 +701,10 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                 for (int h = 16; h; h >>= 1) {
                     const bool up = lane & h;
 #pragma unroll
-                    for (int i = 0; i < h; ++i) {
-                        const float send = up ? m[i] : m[i + h];
-                        const float keep = up ? m[i + h] : m[i];
-                        m[i] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+                    for (int j = 0; j < h; ++j) {
+                        const float send = up ? m[j] : m[j + h];
+                        const float keep = up ? m[j + h] : m[j];
+                        m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
                     }
                 }
                 if (cb + lane < nq)
@@ -692,31 +723,58 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
 }
 
 
-// Per query block row q < nq: the bf16 hi / lo planes q2[0][q], q2[1][q] (rows
-// nq..N-1 zero) and S0[q] = sum_j (q_j - c0)^2 (a per-query constant: its
-// rounding shifts every s~ of the query alike and cancels in the selection).
+// Per query block row q < nq: the signed byte planes q8[q] = Qh, q8[N + q] =
+// Ql of Q = rint(q / s), s = max|q| / 32000 (rows nq..N-1 zero), and per query
+// S0 = sum_j (q_j - c0)^2 (a per-query constant: its rounding shifts every s~
+// of the query alike and cancels in the selection), the scale s and the
+// quantisation residual R1 = sum_j |q_j - s Q_j|.
 __global__ void flat_prep_kernel(const float* __restrict__ q_rot, int nq, int N, int d, float c0,
-                                 uint16_t* __restrict__ q2, float* __restrict__ S0) {
+                                 int8_t* __restrict__ q8, float* __restrict__ S0,
+                                 float* __restrict__ qscale, float* __restrict__ R1) {
     const int q = blockIdx.x;
-    float acc = 0.0f;
+    __shared__ float red[2][32];
+    __shared__ float s_sh;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float amax = 0.0f;
+    for (int j = threadIdx.x; j < d; j += blockDim.x)
+        amax = fmaxf(amax, q < nq ? fabsf(q_rot[(int64_t)q * d + j]) : 0.0f);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[0][warp] = amax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.0f;
+        for (int w = 0; w < nw; ++w) a = fmaxf(a, red[0][w]);
+        s_sh = a > 0.0f ? a / FT_QMAX : 1.0f;
+    }
+    __syncthreads();
+    const float sc = s_sh;
+    float acc = 0.0f, res = 0.0f;
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
         const float x = q < nq ? q_rot[(int64_t)q * d + j] : 0.0f;
-        const uint16_t hi = bf16_rne(__float_as_uint(x));
-        const uint16_t lo = bf16_rne(__float_as_uint(x - __uint_as_float((uint32_t)hi << 16)));
-        q2[(int64_t)q * d + j] = hi;
-        q2[((int64_t)N + q) * d + j] = lo;
+        const float Qf = fminf(fmaxf(rintf(x / sc), -FT_QMAX), FT_QMAX);
+        const int Q = (int)Qf;
+        const int qh = (Q + 128) >> 8;                 // floor((Q + 128) / 256)
+        q8[(int64_t)q * d + j] = (int8_t)qh;
+        q8[((int64_t)N + q) * d + j] = (int8_t)(Q - qh * 256);
+        res += fabsf(__fmaf_rn(-sc, Qf, x));
         const float t = x - c0;
         acc = __fmaf_rn(t, t, acc);
     }
-    __shared__ float red[32];
+    __syncthreads();
 #pragma unroll
-    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    for (int o = 16; o; o >>= 1) {
+        acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        res += __shfl_xor_sync(0xffffffffu, res, o);
+    }
+    if (lane == 0) { red[0][warp] = acc; red[1][warp] = res; }
     __syncthreads();
     if (threadIdx.x == 0 && q < nq) {
-        float tot = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        float tot = 0.0f, rt = 0.0f;
+        for (int w = 0; w < nw; ++w) { tot += red[0][w]; rt += red[1][w]; }
         S0[q] = tot;
+        qscale[q] = sc;
+        R1[q] = rt;
     }
 }
 
@@ -743,9 +801,9 @@ __host__ __device__ inline size_t fs_smem_bytes(int M, int ntiles_pad) {
 __global__ void __launch_bounds__(FS_THREADS, 1)
 flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1d_g,
                    const uint8_t* __restrict__ codes, const float* __restrict__ scores,
-                   const uint32_t* __restrict__ tile_min, int nvec, int M, int nq, int ck,
-                   int ck_pad, int ntiles, int ntiles_pad, float cmax, float ec, float Dc,
-                   uint64_t* __restrict__ cand, uint64_t* __restrict__ gthr,
+                   const uint32_t* __restrict__ tile_min, const float* __restrict__ R1q, int nvec,
+                   int M, int nq, int ck, int ck_pad, int ntiles, int ntiles_pad, float cmax,
+                   float ec, float Dc, uint64_t* __restrict__ cand, uint64_t* __restrict__ gthr,
                    int64_t* __restrict__ qslot_off, const int* __restrict__ d_nvalid) {
     extern __shared__ __align__(16) unsigned char fs_smem[];
     __shared__ float red[3][FS_THREADS / 32];
@@ -777,7 +835,8 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
     const unsigned lt = (1u << lane) - 1u;
 
     // error bound (all but per-query constants): LUT-path rounding of s, the
-    // bf16 split and fp32 tensor accumulation of g, and the roundings forming s~
+    // quantisation of q (R1: exact integer products and sums after it), and the
+    // roundings forming g~ and s~
     float V = 0.0f, L1 = 0.0f, S0 = 0.0f;
     for (int j = tid; j < d; j += FS_THREADS) {
         const float x = qv[j], a = fabsf(x) + cmax, t = x - c0;
@@ -809,12 +868,13 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
     V = L1 = S0 = 0.0f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) { V += red[0][w]; L1 += red[1][w]; S0 += red[2][w]; }
-    // the 1.001 factors cover the fp32 rounding of V and S0 themselves
+    // the 1.001 factors cover the fp32 rounding of V, S0 and R1 themselves
     const float u = 5.9604645e-08f;                                    // 2^-24
-    const float aD = fabsf(Dc), ae = fabsf(ec);
+    const float aD = fabsf(Dc), ae = fabsf(ec), R1 = R1q[q] * 1.001f;
+    const float G = (L1 + R1) * 1.001f;                                // bounds |g~|
     const float E = 1.1f * (V * 1.001f * (float)(2 * M + 16) * u + aD * (float)d * u +
-                            2.0f * ae * L1 * (3.8146973e-06f + (float)(2 * d) * 1.1920929e-07f) +
-                            2.0f * u * (S0 + aD * (float)d + 2.0f * ae * L1) * 1.001f);
+                            2.0f * ae * (R1 + 2.0f * u * G) +
+                            2.0f * u * (S0 * 1.001f + aD * (float)d + 2.0f * ae * G));
 
     // tau = the ck-th smallest tile minimum: bisection over the order keys
     // (one barrier per step: the warp counts alternate between two rows)
@@ -934,43 +994,76 @@ flat_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1
 }  // namespace
 
 bool flat_tc_supported(int d, int M, int B, int nvec) {
-    return M > 0 && d == 8 * M && B == 8 && M % 16 == 0 && nvec > 0 &&
-           (nvec + FT_BM - 1) / FT_BM <= FS_TILES;
+    return M > 0 && d == 8 * M && B == 8 && M % 16 == 0 && ft_block_queries(d) >= 32 &&
+           nvec > 0 && (nvec + FT_BM - 1) / FT_BM <= FS_TILES;
 }
 
-float* flat_tc_scores_of(void* scratch, int Bq, int d) {
-    const int Nb = std::min(128, (Bq + 31) / 32 * 32);
-    unsigned char* p = reinterpret_cast<unsigned char*>(scratch);
-    p += (((size_t)2 * Nb * d * 2) + 255) & ~size_t(255);
-    p += (((size_t)Bq * 4) + 255) & ~size_t(255);
-    return reinterpret_cast<float*>(p);
+namespace {
+// scratch carve: q8 [2][Nb][d] s8, S0 / scale / R1 [Bq], scores [Bq][nvec],
+// tile_min [Bq][ntiles], each 256-byte aligned
+struct FlatScratch {
+    int8_t* q8;
+    float *S0, *qscale, *R1, *scores;
+    uint32_t* tmin;
+    size_t bytes;
+};
+FlatScratch flat_carve(void* base, int Bq, int d, int nvec) {
+    const int Nb = std::min(ft_block_queries(d), (Bq + 31) / 32 * 32);
+    const int ntiles = (nvec + FT_BM - 1) / FT_BM;
+    const uintptr_t p = reinterpret_cast<uintptr_t>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        void* r = reinterpret_cast<void*>(p + off);
+        off += (bytes + 255) & ~size_t(255);
+        return r;
+    };
+    FlatScratch f;
+    f.q8 = reinterpret_cast<int8_t*>(take((size_t)2 * Nb * d));
+    f.S0 = reinterpret_cast<float*>(take((size_t)Bq * 4));
+    f.qscale = reinterpret_cast<float*>(take((size_t)Bq * 4));
+    f.R1 = reinterpret_cast<float*>(take((size_t)Bq * 4));
+    f.scores = reinterpret_cast<float*>(take((size_t)Bq * nvec * 4));
+    f.tmin = reinterpret_cast<uint32_t*>(take((size_t)Bq * ntiles * 4));
+    f.bytes = off;
+    return f;
+}
+
+// [rows][K] s8 row-major, boxes of box_rows x 128 bytes, 128-byte swizzle
+CUtensorMap make_map_s8(const int8_t* base, int64_t rows, int K, int box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)FT_BK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)base, dims,
+                                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(JHQ_EDEVICE, "flat_search_tc: tensor map encoding failed");
+    return m;
+}
+}  // namespace
+
+float* flat_tc_scores_of(void* scratch, int Bq, int d, int nvec) {
+    return flat_carve(scratch, Bq, d, nvec).scores;
 }
 
 size_t flat_tc_scratch_bytes(int Bq, int d, int nvec) {
-    const int Nb = std::min(128, (Bq + 31) / 32 * 32);
-    const int ntiles = (nvec + FT_BM - 1) / FT_BM;
-    return (size_t)2 * Nb * d * 2 + 256 + (size_t)Bq * 4 + 256 + (size_t)Bq * nvec * 4 + 256 +
-           (size_t)Bq * ntiles * 4 + 256;
+    return flat_carve(nullptr, Bq, d, nvec).bytes + 256;
 }
 
 void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
     if (a.nq <= 0) return;
     const int d = a.M * 8, ntiles = (a.nvec + FT_BM - 1) / FT_BM;
+    if (!flat_tc_supported(d, a.M, 8, a.nvec)) fail(JHQ_EINVAL, "flat_search_tc: unsupported shape");
     int ntiles_pad = 32;
     while (ntiles_pad < ntiles) ntiles_pad <<= 1;
-    const int Nb = std::min(128, (a.nq + 31) / 32 * 32);
-    // scratch carve: q2 [2][Nb][d] bf16, S0 [nq], scores [nq][nvec], tile_min [nq][ntiles]
-    unsigned char* p = reinterpret_cast<unsigned char*>(a.scratch);
-    auto take = [&](size_t bytes) { unsigned char* r = p; p += (bytes + 255) & ~size_t(255); return r; };
-    uint16_t* q2 = reinterpret_cast<uint16_t*>(take((size_t)2 * Nb * d * 2));
-    float* S0 = reinterpret_cast<float*>(take((size_t)a.nq * 4));
-    float* scores = reinterpret_cast<float*>(take((size_t)a.nq * a.nvec * 4));
-    uint32_t* tmin = reinterpret_cast<uint32_t*>(take((size_t)a.nq * ntiles * 4));
-    JHQ_CUDA(cudaMemsetAsync(tmin, 0xFF, (size_t)a.nq * ntiles * 4, s));
+    const FlatScratch f = flat_carve(a.scratch, a.nq, d, a.nvec);
+    JHQ_CUDA(cudaMemsetAsync(f.tmin, 0xFF, (size_t)a.nq * ntiles * 4, s));
     static std::atomic<uint64_t> attr{0};
     once_per_device(attr, [] {
         JHQ_CUDA(cudaFuncSetAttribute(flat_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      ft_smem_bytes(128)));
+                                      FT_SMEM_MAX));
         JHQ_CUDA(cudaFuncSetAttribute(flat_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       FS_SMEM_MAX));
     });
@@ -982,16 +1075,20 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
     const float c0 = a.c1d_host[0], c1 = a.c1d_host[1];
     const float Dc = c1 * c1 - c0 * c0, ec = c1 - c0;
     const float cmax = std::max(std::fabs(c0), std::fabs(c1));
-    for (int q0 = 0; q0 < a.nq; q0 += 128) {
-        const int nqb = std::min(128, a.nq - q0);
+    const int NB = ft_block_queries(d);
+    for (int q0 = 0; q0 < a.nq; q0 += NB) {
+        const int nqb = std::min(NB, a.nq - q0);
         const int N = (nqb + 31) / 32 * 32;        // the epilogue reads 32 TMEM columns at a time
-        flat_prep_kernel<<<N, 256, 0, s>>>(a.q_rot + (int64_t)q0 * d, nqb, N, d, c0, q2, S0 + q0);
+        flat_prep_kernel<<<N, 256, 0, s>>>(a.q_rot + (int64_t)q0 * d, nqb, N, d, c0, f.q8,
+                                           f.S0 + q0, f.qscale + q0, f.R1 + q0);
         JHQ_LAUNCH_CHECK();
-        const CUtensorMap mq = make_map(q2, 2 * N, d, N);
+        const CUtensorMap mq = make_map_s8(f.q8, 2 * N, d, 2 * N);
         const int grid = std::min(ntiles, nsm);
-        flat_tc_kernel<<<grid, FT_THREADS, ft_smem_bytes(N), s>>>(
-            mq, a.codes, a.pop, S0 + q0, a.nvec, a.M, nqb, N, Dc, ec, scores + (int64_t)q0 * a.nvec,
-            tmin + (int64_t)q0 * ntiles, ntiles, wait_limit);
+        if (ft_smem_bytes(N, d) > FT_SMEM_MAX || ft_stages(N, d) < 2)
+            fail(JHQ_EINVAL, "flat_search_tc: shared memory plan");
+        flat_tc_kernel<<<grid, FT_THREADS, ft_smem_bytes(N, d), s>>>(
+            mq, a.codes, a.pop, f.S0 + q0, f.qscale + q0, a.nvec, a.M, nqb, N, Dc, ec,
+            f.scores + (int64_t)q0 * a.nvec, f.tmin + (int64_t)q0 * ntiles, ntiles, wait_limit);
         JHQ_LAUNCH_CHECK();
         count_launch(2);
     }
@@ -999,7 +1096,7 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
     const size_t smem = fs_smem_bytes(a.M, ntiles_pad);
     if (smem > (size_t)FS_SMEM_MAX) fail(JHQ_EINVAL, "flat_search_tc: selection buffers too large");
     flat_select_kernel<<<(unsigned)a.nq, FS_THREADS, smem, s>>>(
-        a.q_rot, a.c1d, a.codes, scores, tmin, a.nvec, a.M, a.nq, a.ck, a.ck_pad, ntiles,
+        a.q_rot, a.c1d, a.codes, f.scores, f.tmin, f.R1, a.nvec, a.M, a.nq, a.ck, a.ck_pad, ntiles,
         ntiles_pad, cmax, ec, Dc, a.cand, a.gthr, a.qslot_off, a.d_nvalid);
     JHQ_LAUNCH_CHECK();
     count_launch();

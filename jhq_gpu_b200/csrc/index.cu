@@ -1077,7 +1077,7 @@ bool Index::flat_tc_scores(const float* h_q, int nq, float* h_scores) {
     fa.scratch = fl.get(); fa.cand = cand.get(); fa.gthr = gth.get(); fa.qslot_off = qs.get();
     fa.scores_only = true;
     flat_search_tc(fa, stream_);
-    d2h(h_scores, flat_tc_scores_of(fl.get(), nq, d_), (size_t)nq * ntotal_, stream_);
+    d2h(h_scores, flat_tc_scores_of(fl.get(), nq, d_, (int)ntotal_), (size_t)nq * ntotal_, stream_);
     JHQ_CUDA(cudaStreamSynchronize(stream_));
     return true;
 }

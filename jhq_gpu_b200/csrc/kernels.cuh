@@ -197,7 +197,7 @@ struct FlatTcArgs {
     bool scores_only = false;    // stop after the GEMM (diagnostics)
 };
 // the approximate scores [nq][nvec] inside a flat_search_tc scratch block
-float* flat_tc_scores_of(void* scratch, int Bq, int d);
+float* flat_tc_scores_of(void* scratch, int Bq, int d, int nvec);
 bool flat_tc_supported(int d, int M, int B, int nvec);
 size_t flat_tc_scratch_bytes(int Bq, int d, int nvec);
 void flat_search_tc(const FlatTcArgs& a, cudaStream_t s);
