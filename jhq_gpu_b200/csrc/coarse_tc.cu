@@ -483,18 +483,22 @@ namespace {
 //   * the B operand (the block's Qh rows, then its Ql rows, all K) is loaded
 //     into shared memory once per CTA by TMA and stays there;
 //   * the A operand (128 vectors x 128 dims per K chunk) is expanded from the
-//     code bytes to s8 0/1 in shared memory by four warps, in the 128-byte
-//     swizzled K-major layout a TMA would produce (row r at r * 128 bytes,
-//     16-byte chunk c stored at c ^ (r & 7));
+//     code bytes to s8 0/1 in shared memory by eight warps (two threads per
+//     row), in the 128-byte swizzled K-major layout a TMA would produce (row r
+//     at r * 128 bytes, 16-byte chunk c stored at c ^ (r & 7));
 //   * one MMA of N' = 2N columns per 32-dim step: TMEM columns [0, N) collect
 //     Qh . b and [N, 2N) Ql . b.
-// The epilogue forms g~ = s (256 Gh + Gl), s~ = S0 + D pop - 2 e g~, stores s~
-// [q][v] and the per-query minimum of each 128-vector tile. The scores are
+// Eight epilogue warps (two per TMEM lane quarter, alternating 32-column
+// blocks) form s~ = S0 + D pop + (-2 e s) (256 Gh + Gl), store s~ [q][v] and
+// the per-query minimum of each 128-vector tile. The scores are
 // approximate; flat_select (below) turns them into the exact top-ck of the
 // LUT-path keys. Same bounded-wait / abort / drain discipline as
 // coarse_tc_kernel.
 constexpr int FT_BM = 128, FT_BK = 128;       // BK in bytes = dims (u8 / s8 operands)
-constexpr int FT_THREADS = 9 * 32;            // warps 0-3 expand A (+ the B load), 4 MMA, 5-8 epilogue
+constexpr int FT_EXP = 256;                  // expander threads: two per tile row (64 dims each)
+constexpr int FT_MMA_WARP = FT_EXP / 32;      // warp 8 issues the MMAs
+constexpr int FT_EPI = 256;                   // epilogue threads: two warps per TMEM lane quarter
+constexpr int FT_THREADS = FT_EXP + 32 + FT_EPI;
 constexpr int FT_A_BYTES = FT_BM * FT_BK;     // 16 KB per stage
 constexpr int FT_B_MAX = 128 * 1024;          // resident query block
 constexpr int FT_SMEM_MAX = 227 * 1024;
@@ -506,11 +510,11 @@ __host__ __device__ inline int ft_block_queries(int d) {
     return n < 128 ? n : 128;
 }
 __host__ __device__ inline int ft_stages(int N, int d) {
-    const int s = (FT_SMEM_MAX - 2048 - 2 * N * d) / FT_A_BYTES;
+    const int s = (FT_SMEM_MAX - 3072 - 2 * N * d) / FT_A_BYTES;
     return s < 6 ? s : 6;
 }
 __host__ __device__ inline int ft_smem_bytes(int N, int d) {
-    return 2 * N * d + ft_stages(N, d) * FT_A_BYTES + 1024 + 256;
+    return 2 * N * d + ft_stages(N, d) * FT_A_BYTES + 1024 + 256 + 1024;
 }
 
 // 32 consecutive 32-bit TMEM columns of this warp's 32 lanes
@@ -545,6 +549,7 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
     const int S = ft_stages(N, d);
     uint64_t* bars = (uint64_t*)(asm_ + S * FT_A_BYTES);
     uint32_t* tmem_slot = (uint32_t*)(bars + 2 * S + 6);
+    float* cst = (float*)(asm_ + S * FT_A_BYTES + 256);    // [2][128] epilogue constants
     volatile int* abort = (volatile int*)(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, tfull0 = empty0 + 8 * S,
@@ -559,14 +564,14 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
         for (int i = 0; i < 2 * S + 6; ++i) {
             const uint32_t a = full0 + 8 * i;
             uint32_t cnt = 1;
-            if (a < empty0) cnt = 128;                     // the 128 expanders
-            else if (a >= tempty0 && a < drain) cnt = 128; // epilogue threads
+            if (a < empty0) cnt = FT_EXP;                  // the expanders
+            else if (a >= tempty0 && a < drain) cnt = FT_EPI; // epilogue threads
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(a), "r"(cnt));
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *abort = 0;
     }
-    if (warp == 4) {
+    if (warp == FT_MMA_WARP) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      :: "r"(smem_u32(tmem_slot)), "r"(cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -576,9 +581,10 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {                                        // A expansion (+ the B load)
-        const int r = tid;                                 // tile row = vector
-        if (r == 0) {
+    if (warp < FT_MMA_WARP) {                              // A expansion (+ the B load)
+        const int r = tid & (FT_BM - 1);                   // tile row = vector
+        const int hf = tid >> 7;                           // dims 64 hf .. 64 hf + 63 of a chunk
+        if (tid == 0) {
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                          :: "r"(bfull), "r"((uint32_t)(2 * N * d)) : "memory");
             for (int kb = 0; kb < nk; ++kb)
@@ -593,10 +599,10 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
             const int t = blockIdx.x + (item / nk) * gridDim.x, kc = item % nk;
             const int v = t * FT_BM + r;
             return (item < total && v < nvec)
-                       ? __ldg(reinterpret_cast<const uint4*>(codes + (int64_t)v * M + kc * 16))
-                       : make_uint4(0u, 0u, 0u, 0u);
+                       ? __ldg(reinterpret_cast<const uint2*>(codes + (int64_t)v * M + kc * 16 + hf * 8))
+                       : make_uint2(0u, 0u);
         };
-        uint4 cur[8], nxt[8];
+        uint2 cur[8], nxt[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) cur[j] = load_item(j);
         bool stop = false;
@@ -613,13 +619,13 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                     break;
                 }
                 uint8_t* row = asm_ + s * FT_A_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
-                const uint32_t w[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
+                const uint32_t w[2] = {cur[j].x, cur[j].y};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {              // 16 dims = code bytes 2c, 2c + 1
+                for (int c = 0; c < 4; ++c) {              // 16 dims = code bytes 2c, 2c + 1 of the half
                     const uint32_t b2 = w[c >> 1] >> ((c & 1) * 16);
                     const uint4 o = make_uint4(spread4(b2 & 15u), spread4((b2 >> 4) & 15u),
                                                spread4((b2 >> 8) & 15u), spread4((b2 >> 12) & 15u));
-                    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = o;
+                    *reinterpret_cast<uint4*>(row + (((hf * 4 + c) ^ (r & 7)) << 4)) = o;
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(full0 + 8 * s)
@@ -629,8 +635,8 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
             for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
         }
         // the B copy must complete before the CTA exits
-        if (r == 0) mbar_wait(bfull, 0, nullptr);
-    } else if (warp == 4) {
+        if (tid == 0) mbar_wait(bfull, 0, nullptr);
+    } else if (warp == FT_MMA_WARP) {
         if (lane == 0) {                                   // MMA issuer
             int it = 0, i = 0;
             bool ok = mbar_wait(bfull, 0, abort, wait_limit);
@@ -663,8 +669,15 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
             mma_commit(drain);
             mbar_wait(drain, 0, nullptr);
         }
-    } else {                                               // epilogue, warps 5-8
+    } else {                                               // epilogue, warps 9-16
         const int q4 = warp & 3;          // TMEM lane quarter: a warp reads lanes 32 (warp % 4) ..
+        const int half = (warp - FT_MMA_WARP - 1) >> 2;    // column blocks half, half + 2, ...
+        // per query column: S0 and -2 e s (one rounding, like the product it replaces)
+        for (int q = tid - FT_EXP - 32; q < N; q += FT_EPI) {
+            cst[q] = q < nq ? S0[q] : 0.0f;
+            cst[128 + q] = q < nq ? -2.0f * ec * qscale[q] : 0.0f;
+        }
+        asm volatile("bar.sync 1, %0;" :: "n"(FT_EPI) : "memory");
         int i = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
             const int acc = i & 1;
@@ -673,7 +686,7 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int v = t * FT_BM + q4 * 32 + lane;
             const float pv = v < nvec ? (float)__ldg(pop + v) : 0.0f;
-            for (int cb = 0; cb < N; cb += 32) {
+            for (int cb = half * 32; cb < N; cb += 64) {
                 uint32_t rh[32], rl[32];
                 const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(acc * 2 * N + cb);
                 tmem_ld32(taddr, rh);
@@ -687,8 +700,7 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
                     if (q < nq) {                                       // warp-uniform
                         // |256 Gh + Gl| <= 32000 d: exact in int32
                         const int gi = (int)rh[c] * 256 + (int)rl[c];
-                        const float g = __fmul_rn(__ldg(qscale + q), (float)gi);
-                        const float sv = __fmaf_rn(-2.0f * ec, g, __fmaf_rn(Dc, pv, __ldg(S0 + q)));
+                        const float sv = __fmaf_rn(cst[128 + q], (float)gi, __fmaf_rn(Dc, pv, cst[q]));
                         if (v < nvec) {
                             scores[(int64_t)q * nvec + v] = sv;
                             m[c] = sv;
@@ -718,7 +730,7 @@ flat_tc_kernel(const __grid_constant__ CUtensorMap map_q, const uint8_t* __restr
     __syncwarp();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 4)
+    if (warp == FT_MMA_WARP)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(cols));
 }
 

@@ -201,11 +201,14 @@ gemm_argmin_kernel(const float* __restrict__ A, const float* __restrict__ B,
 // Skinny path: CTA = SK_ROWS rows x SK_BN columns, 256 threads; thread
 // (column c, row group r) owns rows r*SK_TR .. r*SK_TR+SK_TR-1 of column c:
 // SK_TR (1 or 4) independent chains. Chunks of SK_KC rows of B (and the matching
-// SK_ROWS x SK_KC slice of A) are staged in shared memory by cp.async,
-// double-buffered. 16 rows per CTA keep the L2 re-reads of B (the d x d
+// SK_ROWS x SK_KC slice of A) are staged in shared memory by cp.async in a
+// ring of SK_STAGES buffers: a chunk computes in less time than an L2 round
+// trip, so SK_STAGES - 1 chunks are kept in flight. 16 rows per CTA keep the L2 re-reads of B (the d x d
 // rotation) at a quarter of a 4-row tiling.
-constexpr int SK_RG = 4, SK_BN = 64, SK_KC = 64;
+constexpr int SK_RG = 4, SK_BN = 64, SK_KC = 64, SK_STAGES = 6;
 constexpr int SK_THREADS = SK_BN * SK_RG;
+template <int SK_TR>
+constexpr int sk_smem_bytes() { return SK_STAGES * (SK_KC * SK_BN + SK_TR * SK_RG * SK_KC) * 4; }
 
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool ok) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
@@ -218,6 +221,8 @@ __device__ __forceinline__ void cp_async16(float* dst, const float* src, int byt
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N)); }
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n"); }
 
 template <int EPI, int SK_TR>
@@ -225,8 +230,9 @@ __global__ void __launch_bounds__(SK_THREADS)
 gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
                    int64_t R, int K, int N, const float* __restrict__ norms, int vec16) {
     constexpr int SK_ROWS = SK_TR * SK_RG;
-    __shared__ __align__(16) float Bs[2][SK_KC][SK_BN];
-    __shared__ __align__(16) float As[2][SK_ROWS][SK_KC];
+    extern __shared__ __align__(16) float sk_smem[];
+    auto Bs = reinterpret_cast<float (*)[SK_KC][SK_BN]>(sk_smem);
+    auto As = reinterpret_cast<float (*)[SK_ROWS][SK_KC]>(sk_smem + SK_STAGES * SK_KC * SK_BN);
     const int tid = threadIdx.x, col = tid % SK_BN, rg = tid / SK_BN;
     const int n0 = blockIdx.x * SK_BN;
     const int64_t r0 = (int64_t)blockIdx.y * SK_ROWS;
@@ -271,12 +277,17 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
 #pragma unroll
     for (int r = 0; r < SK_TR; ++r) acc[r] = 0.0f;
     const int nchunks = (K + SK_KC - 1) / SK_KC;
-    stage(0, 0);
+    for (int p = 0; p < SK_STAGES - 1; ++p) {
+        if (p < nchunks) stage(p, p * SK_KC);
+        else cp_async_commit();                      // empty group: uniform group counts
+    }
     for (int ch = 0; ch < nchunks; ++ch) {
-        const int buf = ch & 1;
-        if (ch + 1 < nchunks) { stage(buf ^ 1, (ch + 1) * SK_KC); cp_async_wait1(); }
-        else cp_async_wait0();
-        __syncthreads();
+        const int buf = ch % SK_STAGES;
+        cp_async_wait<SK_STAGES - 2>();              // chunk ch has landed
+        __syncthreads();                             // ... for every thread; chunk ch - 1 is consumed
+        const int nx = ch + SK_STAGES - 1;
+        if (nx < nchunks) stage(nx % SK_STAGES, nx * SK_KC);
+        else cp_async_commit();
         const int kl = min(SK_KC, K - ch * SK_KC);
         if (kl == SK_KC) {
 #pragma unroll
@@ -300,7 +311,6 @@ gemm_skinny_kernel(const float* __restrict__ A, const float* __restrict__ B, flo
                     acc[r] = __fmaf_rn(As[buf][rg * SK_TR + r][k], b, acc[r]);
             }
         }
-        __syncthreads();
     }
     if (n < N) {
 #pragma unroll
@@ -331,16 +341,16 @@ void gemm_rows(const float* A, const float* B, float* C, int64_t R, int K, int N
         dim3 grid((unsigned)ceil_div(N, SK_BN), (unsigned)ceil_div(R, tr * SK_RG));
         const int vec16 = (N % 4 == 0) && (K % 4 == 0) && (((uintptr_t)A | (uintptr_t)B) % 16 == 0);
         if (grid.y > 65535) fail(JHQ_EINVAL, "gemm_rows: too many rows in one call");
+        auto launch = [&](auto kern, int smem) {      // ring above the 48 KB static limit
+            JHQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            kern<<<grid, SK_THREADS, smem, s>>>(A, B, C, R, K, N, norms, vec16);
+        };
         if (tr == 1) {
-            if (epi == EPI_COARSE)
-                gemm_skinny_kernel<EPI_COARSE, 1><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
-            else
-                gemm_skinny_kernel<EPI_STORE, 1><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            if (epi == EPI_COARSE) launch(gemm_skinny_kernel<EPI_COARSE, 1>, sk_smem_bytes<1>());
+            else launch(gemm_skinny_kernel<EPI_STORE, 1>, sk_smem_bytes<1>());
         } else {
-            if (epi == EPI_COARSE)
-                gemm_skinny_kernel<EPI_COARSE, 4><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
-            else
-                gemm_skinny_kernel<EPI_STORE, 4><<<grid, SK_THREADS, 0, s>>>(A, B, C, R, K, N, norms, vec16);
+            if (epi == EPI_COARSE) launch(gemm_skinny_kernel<EPI_COARSE, 4>, sk_smem_bytes<4>());
+            else launch(gemm_skinny_kernel<EPI_STORE, 4>, sk_smem_bytes<4>());
         }
     } else {
         dim3 grid((unsigned)ceil_div(N, TBN), (unsigned)ceil_div(R, TBM));
