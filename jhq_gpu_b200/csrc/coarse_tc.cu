@@ -1114,4 +1114,80 @@ void flat_search_tc(const FlatTcArgs& a, cudaStream_t s) {
     count_launch();
 }
 
+#include "ivf_tc.cuh"
+
+bool ivf_tc_supported(int d, int M, int B, int nprobe) {
+    return M > 0 && d % M == 0 && d / M == 4 && B == 8 && (M + 15) / 16 * 16 * 4 == 128 &&
+           nprobe >= 1 && nprobe <= 128;
+}
+
+namespace {
+struct IvfScratch {
+    int8_t* qw;
+    float4* qc;
+    int64_t* qtile;
+    uint32_t* tmin;
+    size_t bytes;
+};
+IvfScratch ivf_carve(void* base, int Bq, int64_t max_tiles) {
+    const uintptr_t p = reinterpret_cast<uintptr_t>(base);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        void* r = reinterpret_cast<void*>(p + off);
+        off += (bytes + 255) & ~size_t(255);
+        return r;
+    };
+    IvfScratch f;
+    f.qw = reinterpret_cast<int8_t*>(take((size_t)Bq * 2 * IT_KP));
+    f.qc = reinterpret_cast<float4*>(take((size_t)Bq * sizeof(float4)));
+    f.qtile = reinterpret_cast<int64_t*>(take((size_t)(Bq + 1) * 8));
+    f.tmin = reinterpret_cast<uint32_t*>(take((size_t)std::max<int64_t>(1, max_tiles) * 4));
+    f.bytes = off;
+    return f;
+}
+}  // namespace
+
+size_t ivf_tc_scratch_bytes(int Bq, int64_t max_tiles) {
+    return ivf_carve(nullptr, Bq, max_tiles).bytes + 256;
+}
+
+void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
+    if (a.nq <= 0) return;
+    if (!ivf_tc_supported(a.d, a.M, 8, a.nprobe)) fail(JHQ_EINVAL, "ivf_search_tc: unsupported shape");
+    const int Mp = (a.M + 15) / 16 * 16;
+    const IvfScratch f = ivf_carve(a.scratch, a.nq, a.max_tiles);
+    PlanBufs pb = a.plan;
+    pb.qslot_off = f.qtile;                        // tile offsets per query (the refine's stay apart)
+    plan_build(a.probes, a.nq, a.nprobe, a.nlist, a.list_page_off, a.d_nvalid, 4, IT_NQ, pb, s);
+    static std::atomic<uint64_t> attr{0};
+    once_per_device(attr, [Mp] {
+        JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      IT_SMEM));
+        JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_select_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)is_smem_bytes(128)));
+    });
+    const float* c = a.c1d_host;
+    const float e1 = c[1] - c[0], e2 = c[2] - c[0], e3 = c[3] - c[2] - c[1] + c[0];
+    float cmax = 0.0f;
+    for (int i = 0; i < 4; ++i) cmax = std::max(cmax, std::fabs(c[i]));
+    ivf_prep_kernel<<<a.nq, IT_THREADS, 0, s>>>(a.q_rot, a.nq, a.d, Mp, c[0], e1, e2, e3, cmax,
+                                                f.qw, f.qc);
+    JHQ_LAUNCH_CHECK();
+    int dev = 0, nsm = 0;
+    JHQ_CUDA(cudaGetDevice(&dev));
+    JHQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    long long wait_limit = TC_WAIT_CYCLES;
+    if (const char* e = std::getenv("JHQ_TEST_TC_WAIT_CYCLES")) wait_limit = std::atoll(e);
+    ivf_tc_kernel<<<2 * nsm, IT_THREADS, IT_SMEM, s>>>(
+        a.pages, a.slot_ids, a.list_page_off, pb, f.qw, f.qc, a.nlist, a.nprobe, a.d, Mp,
+        c[0] * c[0], c[1] * c[1], c[2] * c[2], c[3] * c[3], f.tmin, wait_limit);
+    JHQ_LAUNCH_CHECK();
+    ivf_tc_select_kernel<<<a.nq, IS_THREADS, is_smem_bytes(Mp), s>>>(
+        a.q_rot, a.c1d, a.pages, a.slot_ids, a.list_page_off, a.probes, pb, f.qc, f.tmin, a.nq,
+        a.nprobe, a.d, a.M, Mp, a.ck, a.ck_pad, a.cand, a.gthr, a.qslot_out, a.d_nvalid);
+    JHQ_LAUNCH_CHECK();
+    count_launch(3);
+}
+
 }  // namespace jhq

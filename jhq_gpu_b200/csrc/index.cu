@@ -95,6 +95,14 @@ bool Index::flat_tc() const {
            !paging();
 }
 
+// IVF, 2 bits per dimension, d padded to 128 (C3 / C4): the two-pass
+// tensor-core scan when JHQ_IVF=tc, else the query-major SIMT scan
+bool Index::ivf_tc() const {
+    const char* e = std::getenv("JHQ_IVF");
+    if (!e || std::string(e) != "tc") return false;
+    return p_.nlist > 1 && ntotal_ > 0 && ivf_tc_supported(d_, M_, B_, p_.nprobe) && !paging();
+}
+
 size_t Index::rotq_scratch_floats(int Bq) const {
     if (!rot_tc_) return 0;
     const size_t q3f = (((size_t)Bq * coarse_tc_k3(d_) + 1) / 2 + 63) & ~(size_t)63;
@@ -683,6 +691,15 @@ void Index::prepare_workspace(int k) {
     ws_.gthr.ensure((size_t)Bq);
     ws_.cand.ensure((size_t)sh.max_slots * sh.ck);
     if (flat_tc()) ws_.flat.ensure(flat_tc_scratch_bytes(Bq, d_, (int)ntotal_));
+    ws_.ivf_tiles = 0;
+    if (ivf_tc()) {
+        // per query at most nprobe partial tiles plus the tiles of the nprobe largest lists
+        int64_t top_pages = 0;
+        for (int i = 0; i < np && i < (int)h_list_pages_sorted_.size(); ++i)
+            top_pages += h_list_pages_sorted_[i];
+        ws_.ivf_tiles = (int64_t)Bq * (np + ceil_div(top_pages, 4));
+        ws_.ivf.ensure(ivf_tc_scratch_bytes(Bq, ws_.ivf_tiles));
+    }
     if (pilotP_ > 0) {
         ws_.pkeys.ensure((size_t)Bq * PILOT_SPLIT * sh.ck);
         ws_.pscores.ensure((size_t)Bq * pilotP_);
@@ -765,16 +782,8 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
         coarse_probes(b.q_rot, nq, sh.Bq, p_.nprobe, b.scores, b.probes, s);
     }
     mark(2);
-    if (p_.nlist == 1 && b.flat && !probes_in) {     // flat, 1-bit codes: tensor-core ADC
-        FlatTcArgs fa;
-        fa.q_rot = b.q_rot; fa.c1d = dc1d_.get(); fa.c1d_host = c1d_.data();
-        fa.codes = dpcodes_.get(); fa.pop = dpop_.get();
-        fa.nvec = (int)ntotal_; fa.M = M_; fa.nq = nq; fa.ck = sh.ck; fa.ck_pad = sh.ck_pad;
-        fa.scratch = b.flat; fa.cand = b.cand; fa.gthr = b.plan.gthr;
-        fa.qslot_off = b.plan.qslot_off; fa.d_nvalid = d_nvalid;
-        mark(3);                       // no plan: the "scan" stage is the GEMM + selection
-        flat_search_tc(fa, s);
-        mark(4);
+    // the refine of a scan that leaves one candidate slot per query
+    auto refine_single = [&]() {
         RefineArgs ra;
         ra.q_rot = b.q_rot; ra.res_c1d = dres_.get(); ra.cand = b.cand;
         ra.res_per_sub = res_per_sub_ ? 1 : 0; ra.M = M_;
@@ -787,6 +796,35 @@ void Index::enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid,
             ra.raw = draw_.get();
         }
         refine_topk(ra, s);
+    };
+    if (p_.nlist == 1 && b.flat && !probes_in) {     // flat, 1-bit codes: tensor-core ADC
+        FlatTcArgs fa;
+        fa.q_rot = b.q_rot; fa.c1d = dc1d_.get(); fa.c1d_host = c1d_.data();
+        fa.codes = dpcodes_.get(); fa.pop = dpop_.get();
+        fa.nvec = (int)ntotal_; fa.M = M_; fa.nq = nq; fa.ck = sh.ck; fa.ck_pad = sh.ck_pad;
+        fa.scratch = b.flat; fa.cand = b.cand; fa.gthr = b.plan.gthr;
+        fa.qslot_off = b.plan.qslot_off; fa.d_nvalid = d_nvalid;
+        mark(3);                       // no plan: the "scan" stage is the GEMM + selection
+        flat_search_tc(fa, s);
+        mark(4);
+        refine_single();
+        mark(5);
+        return;
+    }
+    if (p_.nlist > 1 && b.ivf) {      // IVF, 2 bits per dimension: two-pass tensor-core scan
+        IvfTcArgs ia;
+        ia.q_rot = b.q_rot; ia.c1d = dc1d_.get(); ia.c1d_host = c1d_.data();
+        ia.probes = probes; ia.list_page_off = dlist_page_off_.get();
+        ia.pages = dpages_.get(); ia.slot_ids = dslot_ids_.get();
+        ia.plan = b.plan; ia.scratch = b.ivf; ia.max_tiles = b.ivf_tiles;
+        ia.nq = nq; ia.nprobe = p_.nprobe; ia.nlist = p_.nlist; ia.d = d_; ia.M = M_;
+        ia.ck = sh.ck; ia.ck_pad = sh.ck_pad;
+        ia.cand = b.cand; ia.gthr = b.plan.gthr; ia.qslot_out = b.plan.qslot_off;
+        ia.d_nvalid = d_nvalid;
+        mark(3);                       // the plan is built inside: the "scan" stage is all of it
+        ivf_search_tc(ia, s);
+        mark(4);
+        refine_single();
         mark(5);
         return;
     }
@@ -846,6 +884,8 @@ void Index::enqueue_batch(cudaStream_t s, cudaEvent_t* ev) {
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
     b.rotq = ws_.rotq.get();
     b.flat = flat_tc() ? ws_.flat.get() : nullptr;
+    b.ivf = ws_.ivf_tiles > 0 ? ws_.ivf.get() : nullptr;
+    b.ivf_tiles = ws_.ivf_tiles;
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();
@@ -1025,6 +1065,8 @@ void Index::search_device_probes(const float* d_q, const int32_t* d_probes, int6
     b.q_rot = ws_.q_rot.get(); b.scores = ws_.scores.get(); b.probes = ws_.probes.get();
     b.rotq = ws_.rotq.get();
     b.flat = flat_tc() ? ws_.flat.get() : nullptr;
+    b.ivf = ws_.ivf_tiles > 0 ? ws_.ivf.get() : nullptr;
+    b.ivf_tiles = ws_.ivf_tiles;
     b.plan = PlanBufs{ws_.cnt.get(), ws_.bucket_off.get(), ws_.unit_off.get(), ws_.fill.get(),
                       ws_.bucket.get(), ws_.cpo.get(), ws_.qslot_off.get(), ws_.gthr.get()};
     b.cand = ws_.cand.get();

@@ -127,6 +127,8 @@ private:
         PinnedBuf<int> h_nvalid;
         DevBuf<float> q, q_rot, scores, out_d, rotq;
         DevBuf<unsigned char> flat;    // flat_search_tc scratch
+        DevBuf<unsigned char> ivf;     // ivf_search_tc scratch
+        int64_t ivf_tiles = 0;         // (query, probed tile) pairs it holds
         DevBuf<int32_t> probes, out_i, cnt, bucket_off, unit_off, fill, cpo;
         DevBuf<int2> bucket;
         DevBuf<int64_t> qslot_off;
@@ -177,6 +179,8 @@ private:
         float* pscores = nullptr;
         float* rotq = nullptr;         // tensor-core query rotation scratch
         void* flat = nullptr;          // tensor-core flat scan scratch (nullptr: SIMT scan)
+        void* ivf = nullptr;           // tensor-core IVF scan scratch (nullptr: SIMT scan)
+        int64_t ivf_tiles = 0;
     };
     BatchShape batch_shape(int Bq, int k) const;
     void enqueue_pipeline(const float* q_in, int nq, const int* d_nvalid, const BatchShape& sh,
@@ -193,6 +197,7 @@ private:
     // flat index with 1-bit codes: the ADC scan runs as a tensor-core GEMM of
     // the code bits with the queries (coarse_tc.cu: flat_search_tc)
     bool flat_tc() const;
+    bool ivf_tc() const;
 
     int d_, M_, B_, Br_, Ds_, bpd_, K1D_, Kr_, bpv_, bpv_pad_, Mp_;
     Params p_;

@@ -151,6 +151,28 @@ size_t scan_qmajor_smem_bytes(int Mp, int ck_pad);
 void scan_topck(const ScanArgs& a, cudaStream_t st);
 void scan_configure();                               // opt-in shared memory, current device
 
+// ---- IVF ADC scan on the tensor cores, 2 bits per dimension (coarse_tc.cu) -
+struct IvfTcArgs {
+    const float* q_rot;            // [nq][d]
+    const float* c1d;              // [4] on the device
+    const float* c1d_host;         // [4] on the host
+    const int32_t* probes;         // [nq][nprobe]
+    const int32_t* list_page_off;  // [nlist+1]
+    const uint8_t* pages;          // [npages][Mp/16][32][16]
+    const int32_t* slot_ids;       // [npages*32]
+    PlanBufs plan;                 // list-major plan buffers (rebuilt here; qslot_off unused)
+    void* scratch;                 // ivf_tc_scratch_bytes(nq, max_tiles)
+    int64_t max_tiles;             // bound on the batch's (query, probed tile) pairs
+    int nq, nprobe, nlist, d, M, ck, ck_pad;
+    uint64_t* cand;                // [nq][ck] out: the exact top-ck, one slot per query
+    uint64_t* gthr;                // [nq] out: the ck-th key
+    int64_t* qslot_out;            // [nq+1] out: q
+    const int* d_nvalid = nullptr; // device count of valid rows (rest: no candidates)
+};
+bool ivf_tc_supported(int d, int M, int B, int nprobe);
+size_t ivf_tc_scratch_bytes(int Bq, int64_t max_tiles);
+void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s);
+
 // ---- merge + residual refine + final top-k (refine.cu) --------------------
 struct RefineArgs {
     const float* q_rot;        // [nq][d]

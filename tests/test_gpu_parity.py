@@ -752,3 +752,40 @@ def test_flat_tensor_core_scores_within_the_bound(jhq, oracle):
               f"shift {np.median(diff):.3e}, spread of s* {s_ex.std():.3e}")
         worst = max(worst, dev / E)
     assert worst <= 1.0
+
+
+@pytest.mark.parametrize("gen,d,M,nlist,nprobe,nq,batch,k,R", [
+    ("c3", 128, 32, 2048, 32, 150, 64, 10, 0),     # ragged last batch (150 = 2 x 64 + 22)
+    ("c4", 104, 26, 1024, 24, 130, 128, 10, 0),    # d = 104 padded to 128 inside the planes
+    ("c3", 128, 32, 4096, 8, 96, 96, 40, 0),       # ck = 160 > the tiles of most queries
+    ("c3", 128, 32, 512, 16, 64, 64, 10, 24),      # exact rerank behind the scan
+])
+def test_ivf_tensor_core_scan_bit_exact(jhq, oracle, monkeypatch, gen, d, M, nlist, nprobe, nq,
+                                        batch, k, R):
+    """IVF with 2-bit-per-dimension codes (C3 uint8 / C4 int8 generators): the
+    two-pass tensor-core scan (per-query tile minima of the int8 GEMM of the code
+    bit planes with the queries, then exact rescoring of the tiles within the
+    margin) returns the oracle's ids and distances, and the query-major SIMT
+    scan's (JHQ_IVF=simt), bit for bit."""
+    from jhq_gpu_b200 import datasets
+    g = datasets.rows_c3 if gen == "c3" else datasets.rows_c4
+    x = np.concatenate(list(g(0, 40000)))
+    q = np.concatenate(list(g(0, nq, sub=2)))
+    monkeypatch.setenv("JHQ_IVF", "tc")
+    p = jhq.Params(M=M, nlist=nlist, nprobe=nprobe, batch_size=batch)
+    idx = jhq.JHQGpuIndex(d, p)
+    idx.train(x[:20000])
+    if R:
+        idx.set_rerank(R)
+    idx.add(x)
+    ox = _oracle_index(oracle, idx, x)
+    D, I = idx.search(q, k)
+    if R:
+        _, Ic = _oracle_search(oracle, idx, ox, q, max(R, k))
+        D2, I2 = oracle.rerank(q, x, Ic, k)
+    else:
+        D2, I2 = _oracle_search(oracle, idx, ox, q, k)
+    _assert_same(D, I, D2, I2)
+    monkeypatch.setenv("JHQ_IVF", "simt")
+    idx.set_nprobe(nprobe)                          # re-plan on the SIMT scan
+    _assert_same(*idx.search(q, k), D, I)
