@@ -96,10 +96,10 @@ bool Index::flat_tc() const {
 }
 
 // IVF, 2 bits per dimension, d padded to 128 (C3 / C4): the two-pass
-// tensor-core scan when JHQ_IVF=tc, else the query-major SIMT scan
+// tensor-core scan (JHQ_IVF=simt keeps the query-major SIMT scan)
 bool Index::ivf_tc() const {
     const char* e = std::getenv("JHQ_IVF");
-    if (!e || std::string(e) != "tc") return false;
+    if (e && std::string(e) == "simt") return false;
     return p_.nlist > 1 && ntotal_ > 0 && ivf_tc_supported(d_, M_, B_, p_.nprobe) && !paging();
 }
 

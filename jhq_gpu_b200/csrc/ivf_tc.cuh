@@ -205,7 +205,34 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     int cur_l = -1, cur_g = -1, nqg = 0;
     uint32_t phase = 0;
     bool failed = false;
+    // the A row of this thread in unit (L, T): slot id and code words, loaded
+    // one unit ahead so that their latency overlaps the current unit
+    auto load_row = [&](int L, int T, int& id, uint4& w0, uint4& w1) {
+        const int pg = lpo[L] + 4 * T + (tid >> 5);
+        const bool okp = pg < lpo[L + 1];
+        id = okp ? __ldg(slot_ids + (int64_t)pg * 32 + lane) : -1;
+        const uint4* pp = reinterpret_cast<const uint4*>(pages) + (int64_t)pg * G * 32 + lane;
+        w0 = okp ? __ldg(pp) : make_uint4(0u, 0u, 0u, 0u);
+        w1 = okp ? __ldg(pp + 32) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    int id_c, id_n = -1;
+    uint4 w0_c, w1_c, w0_n = make_uint4(0u, 0u, 0u, 0u), w1_n = w0_n;
+    load_row(l, t, id_c, w0_c, w1_c);
     for (int64_t u = u0; u < u1; ++u) {
+        // the next unit: tile, then group, then the next list with units
+        int l2 = l, g2 = g, t2 = t + 1, tiles2 = tiles_l;
+        if (u + 1 < u1) {
+            if (t2 == tiles_l) {
+                t2 = 0;
+                const int ng = (pb.bucket_off[l + 1] - pb.bucket_off[l] + IT_NQ - 1) / IT_NQ;
+                if (++g2 == ng) {
+                    g2 = 0;
+                    do { ++l2; } while (l2 < nlist - 1 && pb.unit_off[l2 + 1] == pb.unit_off[l2]);
+                    tiles2 = (lpo[l2 + 1] - lpo[l2] + 3) >> 2;
+                }
+            }
+            load_row(l2, t2, id_n, w0_n, w1_n);
+        }
         if (cur_l != l || cur_g != g) {                    // the group's B rows and constants
             const int b0 = pb.bucket_off[l] + g * IT_NQ;
             nqg = min(IT_NQ, pb.bucket_off[l + 1] - b0);
@@ -239,13 +266,11 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         }
         // A row tid: slot (page, lane) of tile t of list l
         {
-            const int pg = lpo[l] + 4 * t + (tid >> 5);
-            const bool okp = pg < lpo[l + 1];
-            const int id = okp ? __ldg(slot_ids + (int64_t)pg * 32 + lane) : -1;
+            const int id = id_c;
             int nL = 0, nH = 0, nLH = 0;
-            const uint4* pp = reinterpret_cast<const uint4*>(pages) + (int64_t)pg * G * 32 + lane;
-            for (int gg = 0; gg < G; ++gg) {
-                const uint4 cw = okp ? __ldg(pp + gg * 32) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg) {               // Mp = 32: two 16-subspace groups
+                const uint4 cw = gg == 0 ? w0_c : w1_c;
                 const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
                 for (int wi = 0; wi < 4; ++wi) {           // 4 subspaces = 16 dims
@@ -323,16 +348,8 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             const float mn = fminf(fminf(red[0][tid], red[1][tid]), fminf(red[2][tid], red[3][tid]));
             tmin[base_s[tid] + t] = float_order(mn);
         }
-        // next unit: tile, then group, then the next list with units
-        if (++t == tiles_l) {
-            t = 0;
-            const int ng = (pb.bucket_off[l + 1] - pb.bucket_off[l] + IT_NQ - 1) / IT_NQ;
-            if (++g == ng && u + 1 < u1) {
-                g = 0;
-                do { ++l; } while (l < nlist - 1 && pb.unit_off[l + 1] == pb.unit_off[l]);
-                tiles_l = (lpo[l + 1] - lpo[l] + 3) >> 2;
-            }
-        }
+        l = l2; g = g2; t = t2; tiles_l = tiles2;
+        id_c = id_n; w0_c = w0_n; w1_c = w1_n;
     }
     if (failed && tid == 0) atomicExch(&g_tc_error, 1);
     // no MMA may still read shared memory or write TMEM when the CTA frees them
@@ -345,9 +362,11 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
 
 // Pass 2, one CTA per query: tau (bisection over the order keys of the
 // query's tile minima), then the tiles whose minimum is <= tau + 2E, 256 at a
-// time, their slots rescored one per thread with the nibble tables, the keys
-// appended to buf (compacted to the best ck_pad when full); finally the exact
-// top-ck by (distance, id), written as the query's single candidate slot
+// time. Their pages are rescored a warp per page (lane = slot, two pages per
+// warp and step, all loads issued first) with the nibble tables; the keys go
+// to buf, which is compacted to the best ck_pad when full, after which keys
+// above the ck-th kept one are dropped. Finally the exact top-ck by
+// (distance, id) is written as the query's single candidate slot
 // (cand[q][ck], gthr[q], qslot_out[q] = q).
 __global__ void __launch_bounds__(IS_THREADS, 1)
 ivf_tc_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ c1d_g,
@@ -362,6 +381,7 @@ ivf_tc_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ 
     __shared__ int nhot_s, n_s;
     __shared__ int hot[IS_THREADS];
     __shared__ int cpo_s[129];
+    __shared__ int lb_s[128], le_s[128];                   // page range of each probed list
     __shared__ float c1d[4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NW = IS_THREADS / 32;
@@ -386,6 +406,11 @@ ivf_tc_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ 
     const bool in_smem = ntq <= IS_TK;
     if (tid < 4) c1d[tid] = c1d_g[tid];
     for (int p = tid; p <= nprobe; p += IS_THREADS) cpo_s[p] = pb.cpo[(int64_t)q * (nprobe + 1) + p];
+    for (int p = tid; p < nprobe; p += IS_THREADS) {
+        const int l = probes[(int64_t)q * nprobe + p];
+        lb_s[p] = lpo[l];
+        le_s[p] = lpo[l + 1];
+    }
     if (in_smem)
         for (int i = tid; i < ntq; i += IS_THREADS) tks[i] = tq[i];
     if (tid == 0) { nhot_s = 0; n_s = 0; }
@@ -429,6 +454,7 @@ ivf_tc_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ 
     __syncthreads();                                       // tables complete
     const int G = Mp / 16;
     int n = 0;                                             // keys in buf (block-uniform)
+    uint64_t thr = KEY_EMPTY;     // the ck-th key after a compaction: larger keys cannot enter
     for (int b0 = 0; b0 < ntq; b0 += IS_THREADS) {
         // this round's hot tiles
         const int i = b0 + tid;
@@ -439,56 +465,70 @@ ivf_tc_select_kernel(const float* __restrict__ q_rot, const float* __restrict__ 
         base = __shfl_sync(0xffffffffu, base, 0);
         if (in) hot[base + __popc(mk & lt)] = i;
         __syncthreads();
-        const int nh = nhot_s;
-        // their slots, one per thread: 128 per tile
-        for (int s0 = 0; s0 < nh * 128; s0 += IS_THREADS) {
-            if (n + IS_THREADS > IS_CAP) {                 // keep the best ck_pad
+        const int npg = nhot_s * 4;                        // their pages
+        // a step: every warp scores two pages (lane = slot), all loads issued first
+        for (int p0 = 0; p0 < npg; p0 += 2 * NW) {
+            if (n + 2 * NW * 32 > IS_CAP) {                // keep the best ck_pad
                 for (int k = n + tid; k < IS_CAP; k += IS_THREADS) buf[k] = KEY_EMPTY;
                 __syncthreads();
                 block_bitonic_sort(buf, IS_CAP);
                 n = ck_pad;
+                thr = buf[ck - 1];
+                __syncthreads();
                 if (tid == 0) n_s = n;
                 __syncthreads();
             }
-            uint64_t key = KEY_EMPTY;
-            const int s = s0 + tid;
-            if (s < nh * 128) {
-                const int ti = hot[s >> 7], r = s & 127;
-                int plo = 0, phi = nprobe;                 // last p with cpo[p] <= ti
-                while (phi - plo > 1) {
-                    const int mid = (plo + phi) >> 1;
-                    if (cpo_s[mid] <= ti) plo = mid; else phi = mid;
-                }
-                const int l = probes[(int64_t)q * nprobe + plo];
-                const int pg = lpo[l] + 4 * (ti - cpo_s[plo]) + (r >> 5);
-                if (pg < lpo[l + 1]) {
-                    const int id = __ldg(slot_ids + (int64_t)pg * 32 + (r & 31));
-                    if (id >= 0) {
-                        const uint4* pp = reinterpret_cast<const uint4*>(pages) +
-                                          (int64_t)pg * G * 32 + (r & 31);
-                        float dist = 0.0f;
-                        for (int g = 0; g < G; ++g) {
-                            const uint4 w4 = __ldg(pp + g * 32);
-                            const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+            int id[2];
+            uint4 cw[2][2];
 #pragma unroll
-                            for (int wi = 0; wi < 4; ++wi)
-#pragma unroll
-                                for (int bb = 0; bb < 4; ++bb) {
-                                    const int m = g * 16 + wi * 4 + bb;
-                                    const uint32_t b = (ws[wi] >> (bb * 8)) & 0xFFu;
-                                    dist = __fadd_rn(dist, __fadd_rn(tab[m * 32 + (b & 15u)],
-                                                                      tab[m * 32 + 16 + (b >> 4)]));
-                                }
-                        }
-                        key = make_key(dist, id);
+            for (int v = 0; v < 2; ++v) {
+                const int pi = p0 + v * NW + warp;
+                id[v] = -1;
+                cw[v][0] = cw[v][1] = make_uint4(0u, 0u, 0u, 0u);
+                if (pi < npg) {
+                    const int ti = hot[pi >> 2];
+                    int plo = 0, phi = nprobe;             // last p with cpo[p] <= ti
+                    while (phi - plo > 1) {
+                        const int mid = (plo + phi) >> 1;
+                        if (cpo_s[mid] <= ti) plo = mid; else phi = mid;
+                    }
+                    const int pg = lb_s[plo] + 4 * (ti - cpo_s[plo]) + (pi & 3);
+                    if (pg < le_s[plo]) {
+                        id[v] = __ldg(slot_ids + (int64_t)pg * 32 + lane);
+                        const uint4* pp = reinterpret_cast<const uint4*>(pages) + (int64_t)pg * G * 32 + lane;
+                        cw[v][0] = __ldg(pp);
+                        if (G > 1) cw[v][1] = __ldg(pp + 32);
                     }
                 }
             }
-            const unsigned km = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
-            int kb = 0;
-            if (lane == 0 && km) kb = atomicAdd(&n_s, __popc(km));
-            kb = __shfl_sync(0xffffffffu, kb, 0);
-            if (key != KEY_EMPTY) buf[kb + __popc(km & lt)] = key;
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                uint64_t key = KEY_EMPTY;
+                if (id[v] >= 0) {
+                    float dist = 0.0f;
+#pragma unroll
+                    for (int g = 0; g < 2; ++g) {
+                        if (g >= G) break;
+                        const uint32_t ws[4] = {cw[v][g].x, cw[v][g].y, cw[v][g].z, cw[v][g].w};
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                            for (int bb = 0; bb < 4; ++bb) {
+                                const int m = g * 16 + wi * 4 + bb;
+                                const uint32_t bt = (ws[wi] >> (bb * 8)) & 0xFFu;
+                                dist = __fadd_rn(dist, __fadd_rn(tab[m * 32 + (bt & 15u)],
+                                                                  tab[m * 32 + 16 + (bt >> 4)]));
+                            }
+                    }
+                    key = make_key(dist, id[v]);
+                    if (key > thr) key = KEY_EMPTY;
+                }
+                const unsigned km = __ballot_sync(0xffffffffu, key != KEY_EMPTY);
+                int kb = 0;
+                if (lane == 0 && km) kb = atomicAdd(&n_s, __popc(km));
+                kb = __shfl_sync(0xffffffffu, kb, 0);
+                if (key != KEY_EMPTY) buf[kb + __popc(km & lt)] = key;
+            }
             __syncthreads();
             n = n_s;
         }

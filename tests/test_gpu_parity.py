@@ -129,9 +129,11 @@ def test_search_bit_exact_vs_oracle(jhq, oracle, cfg):
     dict(d=32, M=8, nlist=5000, nprobe=64, n=12000, nq=30, batch=16),         # nlist > 4096 probe path
 ])
 def test_ivf_scan_orders_bit_exact(jhq, oracle, monkeypatch, cfg, order):
-    """Both scan work orders (list-major units / query-major warp items) give the
-    oracle's results bit for bit."""
+    """Both SIMT scan work orders (list-major units / query-major warp items)
+    give the oracle's results bit for bit (JHQ_IVF=simt: the C3 / C4 shapes
+    would otherwise take the tensor-core scan)."""
     monkeypatch.setenv("JHQ_SCAN_ORDER", order)
+    monkeypatch.setenv("JHQ_IVF", "simt")
     d, n = cfg["d"], cfg["n"]
     x = _data(n, d, 21)
     q = _data(cfg["nq"], d, 22)
@@ -448,8 +450,9 @@ def test_exact_rerank_reaches_recall_gate_on_c1_generator(jhq):
 ])
 def test_integer_generators_bit_exact_vs_oracle(jhq, oracle, gen, d, M, nlist, nprobe):
     """The C3 / C4 data generators (not i.i.d. normal) at 60k rows with nlist in the
-    thousands, both scan orders: ids and distances equal the oracle's, and every
-    result row is ordered by (distance, id) — the tie rule applied everywhere."""
+    thousands, the tensor-core scan and both SIMT scan orders: ids and distances
+    equal the oracle's, and every result row is ordered by (distance, id) — the
+    tie rule applied everywhere."""
     from jhq_gpu_b200 import datasets
     g = datasets.rows_c3 if gen == "c3" else datasets.rows_c4
     x = np.concatenate(list(g(0, 60000)))
@@ -459,13 +462,17 @@ def test_integer_generators_bit_exact_vs_oracle(jhq, oracle, gen, d, M, nlist, n
     ox = _oracle_index(oracle, idx, x)
     D2, I2 = _oracle_search(oracle, idx, ox, q, 10)
     ties = 0
-    for order in ("query", "list"):
+    D, I = idx.search(q, 10)                        # the default (tensor-core) scan
+    _assert_same(D, I, D2, I2)
+    for order in ("query", "list"):                 # both SIMT orders
         os.environ["JHQ_SCAN_ORDER"] = order
+        os.environ["JHQ_IVF"] = "simt"
         try:
             idx.set_nprobe(nprobe)                  # re-plan with the forced order
             D, I = idx.search(q, 10)
         finally:
             del os.environ["JHQ_SCAN_ORDER"]
+            del os.environ["JHQ_IVF"]
         _assert_same(D, I, D2, I2)
     for row_d, row_i in zip(D, I):
         keys = list(zip(row_d.tolist(), row_i.tolist()))
@@ -771,7 +778,6 @@ def test_ivf_tensor_core_scan_bit_exact(jhq, oracle, monkeypatch, gen, d, M, nli
     g = datasets.rows_c3 if gen == "c3" else datasets.rows_c4
     x = np.concatenate(list(g(0, 40000)))
     q = np.concatenate(list(g(0, nq, sub=2)))
-    monkeypatch.setenv("JHQ_IVF", "tc")
     p = jhq.Params(M=M, nlist=nlist, nprobe=nprobe, batch_size=batch)
     idx = jhq.JHQGpuIndex(d, p)
     idx.train(x[:20000])
