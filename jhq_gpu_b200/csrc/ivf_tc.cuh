@@ -12,7 +12,7 @@
 //   bits(v) = (L | H | L&H) (3 x 128 zero-one entries),
 //   cn(v) = sum_j c[b_j]^2 (from the level counts of v).
 // The scan is two passes over the batch's probed lists:
-//   1. ivf_tc_kernel: per work unit (list l, up to 32 of the queries probing l,
+//   1. ivf_tc_kernel: per work unit (list l, up to 64 of the queries probing l,
 //      one tile of 128 slots = 4 pages of l) the bit planes of the tile are
 //      expanded to s8 0/1 rows in shared memory, w is quantised (per query,
 //      int16 split in two s8 planes, exactly as in the flat scan), and one
@@ -31,12 +31,12 @@
 namespace {
 
 constexpr int IT_THREADS = 128;               // one thread per tile row in pass 1
-constexpr int IT_NQ = 32;                     // queries per work unit (B rows: 32 hi + 32 lo)
+constexpr int IT_NQ = 64;                     // queries per work unit (B rows: 64 hi + 64 lo)
 constexpr int IT_KP = 384;                    // K: three planes of 128 dims
 constexpr int IT_KB = IT_KP / 128;            // 128-byte K blocks
 constexpr int IT_A_BYTES = 128 * IT_KP;       // 48 KB
 constexpr int IT_B_BYTES = 2 * IT_NQ * IT_KP; // 24 KB
-constexpr int IT_SMEM = IT_A_BYTES + IT_B_BYTES + 1024 /* align */ + 1024 /* tables */;
+constexpr int IT_SMEM = IT_A_BYTES + IT_B_BYTES + 1024 /* align */;
 constexpr int IS_THREADS = 256;               // pass 2: one CTA per query
 constexpr int IS_CAP = 1024;                  // exact keys held before a compaction
 constexpr int IS_TK = 8192;                   // tile minima held in shared memory (more: global)
@@ -139,16 +139,16 @@ __device__ __forceinline__ void sw128_store(uint8_t* blk, int r, int c, uint4 v)
     *reinterpret_cast<uint4*>(blk + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)) = v;
 }
 
-// Pass 1. Work units are numbered list-major, then query group (32 queries of
+// Pass 1. Work units are numbered list-major, then query group (64 queries of
 // the list's bucket), then tile (4 pages), as plan_build(chunk_pages = 4,
-// qg = 32) counts them; a CTA takes a contiguous range. Per unit:
-//   1. (new list or group) the group's s8 query planes -> B (rows 0..31 hi,
-//      32..63 lo, missing queries zero) and the group's constants;
+// qg = 64) counts them; a CTA takes a contiguous range. Per unit:
+//   1. (new list or group) the group's s8 query planes -> B (rows 0..63 hi,
+//      64..127 lo, missing queries zero) and the group's constants;
 //   2. each thread expands its slot's codes into the three bit planes of its
 //      A row and counts the levels (cn);
 //   3. one thread issues the 12 MMAs (K = 32 each) and commits; all wait
 //      (bounded);
-//   4. the four warps read their 32 TMEM lanes (rows) x 64 columns, form
+//   4. the four warps read their 32 TMEM lanes (rows) x 128 columns, form
 //      s~ = (Sq' + cn) + (-2 s)(256 Gh + Gl), reduce each query column's
 //      minimum over the tile and write it to tmin[qtile[q] + cpo[q][p] + t].
 __global__ void __launch_bounds__(IT_THREADS)
@@ -159,14 +159,14 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
               long long wait_limit) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ float cn_s[128];
-    __shared__ float red[4][32];
+    __shared__ float red[4][IT_NQ];
     __shared__ float sq_s[IT_NQ], b_s[IT_NQ];
     __shared__ int64_t base_s[IT_NQ];
     __shared__ uint64_t bar;
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* As = smem;                                    // [3][128][128]
-    uint8_t* Bs = smem + IT_A_BYTES;                       // [3][64][128]
+    uint8_t* Bs = smem + IT_A_BYTES;                       // [3][2 IT_NQ][128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = Mp / 16;
     const int64_t U = pb.unit_off[nlist];
@@ -179,15 +179,15 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     :: "r"(smem_u32(&tmem_slot)), "r"(64));
+                     :: "r"(smem_u32(&tmem_slot)), "r"(2 * IT_NQ));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_slot;
-    // s32 accumulate, A and B s8, K-major, N' = 64, M = 128
-    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(64 >> 3) << 17) |
+    // s32 accumulate, A and B s8, K-major, N' = 2 IT_NQ, M = 128
+    const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(2 * IT_NQ >> 3) << 17) |
                            ((uint32_t)(128 >> 4) << 24);
 
     // the unit u0: its list (last l with unit_off[l] <= u0), group and tile
@@ -236,30 +236,30 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         if (cur_l != l || cur_g != g) {                    // the group's B rows and constants
             const int b0 = pb.bucket_off[l] + g * IT_NQ;
             nqg = min(IT_NQ, pb.bucket_off[l + 1] - b0);
-            for (int i = tid; i < IT_KB * 64 * 8; i += IT_THREADS) {
-                const int kb = i / (64 * 8), r = (i >> 3) & 63, c = i & 7;
-                const int j = r & 31;
+            for (int i = tid; i < IT_KB * 2 * IT_NQ * 8; i += IT_THREADS) {
+                const int kb = i / (2 * IT_NQ * 8), r = (i >> 3) % (2 * IT_NQ), c = i & 7;
+                const int j = r % IT_NQ;
                 uint4 v = make_uint4(0u, 0u, 0u, 0u);
                 if (j < nqg) {
                     const int q = pb.bucket[b0 + j].x;
                     v = __ldg(reinterpret_cast<const uint4*>(
-                        qw + ((int64_t)q * 2 + (r >> 5)) * IT_KP + kb * 128 + c * 16));
+                        qw + ((int64_t)q * 2 + r / IT_NQ) * IT_KP + kb * 128 + c * 16));
                 }
-                sw128_store(Bs + kb * (64 * 128), r, c, v);
+                sw128_store(Bs + kb * (2 * IT_NQ * 128), r, c, v);
             }
-            if (tid < IT_NQ) {
+            for (int j = tid; j < IT_NQ; j += IT_THREADS) {
                 float sq = 0.0f, bq = 0.0f;
                 int64_t base = 0;
-                if (tid < nqg) {
-                    const int2 e = pb.bucket[b0 + tid];
+                if (j < nqg) {
+                    const int2 e = pb.bucket[b0 + j];
                     const float4 c = qc[e.x];
                     sq = c.x;
                     bq = c.y;
                     base = pb.qslot_off[e.x] + pb.cpo[(int64_t)e.x * (nprobe + 1) + e.y];
                 }
-                sq_s[tid] = sq;
-                b_s[tid] = bq;
-                base_s[tid] = base;
+                sq_s[j] = sq;
+                b_s[j] = bq;
+                base_s[j] = base;
             }
             cur_l = l;
             cur_g = g;
@@ -299,7 +299,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
 #pragma unroll
             for (int kb = 0; kb < IT_KB; ++kb) {
                 const uint64_t da = sw128_desc(smem_u32(As + kb * 16384));
-                const uint64_t db = sw128_desc(smem_u32(Bs + kb * (64 * 128)));
+                const uint64_t db = sw128_desc(smem_u32(Bs + kb * (2 * IT_NQ * 128)));
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const uint32_t accum = (kb | k) != 0;
@@ -316,19 +316,19 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         phase ^= 1u;
         if (!__syncthreads_and(ok)) { failed = true; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        {
+        for (int cb = 0; cb < IT_NQ && cb < nqg; cb += 32) {     // 32 query columns at a time
             uint32_t rh[32], rl[32];
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
             tmem_ld32(taddr, rh);
-            tmem_ld32(taddr + 32u, rl);
+            tmem_ld32(taddr + (uint32_t)IT_NQ, rl);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const float cn = cn_s[tid];
             float m[32];
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
                 const int gi = (int)rh[c] * 256 + (int)rl[c];
-                const float sv = __fmaf_rn(b_s[c], (float)gi, __fadd_rn(sq_s[c], cn));
-                m[c] = c < nqg ? sv : __int_as_float(0x7f800000);
+                const float sv = __fmaf_rn(b_s[cb + c], (float)gi, __fadd_rn(sq_s[cb + c], cn));
+                m[c] = cb + c < nqg ? sv : __int_as_float(0x7f800000);
             }
 #pragma unroll
             for (int h = 16; h; h >>= 1) {                 // transpose-reduce: lane c <- column c
@@ -340,7 +340,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
                 }
             }
-            red[warp][lane] = m[0];
+            red[warp][cb + lane] = m[0];
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncthreads();
@@ -357,7 +357,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(64));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(2 * IT_NQ));
 }
 
 // Pass 2, one CTA per query: tau (bisection over the order keys of the
