@@ -1171,7 +1171,7 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
     const float e1 = c[1] - c[0], e2 = c[2] - c[0], e3 = c[3] - c[2] - c[1] + c[0];
     float cmax = 0.0f;
     for (int i = 0; i < 4; ++i) cmax = std::max(cmax, std::fabs(c[i]));
-    ivf_prep_kernel<<<a.nq, IT_THREADS, 0, s>>>(a.q_rot, a.nq, a.d, Mp, c[0], e1, e2, e3, cmax,
+    ivf_prep_kernel<<<a.nq, IP_THREADS, 0, s>>>(a.q_rot, a.nq, a.d, Mp, c[0], e1, e2, e3, cmax,
                                                 f.qw, f.qc);
     JHQ_LAUNCH_CHECK();
     int dev = 0, nsm = 0;

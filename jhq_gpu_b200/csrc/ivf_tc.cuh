@@ -30,7 +30,7 @@
 
 namespace {
 
-constexpr int IT_THREADS = 128;               // one thread per tile row in pass 1
+constexpr int IT_THREADS = 256;               // pass 1: two threads per tile row
 constexpr int IT_NQ = 64;                     // queries per work unit (B rows: 64 hi + 64 lo)
 constexpr int IT_KP = 384;                    // K: three planes of 128 dims
 constexpr int IT_KB = IT_KP / 128;            // 128-byte K blocks
@@ -47,13 +47,14 @@ constexpr int IS_TK = 8192;                   // tile minima held in shared memo
 // E bounds |s~ - s*| for every vector of the query, up to a per-query constant:
 // the LUT path's roundings, the quantisation residual, and the roundings of cn
 // and of the epilogue's fma.
-__global__ void __launch_bounds__(IT_THREADS)
+constexpr int IP_THREADS = 128;
+__global__ void __launch_bounds__(IP_THREADS)
 ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0, float e1,
                 float e2, float e3, float cmax, int8_t* __restrict__ qw,
                 float4* __restrict__ qc) {
     const int q = blockIdx.x;
     if (q >= nq) return;
-    __shared__ float red[6][IT_THREADS / 32];
+    __shared__ float red[6][IP_THREADS / 32];
     __shared__ float s_sh;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float* x = q_rot + (int64_t)q * d;
@@ -63,20 +64,20 @@ ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0
         return j < d ? e[p] * x[j] : 0.0f;
     };
     float amax = 0.0f;
-    for (int i = threadIdx.x; i < IT_KP; i += IT_THREADS) amax = fmaxf(amax, fabsf(wv(i)));
+    for (int i = threadIdx.x; i < IT_KP; i += IP_THREADS) amax = fmaxf(amax, fabsf(wv(i)));
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     if (lane == 0) red[0][warp] = amax;
     __syncthreads();
     if (threadIdx.x == 0) {
         float a = 0.0f;
-        for (int w = 0; w < IT_THREADS / 32; ++w) a = fmaxf(a, red[0][w]);
+        for (int w = 0; w < IP_THREADS / 32; ++w) a = fmaxf(a, red[0][w]);
         s_sh = a > 0.0f ? a / FT_QMAX : 1.0f;
     }
     __syncthreads();
     const float sc = s_sh;
     float r1 = 0.0f, l1w = 0.0f, sq = 0.0f, sx = 0.0f, V = 0.0f;
-    for (int i = threadIdx.x; i < IT_KP; i += IT_THREADS) {
+    for (int i = threadIdx.x; i < IT_KP; i += IP_THREADS) {
         const float w = wv(i);
         const float Wf = fminf(fmaxf(rintf(w / sc), -FT_QMAX), FT_QMAX);
         const int W = (int)Wf;
@@ -86,7 +87,7 @@ ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0
         r1 += fabsf(__fmaf_rn(-sc, Wf, w));
         l1w += fabsf(w);
     }
-    for (int j = threadIdx.x; j < d; j += IT_THREADS) {
+    for (int j = threadIdx.x; j < d; j += IP_THREADS) {
         const float v = x[j], a = fabsf(v) + cmax;
         sq = __fmaf_rn(v, v, sq);
         sx += v;
@@ -105,7 +106,7 @@ ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0
     if (threadIdx.x == 0) {
         float t[5] = {0, 0, 0, 0, 0};
         for (int k = 0; k < 5; ++k)
-            for (int w = 0; w < IT_THREADS / 32; ++w) t[k] += red[k][w];
+            for (int w = 0; w < IP_THREADS / 32; ++w) t[k] += red[k][w];
         const float u = 5.9604645e-08f;                  // 2^-24
         const float R1 = t[0] * 1.001f, L1w = t[1] * 1.001f;
         const float Sq = __fmaf_rn(-2.0f * c0, t[3], t[2]);
@@ -144,11 +145,11 @@ __device__ __forceinline__ void sw128_store(uint8_t* blk, int r, int c, uint4 v)
 // qg = 64) counts them; a CTA takes a contiguous range. Per unit:
 //   1. (new list or group) the group's s8 query planes -> B (rows 0..63 hi,
 //      64..127 lo, missing queries zero) and the group's constants;
-//   2. each thread expands its slot's codes into the three bit planes of its
-//      A row and counts the levels (cn);
+//   2. two threads per slot (one per 16-subspace group) expand its codes into
+//      the three bit planes of its A row and count the levels (cn);
 //   3. one thread issues the 12 MMAs (K = 32 each) and commits; all wait
 //      (bounded);
-//   4. the four warps read their 32 TMEM lanes (rows) x 128 columns, form
+//   4. the eight warps read 32 TMEM lanes (rows) x 32 query columns each, form
 //      s~ = (Sq' + cn) + (-2 s)(256 Gh + Gl), reduce each query column's
 //      minimum over the tile and write it to tmin[qtile[q] + cpo[q][p] + t].
 __global__ void __launch_bounds__(IT_THREADS)
@@ -158,8 +159,9 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
               float c0s, float c1s, float c2s, float c3s, uint32_t* __restrict__ tmin,
               long long wait_limit) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ float cn_s[128];
-    __shared__ float red[4][IT_NQ];
+    __shared__ int cnt_s[2][128];                      // level counts per half row: nL | nH << 10 | nLH << 20
+    __shared__ int id_s[128];
+    __shared__ float red[8][32];
     __shared__ float sq_s[IT_NQ], b_s[IT_NQ];
     __shared__ int64_t base_s[IT_NQ];
     __shared__ uint64_t bar;
@@ -207,17 +209,17 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     bool failed = false;
     // the A row of this thread in unit (L, T): slot id and code words, loaded
     // one unit ahead so that their latency overlaps the current unit
-    auto load_row = [&](int L, int T, int& id, uint4& w0, uint4& w1) {
-        const int pg = lpo[L] + 4 * T + (tid >> 5);
+    const int row = tid & 127, hf = tid >> 7;             // tile row and its 16-subspace group
+    auto load_row = [&](int L, int T, int& id, uint4& w) {
+        const int pg = lpo[L] + 4 * T + (row >> 5);
         const bool okp = pg < lpo[L + 1];
         id = okp ? __ldg(slot_ids + (int64_t)pg * 32 + lane) : -1;
-        const uint4* pp = reinterpret_cast<const uint4*>(pages) + (int64_t)pg * G * 32 + lane;
-        w0 = okp ? __ldg(pp) : make_uint4(0u, 0u, 0u, 0u);
-        w1 = okp ? __ldg(pp + 32) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4* pp = reinterpret_cast<const uint4*>(pages) + ((int64_t)pg * G + hf) * 32 + lane;
+        w = okp ? __ldg(pp) : make_uint4(0u, 0u, 0u, 0u);
     };
     int id_c, id_n = -1;
-    uint4 w0_c, w1_c, w0_n = make_uint4(0u, 0u, 0u, 0u), w1_n = w0_n;
-    load_row(l, t, id_c, w0_c, w1_c);
+    uint4 w_c, w_n = make_uint4(0u, 0u, 0u, 0u);
+    load_row(l, t, id_c, w_c);
     for (int64_t u = u0; u < u1; ++u) {
         // the next unit: tile, then group, then the next list with units
         int l2 = l, g2 = g, t2 = t + 1, tiles2 = tiles_l;
@@ -231,7 +233,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     tiles2 = (lpo[l2 + 1] - lpo[l2] + 3) >> 2;
                 }
             }
-            load_row(l2, t2, id_n, w0_n, w1_n);
+            load_row(l2, t2, id_n, w_n);
         }
         if (cur_l != l || cur_g != g) {                    // the group's B rows and constants
             const int b0 = pb.bucket_off[l] + g * IT_NQ;
@@ -264,33 +266,23 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             cur_l = l;
             cur_g = g;
         }
-        // A row tid: slot (page, lane) of tile t of list l
+        // A row `row`, dims 64 hf .. 64 hf + 63: slot (page, lane) of tile t of list l
         {
-            const int id = id_c;
             int nL = 0, nH = 0, nLH = 0;
+            const uint32_t w4[4] = {w_c.x, w_c.y, w_c.z, w_c.w};
 #pragma unroll
-            for (int gg = 0; gg < 2; ++gg) {               // Mp = 32: two 16-subspace groups
-                const uint4 cw = gg == 0 ? w0_c : w1_c;
-                const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi) {           // 4 subspaces = 16 dims
-                    const uint32_t L = even_bits16(w4[wi]), H = even_bits16(w4[wi] >> 1), LH = L & H;
-                    nL += __popc(L);
-                    nH += __popc(H);
-                    nLH += __popc(LH);
-                    const int cg = gg * 4 + wi;            // 16-dim chunk of the 128 dims
-                    sw128_store(As + 0 * 16384, tid, cg, spread16(L));
-                    sw128_store(As + 1 * 16384, tid, cg, spread16(H));
-                    sw128_store(As + 2 * 16384, tid, cg, spread16(LH));
-                }
+            for (int wi = 0; wi < 4; ++wi) {               // 4 subspaces = 16 dims
+                const uint32_t L = even_bits16(w4[wi]), H = even_bits16(w4[wi] >> 1), LH = L & H;
+                nL += __popc(L);
+                nH += __popc(H);
+                nLH += __popc(LH);
+                const int cg = hf * 4 + wi;                // 16-dim chunk of the 128 dims
+                sw128_store(As + 0 * 16384, row, cg, spread16(L));
+                sw128_store(As + 1 * 16384, row, cg, spread16(H));
+                sw128_store(As + 2 * 16384, row, cg, spread16(LH));
             }
-            float cn = __int_as_float(0x7f800000);         // empty slot: never a minimum
-            if (id >= 0) {
-                const int n3 = nLH, n1 = nL - nLH, n2 = nH - nLH, n0 = d - nL - nH + nLH;
-                cn = __fmaf_rn(c3s, (float)n3,
-                               __fmaf_rn(c2s, (float)n2, __fmaf_rn(c1s, (float)n1, c0s * (float)n0)));
-            }
-            cn_s[tid] = cn;
+            cnt_s[hf][row] = nL | (nH << 10) | (nLH << 20);
+            if (hf == 0) id_s[row] = id_c;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
@@ -316,40 +308,53 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         phase ^= 1u;
         if (!__syncthreads_and(ok)) { failed = true; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int cb = 0; cb < IT_NQ && cb < nqg; cb += 32) {     // 32 query columns at a time
-            uint32_t rh[32], rl[32];
-            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
-            tmem_ld32(taddr, rh);
-            tmem_ld32(taddr + (uint32_t)IT_NQ, rl);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const float cn = cn_s[tid];
-            float m[32];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const int gi = (int)rh[c] * 256 + (int)rl[c];
-                const float sv = __fmaf_rn(b_s[cb + c], (float)gi, __fadd_rn(sq_s[cb + c], cn));
-                m[c] = cb + c < nqg ? sv : __int_as_float(0x7f800000);
-            }
-#pragma unroll
-            for (int h = 16; h; h >>= 1) {                 // transpose-reduce: lane c <- column c
-                const bool up = lane & h;
-#pragma unroll
-                for (int j = 0; j < h; ++j) {
-                    const float send = up ? m[j] : m[j + h];
-                    const float keep = up ? m[j + h] : m[j];
-                    m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+        {
+            // warp w: TMEM lanes (rows) 32 (w % 4) .., query columns 32 (w / 4) ..
+            const int q4 = warp & 3, cb = (warp >> 2) * 32, r = q4 * 32 + lane;
+            if (cb < nqg) {                                // warp-uniform
+                const int c0w = cnt_s[0][r], c1w = cnt_s[1][r];
+                const int nL = (c0w & 1023) + (c1w & 1023), nH = ((c0w >> 10) & 1023) + ((c1w >> 10) & 1023);
+                const int nLH = (c0w >> 20) + (c1w >> 20);
+                float cn = __int_as_float(0x7f800000);     // empty slot: never a minimum
+                if (id_s[r] >= 0) {
+                    const int n3 = nLH, n1 = nL - nLH, n2 = nH - nLH, n0 = d - nL - nH + nLH;
+                    cn = __fmaf_rn(c3s, (float)n3,
+                                   __fmaf_rn(c2s, (float)n2, __fmaf_rn(c1s, (float)n1, c0s * (float)n0)));
                 }
+                uint32_t rh[32], rl[32];
+                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)cb;
+                tmem_ld32(taddr, rh);
+                tmem_ld32(taddr + (uint32_t)IT_NQ, rl);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float m[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int gi = (int)rh[c] * 256 + (int)rl[c];
+                    const float sv = __fmaf_rn(b_s[cb + c], (float)gi, __fadd_rn(sq_s[cb + c], cn));
+                    m[c] = cb + c < nqg ? sv : __int_as_float(0x7f800000);
+                }
+#pragma unroll
+                for (int h = 16; h; h >>= 1) {             // transpose-reduce: lane c <- column c
+                    const bool up = lane & h;
+#pragma unroll
+                    for (int j = 0; j < h; ++j) {
+                        const float send = up ? m[j] : m[j + h];
+                        const float keep = up ? m[j + h] : m[j];
+                        m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+                    }
+                }
+                red[warp][lane] = m[0];
             }
-            red[warp][cb + lane] = m[0];
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncthreads();
         if (tid < nqg) {
-            const float mn = fminf(fminf(red[0][tid], red[1][tid]), fminf(red[2][tid], red[3][tid]));
+            const int bw = (tid >> 5) * 4, c = tid & 31;  // the four lane quarters of the column
+            const float mn = fminf(fminf(red[bw][c], red[bw + 1][c]), fminf(red[bw + 2][c], red[bw + 3][c]));
             tmin[base_s[tid] + t] = float_order(mn);
         }
         l = l2; g = g2; t = t2; tiles_l = tiles2;
-        id_c = id_n; w0_c = w0_n; w1_c = w1_n;
+        id_c = id_n; w_c = w_n;
     }
     if (failed && tid == 0) atomicExch(&g_tc_error, 1);
     // no MMA may still read shared memory or write TMEM when the CTA frees them
