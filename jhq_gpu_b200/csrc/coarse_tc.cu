@@ -1161,14 +1161,19 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
     plan_build(a.probes, a.nq, a.nprobe, a.nlist, a.list_page_off, a.d_nvalid, 4, IT_NQ, pb, s);
     static std::atomic<uint64_t> attr{0};
     once_per_device(attr, [Mp] {
-        JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      IT_SMEM));
+        JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      it_smem_bytes<3>()));
+        JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      it_smem_bytes<2>()));
         JHQ_CUDA(cudaFuncSetAttribute(ivf_tc_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)is_smem_bytes(128)));
     });
     const float* c = a.c1d_host;
-    const float e1 = c[1] - c[0], e2 = c[2] - c[0], e3 = c[3] - c[2] - c[1] + c[0];
+    // a symmetric codebook (the Lloyd-Max levels are) has no L&H term: its true
+    // weight is 0, and the pass-1 GEMM then runs on the L and H planes only
+    const bool sym = c[0] == -c[3] && c[1] == -c[2];
+    const float e1 = c[1] - c[0], e2 = c[2] - c[0], e3 = sym ? 0.0f : c[3] - c[2] - c[1] + c[0];
     float cmax = 0.0f;
     for (int i = 0; i < 4; ++i) cmax = std::max(cmax, std::fabs(c[i]));
     ivf_prep_kernel<<<a.nq, IP_THREADS, 0, s>>>(a.q_rot, a.nq, a.d, Mp, c[0], e1, e2, e3, cmax,
@@ -1179,7 +1184,10 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
     JHQ_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     long long wait_limit = TC_WAIT_CYCLES;
     if (const char* e = std::getenv("JHQ_TEST_TC_WAIT_CYCLES")) wait_limit = std::atoll(e);
-    ivf_tc_kernel<<<2 * nsm, IT_THREADS, IT_SMEM, s>>>(
+    const bool two = sym && !std::getenv("JHQ_IVF_TC_3PLANES");
+    auto pass1 = two ? ivf_tc_kernel<2> : ivf_tc_kernel<3>;
+    const int per_sm = two ? it_ctas_per_sm<2>() : it_ctas_per_sm<3>();
+    pass1<<<per_sm * nsm, IT_THREADS, two ? it_smem_bytes<2>() : it_smem_bytes<3>(), s>>>(
         a.pages, a.slot_ids, a.list_page_off, pb, f.qw, f.qc, a.nlist, a.nprobe, a.d, Mp,
         c[0] * c[0], c[1] * c[1], c[2] * c[2], c[3] * c[3], f.tmin, wait_limit);
     JHQ_LAUNCH_CHECK();

@@ -152,7 +152,29 @@ __device__ __forceinline__ void sw128_store(uint8_t* blk, int r, int c, uint4 v)
 //   4. the eight warps read 32 TMEM lanes (rows) x 32 query columns each, form
 //      s~ = (Sq' + cn) + (-2 s)(256 Gh + Gl), reduce each query column's
 //      minimum over the tile and write it to tmin[qtile[q] + cpo[q][p] + t].
-__global__ void __launch_bounds__(IT_THREADS)
+// NP = 3 K blocks (planes L, H, L&H) in general; NP = 2 when the codebook is
+// symmetric (c0 = -c3, c1 = -c2), where the L&H weight c3 - c2 - c1 + c0 is
+// zero and its query plane is all zeros: the third block would only add 0.
+// The two-plane form needs 64 KB of operands, so three CTAs share an SM
+// (registers capped at 85 a thread; the epilogue reads TMEM 16 columns at a
+// time to fit).
+template <int NP>
+__host__ __device__ constexpr int it_smem_bytes() { return 2 * NP * 16384 + 1024; }
+template <int NP>
+constexpr int it_ctas_per_sm() { return NP == 2 ? 3 : 2; }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+template <int NP>
+__global__ void __launch_bounds__(IT_THREADS, NP == 2 ? 3 : 0)
 ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slot_ids,
               const int32_t* __restrict__ lpo, PlanBufs pb, const int8_t* __restrict__ qw,
               const float4* __restrict__ qc, int nlist, int nprobe, int d, int Mp,
@@ -168,7 +190,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* As = smem;                                    // [3][128][128]
-    uint8_t* Bs = smem + IT_A_BYTES;                       // [3][2 IT_NQ][128]
+    uint8_t* Bs = smem + NP * 16384;                       // [NP][2 IT_NQ][128]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = Mp / 16;
     const int64_t U = pb.unit_off[nlist];
@@ -238,7 +260,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         if (cur_l != l || cur_g != g) {                    // the group's B rows and constants
             const int b0 = pb.bucket_off[l] + g * IT_NQ;
             nqg = min(IT_NQ, pb.bucket_off[l + 1] - b0);
-            for (int i = tid; i < IT_KB * 2 * IT_NQ * 8; i += IT_THREADS) {
+            for (int i = tid; i < NP * 2 * IT_NQ * 8; i += IT_THREADS) {
                 const int kb = i / (2 * IT_NQ * 8), r = (i >> 3) % (2 * IT_NQ), c = i & 7;
                 const int j = r % IT_NQ;
                 uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -279,7 +301,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                 const int cg = hf * 4 + wi;                // 16-dim chunk of the 128 dims
                 sw128_store(As + 0 * 16384, row, cg, spread16(L));
                 sw128_store(As + 1 * 16384, row, cg, spread16(H));
-                sw128_store(As + 2 * 16384, row, cg, spread16(LH));
+                if (NP == 3) sw128_store(As + 2 * 16384, row, cg, spread16(LH));
             }
             cnt_s[hf][row] = nL | (nH << 10) | (nLH << 20);
             if (hf == 0) id_s[row] = id_c;
@@ -289,7 +311,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-            for (int kb = 0; kb < IT_KB; ++kb) {
+            for (int kb = 0; kb < NP; ++kb) {
                 const uint64_t da = sw128_desc(smem_u32(As + kb * 16384));
                 const uint64_t db = sw128_desc(smem_u32(Bs + kb * (2 * IT_NQ * 128)));
 #pragma unroll
@@ -321,29 +343,34 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     cn = __fmaf_rn(c3s, (float)n3,
                                    __fmaf_rn(c2s, (float)n2, __fmaf_rn(c1s, (float)n1, c0s * (float)n0)));
                 }
-                uint32_t rh[32], rl[32];
-                const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)cb;
-                tmem_ld32(taddr, rh);
-                tmem_ld32(taddr + (uint32_t)IT_NQ, rl);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                float m[32];
+#pragma unroll 1
+                for (int hh = 0; hh < 32; hh += 16) {      // 16 query columns at a time
+                    uint32_t rh[16], rl[16];
+                    const uint32_t taddr = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(cb + hh);
+                    tmem_ld16(taddr, rh);
+                    tmem_ld16(taddr + (uint32_t)IT_NQ, rl);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    float m[16];
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const int gi = (int)rh[c] * 256 + (int)rl[c];
-                    const float sv = __fmaf_rn(b_s[cb + c], (float)gi, __fadd_rn(sq_s[cb + c], cn));
-                    m[c] = cb + c < nqg ? sv : __int_as_float(0x7f800000);
-                }
-#pragma unroll
-                for (int h = 16; h; h >>= 1) {             // transpose-reduce: lane c <- column c
-                    const bool up = lane & h;
-#pragma unroll
-                    for (int j = 0; j < h; ++j) {
-                        const float send = up ? m[j] : m[j + h];
-                        const float keep = up ? m[j + h] : m[j];
-                        m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+                    for (int c = 0; c < 16; ++c) {
+                        const int col = cb + hh + c;
+                        const int gi = (int)rh[c] * 256 + (int)rl[c];
+                        const float sv = __fmaf_rn(b_s[col], (float)gi, __fadd_rn(sq_s[col], cn));
+                        m[c] = col < nqg ? sv : __int_as_float(0x7f800000);
                     }
+#pragma unroll
+                    for (int h = 8; h; h >>= 1) {          // transpose-reduce: lane c <- column c & 15
+                        const bool up = lane & h;
+#pragma unroll
+                        for (int j = 0; j < h; ++j) {
+                            const float send = up ? m[j] : m[j + h];
+                            const float keep = up ? m[j + h] : m[j];
+                            m[j] = fminf(keep, __shfl_xor_sync(0xffffffffu, send, h));
+                        }
+                    }
+                    m[0] = fminf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 16));
+                    if (lane < 16) red[warp][hh + lane] = m[0];
                 }
-                red[warp][lane] = m[0];
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
