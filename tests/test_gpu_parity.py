@@ -450,7 +450,7 @@ def test_exact_rerank_reaches_recall_gate_on_c1_generator(jhq):
 ])
 def test_integer_generators_bit_exact_vs_oracle(jhq, oracle, gen, d, M, nlist, nprobe):
     """The C3 / C4 data generators (not i.i.d. normal) at 60k rows with nlist in the
-    thousands, the tensor-core scan and both SIMT scan orders: ids and distances
+    thousands, the tensor-core scan (two and three planes) and both SIMT scan orders: ids and distances
     equal the oracle's, and every result row is ordered by (distance, id) — the
     tie rule applied everywhere."""
     from jhq_gpu_b200 import datasets
@@ -463,6 +463,13 @@ def test_integer_generators_bit_exact_vs_oracle(jhq, oracle, gen, d, M, nlist, n
     D2, I2 = _oracle_search(oracle, idx, ox, q, 10)
     ties = 0
     D, I = idx.search(q, 10)                        # the default (tensor-core) scan
+    _assert_same(D, I, D2, I2)
+    os.environ["JHQ_IVF_TC_3PLANES"] = "1"          # tensor-core scan with the L&H plane kept
+    try:
+        idx.set_nprobe(nprobe)
+        D, I = idx.search(q, 10)
+    finally:
+        del os.environ["JHQ_IVF_TC_3PLANES"]
     _assert_same(D, I, D2, I2)
     for order in ("query", "list"):                 # both SIMT orders
         os.environ["JHQ_SCAN_ORDER"] = order
