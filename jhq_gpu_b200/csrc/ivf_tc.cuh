@@ -119,19 +119,14 @@ ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0
     }
 }
 
-// even bits 0, 2, .., 30 of x -> bits 0..15
-__device__ __forceinline__ uint32_t even_bits16(uint32_t x) {
-    x &= 0x55555555u;
-    x = (x | (x >> 1)) & 0x33333333u;
-    x = (x | (x >> 2)) & 0x0F0F0F0Fu;
-    x = (x | (x >> 4)) & 0x00FF00FFu;
-    x = (x | (x >> 8)) & 0x0000FFFFu;
-    return x;
-}
-
-__device__ __forceinline__ uint4 spread16(uint32_t x) {   // bits 0..15 -> 16 bytes of 0 / 1
-    return make_uint4(spread4(x & 15u), spread4((x >> 4) & 15u), spread4((x >> 8) & 15u),
-                      spread4((x >> 12) & 15u));
+// x holds bits only at even positions (x & 0x55555555 == x): bit 2j -> byte j
+// as 0 / 1, 16 bytes. A byte b with bits 0, 2, 4, 6 times 0x41041 (shifts 0, 6,
+// 12, 18) puts bit 2k at 8k; the other partial products land on odd bits or on
+// bits 12 and 18 (with carries into 13 and 19), all masked off.
+__device__ __forceinline__ uint4 spread_even(uint32_t x) {
+    auto sp = [](uint32_t b) { return (b * 0x41041u) & 0x01010101u; };
+    return make_uint4(sp(__byte_perm(x, 0u, 0x4440)), sp(__byte_perm(x, 0u, 0x4441)),
+                      sp(__byte_perm(x, 0u, 0x4442)), sp(x >> 24));
 }
 
 // 128-byte swizzled K-major store of 16 bytes: row r, 16-byte chunk c of a
@@ -294,14 +289,16 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             const uint32_t w4[4] = {w_c.x, w_c.y, w_c.z, w_c.w};
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {               // 4 subspaces = 16 dims
-                const uint32_t L = even_bits16(w4[wi]), H = even_bits16(w4[wi] >> 1), LH = L & H;
-                nL += __popc(L);
-                nH += __popc(H);
-                nLH += __popc(LH);
+                // bit 2j of xl / xh is dim j's low / high code bit
+                const uint32_t xl = w4[wi] & 0x55555555u, xh = (w4[wi] >> 1) & 0x55555555u;
+                const uint32_t xlh = xl & xh;
+                nL += __popc(xl);
+                nH += __popc(xh);
+                nLH += __popc(xlh);
                 const int cg = hf * 4 + wi;                // 16-dim chunk of the 128 dims
-                sw128_store(As + 0 * 16384, row, cg, spread16(L));
-                sw128_store(As + 1 * 16384, row, cg, spread16(H));
-                if (NP == 3) sw128_store(As + 2 * 16384, row, cg, spread16(LH));
+                sw128_store(As + 0 * 16384, row, cg, spread_even(xl));
+                sw128_store(As + 1 * 16384, row, cg, spread_even(xh));
+                if (NP == 3) sw128_store(As + 2 * 16384, row, cg, spread_even(xlh));
             }
             cnt_s[hf][row] = nL | (nH << 10) | (nLH << 20);
             if (hf == 0) id_s[row] = id_c;
