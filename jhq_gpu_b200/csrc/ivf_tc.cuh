@@ -179,7 +179,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     __shared__ int cnt_s[2][128];                      // level counts per half row: nL | nH << 10 | nLH << 20
     __shared__ int id_s[128];
     __shared__ float red[8][32];
-    __shared__ float sq_s[IT_NQ], b_s[IT_NQ];
+    __shared__ float2 sb_s[IT_NQ];                     // (Sq', -2 s) of each query of the group
     __shared__ int64_t base_s[IT_NQ];
     __shared__ uint64_t bar;
     __shared__ uint32_t tmem_slot;
@@ -276,8 +276,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     bq = c.y;
                     base = pb.qslot_off[e.x] + pb.cpo[(int64_t)e.x * (nprobe + 1) + e.y];
                 }
-                sq_s[j] = sq;
-                b_s[j] = bq;
+                sb_s[j] = make_float2(sq, bq);
                 base_s[j] = base;
             }
             cur_l = l;
@@ -350,10 +349,11 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     float m[16];
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
-                        const int col = cb + hh + c;
+                        // columns past nqg hold junk that never mixes with
+                        // other columns and is never written out
+                        const float2 sb = sb_s[cb + hh + c];
                         const int gi = (int)rh[c] * 256 + (int)rl[c];
-                        const float sv = __fmaf_rn(b_s[col], (float)gi, __fadd_rn(sq_s[col], cn));
-                        m[c] = col < nqg ? sv : __int_as_float(0x7f800000);
+                        m[c] = __fmaf_rn(sb.y, (float)gi, __fadd_rn(sb.x, cn));
                     }
 #pragma unroll
                     for (int h = 8; h; h >>= 1) {          // transpose-reduce: lane c <- column c & 15
