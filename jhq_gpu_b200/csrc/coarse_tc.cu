@@ -1169,6 +1169,9 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)is_smem_bytes(128)));
     });
+    int nsm0 = 0, dev0 = 0;
+    JHQ_CUDA(cudaGetDevice(&dev0));
+    JHQ_CUDA(cudaDeviceGetAttribute(&nsm0, cudaDevAttrMultiProcessorCount, dev0));
     const float* c = a.c1d_host;
     // a symmetric codebook (the Lloyd-Max levels are) has no L&H term: its true
     // weight is 0, and the pass-1 GEMM then runs on the L and H planes only
@@ -1176,6 +1179,8 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
     const float e1 = c[1] - c[0], e2 = c[2] - c[0], e3 = sym ? 0.0f : c[3] - c[2] - c[1] + c[0];
     float cmax = 0.0f;
     for (int i = 0; i < 4; ++i) cmax = std::max(cmax, std::fabs(c[i]));
+    tmin_fill_kernel<<<4 * nsm0, 256, 0, s>>>(f.tmin, f.qtile, a.nq);
+    JHQ_LAUNCH_CHECK();
     ivf_prep_kernel<<<a.nq, IP_THREADS, 0, s>>>(a.q_rot, a.nq, a.d, Mp, c[0], e1, e2, e3, cmax,
                                                 f.qw, f.qc);
     JHQ_LAUNCH_CHECK();
@@ -1195,7 +1200,7 @@ void ivf_search_tc(const IvfTcArgs& a, cudaStream_t s) {
         a.q_rot, a.c1d, a.pages, a.slot_ids, a.list_page_off, a.probes, pb, f.qc, f.tmin, a.nq,
         a.nprobe, a.d, a.M, Mp, a.ck, a.ck_pad, a.cand, a.gthr, a.qslot_out, a.d_nvalid);
     JHQ_LAUNCH_CHECK();
-    count_launch(3);
+    count_launch(4);
 }
 
 }  // namespace jhq

@@ -119,6 +119,13 @@ ivf_prep_kernel(const float* __restrict__ q_rot, int nq, int d, int Mp, float c0
     }
 }
 
+// tmin[0 .. qtile[nq]) = all ones, the identity of the pass-1 atomicMin
+__global__ void tmin_fill_kernel(uint32_t* __restrict__ tmin, const int64_t* __restrict__ qtile, int nq) {
+    const int64_t n = qtile[nq];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        tmin[i] = 0xFFFFFFFFu;
+}
+
 // x holds bits only at even positions (x & 0x55555555 == x): bit 2j -> byte j
 // as 0 / 1, 16 bytes. A byte b with bits 0, 2, 4, 6 times 0x41041 (shifts 0, 6,
 // 12, 18) puts bit 2k at 8k; the other partial products land on odd bits or on
@@ -176,11 +183,12 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
               float c0s, float c1s, float c2s, float c3s, uint32_t* __restrict__ tmin,
               long long wait_limit) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ int cnt_s[2][128];                      // level counts per half row: nL | nH << 10 | nLH << 20
-    __shared__ int id_s[128];
-    __shared__ float red[8][32];
-    __shared__ float2 sb_s[IT_NQ];                     // (Sq', -2 s) of each query of the group
-    __shared__ int64_t base_s[IT_NQ];
+    // per-unit arrays by unit parity and per-group arrays by group parity: a
+    // warp may still read unit u's while others fill unit u+1's
+    __shared__ int cnt_s[2][2][128];                   // level counts per half row: nL | nH << 10 | nLH << 20
+    __shared__ int id_s[2][128];
+    __shared__ float2 sb_s[2][IT_NQ];                  // (Sq', -2 s) of each query of the group
+    __shared__ int64_t base_s[2][IT_NQ];
     __shared__ uint64_t bar;
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -221,7 +229,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
     }
     int tiles_l = (lpo[l + 1] - lpo[l] + 3) >> 2;
     int g = (int)((u0 - pb.unit_off[l]) / tiles_l), t = (int)((u0 - pb.unit_off[l]) % tiles_l);
-    int cur_l = -1, cur_g = -1, nqg = 0;
+    int cur_l = -1, cur_g = -1, nqg = 0, gb = 1;
     uint32_t phase = 0;
     bool failed = false;
     // the A row of this thread in unit (L, T): slot id and code words, loaded
@@ -252,7 +260,9 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             }
             load_row(l2, t2, id_n, w_n);
         }
+        const int ub = (int)(u & 1);
         if (cur_l != l || cur_g != g) {                    // the group's B rows and constants
+            gb ^= 1;
             const int b0 = pb.bucket_off[l] + g * IT_NQ;
             nqg = min(IT_NQ, pb.bucket_off[l + 1] - b0);
             for (int i = tid; i < NP * 2 * IT_NQ * 8; i += IT_THREADS) {
@@ -276,8 +286,8 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     bq = c.y;
                     base = pb.qslot_off[e.x] + pb.cpo[(int64_t)e.x * (nprobe + 1) + e.y];
                 }
-                sb_s[j] = make_float2(sq, bq);
-                base_s[j] = base;
+                sb_s[gb][j] = make_float2(sq, bq);
+                base_s[gb][j] = base;
             }
             cur_l = l;
             cur_g = g;
@@ -299,8 +309,8 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                 sw128_store(As + 1 * 16384, row, cg, spread_even(xh));
                 if (NP == 3) sw128_store(As + 2 * 16384, row, cg, spread_even(xlh));
             }
-            cnt_s[hf][row] = nL | (nH << 10) | (nLH << 20);
-            if (hf == 0) id_s[row] = id_c;
+            cnt_s[ub][hf][row] = nL | (nH << 10) | (nLH << 20);
+            if (hf == 0) id_s[ub][row] = id_c;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
@@ -321,8 +331,11 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             }
             mma_commit(barp);
         }
-        // every thread waits for the MMAs (bounded; a timeout ends the CTA's work)
-        const bool ok = mbar_wait(barp, phase, nullptr, wait_limit);
+        // thread 0 waits for the MMAs (bounded; a timeout ends the CTA's work) and
+        // the barrier releases the rest, whose TMEM reads the fence below orders
+        // after it; polling from one thread leaves the issue slots to the SM's
+        // other CTAs
+        const bool ok = tid == 0 ? mbar_wait(barp, phase, nullptr, wait_limit) : true;
         phase ^= 1u;
         if (!__syncthreads_and(ok)) { failed = true; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -330,11 +343,11 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
             // warp w: TMEM lanes (rows) 32 (w % 4) .., query columns 32 (w / 4) ..
             const int q4 = warp & 3, cb = (warp >> 2) * 32, r = q4 * 32 + lane;
             if (cb < nqg) {                                // warp-uniform
-                const int c0w = cnt_s[0][r], c1w = cnt_s[1][r];
+                const int c0w = cnt_s[ub][0][r], c1w = cnt_s[ub][1][r];
                 const int nL = (c0w & 1023) + (c1w & 1023), nH = ((c0w >> 10) & 1023) + ((c1w >> 10) & 1023);
                 const int nLH = (c0w >> 20) + (c1w >> 20);
                 float cn = __int_as_float(0x7f800000);     // empty slot: never a minimum
-                if (id_s[r] >= 0) {
+                if (id_s[ub][r] >= 0) {
                     const int n3 = nLH, n1 = nL - nLH, n2 = nH - nLH, n0 = d - nL - nH + nLH;
                     cn = __fmaf_rn(c3s, (float)n3,
                                    __fmaf_rn(c2s, (float)n2, __fmaf_rn(c1s, (float)n1, c0s * (float)n0)));
@@ -351,7 +364,7 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                     for (int c = 0; c < 16; ++c) {
                         // columns past nqg hold junk that never mixes with
                         // other columns and is never written out
-                        const float2 sb = sb_s[cb + hh + c];
+                        const float2 sb = sb_s[gb][cb + hh + c];
                         const int gi = (int)rh[c] * 256 + (int)rl[c];
                         m[c] = __fmaf_rn(sb.y, (float)gi, __fadd_rn(sb.x, cn));
                     }
@@ -366,17 +379,17 @@ ivf_tc_kernel(const uint8_t* __restrict__ pages, const int32_t* __restrict__ slo
                         }
                     }
                     m[0] = fminf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 16));
-                    if (lane < 16) red[warp][hh + lane] = m[0];
+                    // this warp's 32 rows; the four row quarters meet in tmin
+                    // (preset to all ones): the minimum of order keys is the
+                    // order key of the minimum
+                    const int col = cb + hh + lane;
+                    if (lane < 16 && col < nqg)
+                        atomicMin(tmin + base_s[gb][col] + t, float_order(m[0]));
                 }
             }
         }
+        // TMEM reads before the next unit's MMAs (ordered by the next barriers)
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
-        if (tid < nqg) {
-            const int bw = (tid >> 5) * 4, c = tid & 31;  // the four lane quarters of the column
-            const float mn = fminf(fminf(red[bw][c], red[bw + 1][c]), fminf(red[bw + 2][c], red[bw + 3][c]));
-            tmin[base_s[tid] + t] = float_order(mn);
-        }
         l = l2; g = g2; t = t2; tiles_l = tiles2;
         id_c = id_n; w_c = w_n;
     }
